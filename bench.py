@@ -1,0 +1,327 @@
+#!/usr/bin/env python
+"""Decode benchmark of the B200 backend (one JSON line on rank 0).
+
+Workload (the metric's configuration): the
+Llama-3-8B-shaped model, random init, Q4_K body with Q8_0 embedding and LM
+head, a 512-token random prompt (seed 1), greedy decode at batch 1.  A step is
+one decode step (one token through all 32 layers, LM head and argmax).
+
+  value  tokens/s of K device-chained decode steps, inputs resident in HBM,
+         CUDA events on the backend stream (max over ranks for N > 1).
+  e2e    the same steps through the public C ABI call nexus_cuda_decode with
+         host buffers: the step's token goes host->device, the argmax comes
+         back device->host, every step.
+  roofline  the dominant kernel (the fused gate/up dequant-GEMV) from a live
+         per-kernel CUDA-event profile of real decode steps; achieved =
+         algorithmic bytes per launch / mean launch time; peak = measured HBM
+         copy bandwidth (MEASURED_PEAKS.json).
+  cpu_baseline  the CPU restatement of the reference decode path (oracle/) on
+         the host cores, bounded sample.
+
+--impl reference times the reference's CPU decode path (the oracle port; the
+Rust reference cannot be built here) on the same config and metric.
+Multi-GPU: the decode path is run as independent replicas, one per rank
+(tensor parallelism is not implemented yet), weak scaling.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PROMPT_LEN = 512
+GEN_TOKENS = 128
+SEED_PROMPT = 1
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.rows = []
+        self._stop = threading.Event()
+        self._thr = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                     timeout=5).stdout.strip()
+                if out:
+                    self.rows.append([c.strip() for c in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._thr = threading.Thread(target=self._run, daemon=True)
+        self._thr.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._thr.join(timeout=10)
+
+    def summary(self) -> dict:
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if len(r) > 5 + i and r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def init_dist(world: int, backend: str):
+    if world <= 1:
+        return None
+    import datetime
+
+    import torch.distributed as dist
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=600))
+    return dist
+
+
+def reduce_max(dist, value: float, device) -> float:
+    if dist is None:
+        return value
+    import torch
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(dist, device):
+    if dist is not None:
+        import torch
+        dist.barrier(device_ids=[device.index] if device.type == "cuda" else None)
+
+
+def cpu_threads() -> int:
+    try:
+        return max(1, min(64, len(os.sched_getaffinity(0))))
+    except Exception:
+        return max(1, min(64, os.cpu_count() or 1))
+
+
+def time_oracle(model_path: Path, steps: int, warmup: int, budget_s: float, threads: int) -> dict:
+    """The CPU restatement of the reference's decode (oracle port) on a bounded
+    sample: a 4-token prompt, then decode steps timed one by one."""
+    from oracle import oracle as O
+
+    m = O.Model(model_path, threads=threads, max_seq_len=64)
+    prompt = np.random.default_rng(SEED_PROMPT).integers(0, m.info.vocab_rows, 4).tolist()
+    logits = m.prefill(prompt)
+    tok = O.greedy(logits)
+    pos = len(prompt)
+    for _ in range(warmup):
+        logits = m.decode(tok, pos)
+        tok = O.greedy(logits)
+        pos += 1
+    times = []
+    t_start = time.perf_counter()
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        logits = m.decode(tok, pos)
+        tok = O.greedy(logits)
+        pos += 1
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s or pos >= 60:
+            break
+    total = sum(times)
+    return {"tok_s": len(times) / total, "steps": len(times), "s_per_token": total / len(times),
+            "threads": threads}
+
+
+def run_reference(args):
+    world, rank, local = dist_env()
+    if rank != 0:
+        return 0
+    import nexus_b200 as nb
+    path = nb.model_path(args.config, threads=cpu_threads())
+    threads = cpu_threads()
+    warm = min(args.warmup, 1)
+    r = time_oracle(path, args.steps, warm, budget_s=args.ref_budget, threads=threads)
+    line = {
+        "impl": "reference", "metric": "decode tok/s, Llama-3-8B-shape Q4_K, b=1", "value": r["tok_s"],
+        "unit": "tok/s", "n_gpus": 0, "steps": r["steps"], "warmup": warm, "ms_per_step": 1000 * r["s_per_token"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded random-init weights and prompt)",
+        "config": {"workload": f"{args.config} b=1 greedy decode; CPU sample: 4-token prompt then decode steps",
+                   "model": args.config, "global_batch": 1, "seq_len": PROMPT_LEN + GEN_TOKENS, "parallelism": "cpu"},
+        "cpu_baseline": {"value": r["tok_s"], "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": f"{r['steps']} decode steps after a 4-token prompt (attention context 5-{4 + r['steps']}),"
+                                   " matvec rows split over threads, bit-identical per row"},
+        "e2e": {"value": r["tok_s"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="llama8b_q4k")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-budget", type=float, default=60.0)
+    ap.add_argument("--profile-steps", type=int, default=4)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.steps + args.warmup > GEN_TOKENS:
+        args.steps = GEN_TOKENS - args.warmup
+    if args.impl == "reference":
+        return run_reference(args)
+
+    world, rank, local = dist_env()
+    import torch
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dist = init_dist(world, "nccl")
+
+    import nexus_b200 as nb
+    from nexus_b200 import _lib as L
+    # rank 0 writes the synthetic model; the others wait for it
+    if rank == 0:
+        path = nb.model_path(args.config, threads=cpu_threads())
+    barrier(dist, device)
+    if rank != 0:
+        path = nb.model_path(args.config)
+
+    backend = nb.CudaBackend(device=local, max_seq_len=PROMPT_LEN + GEN_TOKENS + 8)
+    eng = nb.InferenceEngine(backend)
+    eng.load_model(path)
+    info = eng.info
+    prompt = np.random.default_rng(SEED_PROMPT).integers(0, info.vocab_rows, PROMPT_LEN).tolist()
+
+    # ---- value: device-chained decode steps (generate), inputs resident ----
+    eng.prefill(prompt)
+    lib, model = eng._lib, eng.model
+    import ctypes as C
+    out = np.zeros(PROMPT_LEN + args.warmup, np.uint32)
+    p = np.asarray(prompt, np.uint32)
+    # warm-up (captures the graph), untimed
+    L.check(lib.nexus_cuda_generate(model, 0, p.ctypes.data, p.size, args.warmup, out.ctypes.data), backend.handle)
+    out = np.zeros(PROMPT_LEN + args.steps, np.uint32)
+    barrier(dist, device)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        L.check(lib.nexus_cuda_generate(model, 0, p.ctypes.data, p.size, args.steps, out.ctypes.data),
+                backend.handle)
+        torch.cuda.synchronize()
+    gen_ms = eng.last_step_ms()  # CUDA events around the K chained steps (excludes the prefill)
+    ms_max = reduce_max(dist, gen_ms, device)
+    value = world * args.steps / (ms_max / 1000.0)
+
+    # ---- e2e: nexus_cuda_decode with host token in / argmax out per step ----
+    _, tok = eng.prefill(prompt, want_logits=False)
+    pos = PROMPT_LEN
+    for _ in range(args.warmup):
+        _, tok = eng.decode_with_cache(tok, pos, want_logits=False)
+        pos += 1
+    eng.prefill(prompt, want_logits=False)
+    pos = PROMPT_LEN
+    barrier(dist, device)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    tok_c = C.c_uint32(tok)
+    for _ in range(args.steps):
+        L.check(lib.nexus_cuda_decode(model, 0, tok_c.value, pos, None, C.byref(tok_c)), backend.handle)
+        pos += 1
+    torch.cuda.synchronize()
+    e2e_s = reduce_max(dist, time.perf_counter() - t0, device)
+    e2e_value = world * args.steps / e2e_s
+
+    # ---- live per-kernel profile (CUDA events per launch, no graph) ----
+    eng.prefill(prompt, want_logits=False)
+    prof = eng.profile_decode(int(out[PROMPT_LEN]), args.profile_steps)
+    peaks = measured_peaks()
+    kern = {r["name"]: r for r in prof}
+    dom = max(prof, key=lambda r: r["total_ms"])
+    dom_ms = dom["total_ms"] / dom["launches"]
+    achieved = dom["bytes_per_launch"] / (dom_ms / 1000.0) / 1e9
+    step_ms_prof = sum(r["total_ms"] for r in prof) / args.profile_steps
+    barrier(dist, device)
+
+    line = {
+        "metric": "decode tok/s, Llama-3-8B-shape Q4_K, b=1",
+        "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8x4 dp4a + f32 (Q4_K/Q8_0 weights)", "data": "synthetic (seeded random-init weights, random prompt)",
+        "config": {"workload": f"{args.config}: prompt {PROMPT_LEN} (seed {SEED_PROMPT}), greedy decode b=1, "
+                               f"context {PROMPT_LEN}-{PROMPT_LEN + args.warmup + args.steps}",
+                   "model": args.config, "global_batch": world, "seq_len": PROMPT_LEN + GEN_TOKENS,
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2: every step streams all weights "
+                         f"({info.weight_bytes / 1e9:.3f} GB) from HBM",
+                   "weight_bytes_per_token": info.weight_bytes},
+        "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 28, "d2h_bytes_per_step": 4},
+        "gpu_launches": None,
+        "roofline": {"bound": "hbm", "kernel": dom["name"], "achieved": achieved, "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                     "peak_source": peaks["source"],
+                     "step_achieved_gbs": info.weight_bytes / (ms_max / args.steps / 1000.0) / 1e9},
+        "kernels": {r["name"]: {"launches_per_step": r["launches"] / args.profile_steps,
+                                "ms_per_step": r["total_ms"] / args.profile_steps,
+                                "gbs": r["bytes_per_launch"] * r["launches"] / (r["total_ms"] / 1000.0) / 1e9}
+                    for r in prof},
+        "profile_step_ms": step_ms_prof,
+        "clocks": clk.summary(),
+    }
+    launches_per_step = sum(r["launches"] for r in prof) / args.profile_steps
+    line["gpu_launches"] = int(round(launches_per_step * args.steps))
+
+    if rank == 0 and not args.no_cpu_baseline:
+        r = time_oracle(path, 64, 1, budget_s=20.0, threads=cpu_threads())
+        line["cpu_baseline"] = {"value": r["tok_s"], "unit": "tok/s", "cores": r["threads"], "kind": "port",
+                                "sample": f"{r['steps']} decode steps of the same model after a 4-token prompt "
+                                          "(oracle restatement of the reference CPU path)"}
+    eng.close()
+    backend.close()
+    if dist is not None:
+        barrier(dist, device)
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,280 @@
+/*
+ * nexus_cuda.h -- C ABI of the B200 (sm_100a) CUDA backend for Nexus.
+ *
+ * This library fills the "unavailable" CUDA capability slot of the reference
+ * (luen-eth/Nexus, Rust).  Every entry point is plain C: pointers, sizes and
+ * status codes, no C++ or torch types.  Citations are paths in the reference
+ * project, naming the interface each entry point replaces.
+ *
+ * Conventions
+ *   - Every function returns an int status (NEXUS_OK = 0) unless noted.
+ *     Once the CUDA backend is selected there is no CPU fallback: a failure is
+ *     reported, never silently rerouted (contrast src/engine/mod.rs:1160-1166).
+ *   - Handles are opaque and owned by the library; *_destroy frees them.
+ *   - Caller buffers are borrowed for the duration of the call only.
+ *   - Host pointers unless a name or flag says "device".
+ *   - One in-flight call per model handle; different handles may be used from
+ *     different threads (the reference's Backend is Send + Sync,
+ *     src/backend/mod.rs:75).
+ */
+#ifndef NEXUS_CUDA_H
+#define NEXUS_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NEXUS_CUDA_ABI_VERSION 1
+
+/* ---- status codes (replace io::Result / Result<_, String>) ---- */
+enum {
+    NEXUS_OK = 0,
+    NEXUS_E_INVALID = 1,            /* bad argument or shape */
+    NEXUS_E_UNSUPPORTED_FORMAT = 2, /* tensor type not handled on this path */
+    NEXUS_E_OOM = 3,                /* device or host allocation failed */
+    NEXUS_E_CUDA = 4,               /* CUDA runtime error */
+    NEXUS_E_COMM = 5,               /* NCCL / peer communication error */
+    NEXUS_E_TIMEOUT = 6,            /* a bounded device wait gave up */
+    NEXUS_E_IO = 7,                 /* file open/read/map failed */
+    NEXUS_E_MISSING_TENSOR = 8,     /* a required GGUF tensor is absent */
+    NEXUS_E_TRUNCATED = 9,          /* payload shorter than its block count */
+    NEXUS_E_UNAVAILABLE = 10        /* no usable sm_100 device */
+};
+
+/* ---- weight formats: GGUF type ids (GgufDataType::id, src/gguf/mod.rs:104-151)
+ *      and the QuantFormat subset the backend handles (src/quant/mod.rs:16-31) ---- */
+enum {
+    NEXUS_FMT_F32 = 0,
+    NEXUS_FMT_F16 = 1,
+    NEXUS_FMT_Q4_0 = 2,
+    NEXUS_FMT_Q8_0 = 8,
+    NEXUS_FMT_Q2_K = 10,
+    NEXUS_FMT_Q4_K = 12,
+    NEXUS_FMT_BF16 = 28
+};
+
+/* ======================================================================== */
+/* Backend selection and the Backend trait (src/backend/mod.rs:75-96)        */
+/* ======================================================================== */
+
+/* Replaces BackendFactory::unavailable_capability(BackendType::Cuda)
+ * (src/backend/mod.rs:222-240): 1 when an sm_100 device is present. */
+int nexus_cuda_is_available(void);
+
+/* BackendCapabilities (src/backend/mod.rs:25-31).  Strings are static. */
+typedef struct {
+    int available;
+    int device_count;
+    const char *backend;              /* "cuda" (BackendType::name, :34-41) */
+    const char *features[16];
+    int n_features;
+    const char *supported_ops[16];    /* same names as src/backend/cpu.rs:128-136 */
+    int n_supported_ops;
+} nexus_cuda_caps;
+int nexus_cuda_capabilities(nexus_cuda_caps *caps);
+
+/* Backend construction (BackendFactory::create(Some(BackendType::Cuda)),
+ * src/backend/mod.rs:190-214, with the InferenceConfig knobs the device needs,
+ * src/engine/mod.rs:65-98). */
+typedef struct {
+    int device;            /* first CUDA ordinal */
+    int tp;                /* tensor-parallel degree, 1 = single GPU */
+    uint32_t kv_bits_k;    /* 0 = float KV (KvQuantType::None); else packed key bits */
+    uint32_t kv_bits_v;    /* packed value bits (KvQuantType::val_bits, src/quant/mod.rs:150) */
+    uint32_t max_batch;    /* largest decode_batch the model will see (>= 1) */
+    uint32_t max_seq_len;  /* 0 = GGUF llama.context_length (src/engine/mod.rs:561) */
+    uint32_t page_tokens;  /* KV page size in tokens; 0 = 16 (src/scheduler.rs page size) */
+    uint32_t max_pages;    /* KV pages to reserve per rank; 0 = max_batch * pages(max_seq_len) */
+    uint32_t flags;        /* NEXUS_CFG_* */
+} nexus_cuda_config;
+
+#define NEXUS_CFG_NO_GRAPH 0x1u  /* launch kernels directly instead of a CUDA graph */
+#define NEXUS_CFG_NO_PDL 0x2u    /* no programmatic dependent launch between kernels */
+
+typedef struct nexus_cuda_backend nexus_cuda_backend;
+
+/* Fills cfg with defaults (device 0, tp 1, float KV, max_batch 1, page 16). */
+void nexus_cuda_config_default(nexus_cuda_config *cfg);
+int nexus_cuda_backend_create(const nexus_cuda_config *cfg, nexus_cuda_backend **out);
+int nexus_cuda_backend_destroy(nexus_cuda_backend *b);
+/* Backend::name (src/backend/mod.rs:77): returns "cuda" */
+const char *nexus_cuda_backend_name(const nexus_cuda_backend *b);
+/* Backend::memory_info / MemoryInfo (src/backend/mod.rs:86,99-104) */
+int nexus_cuda_memory_info(nexus_cuda_backend *b, size_t *total, size_t *free_bytes,
+                           size_t *used);
+/* Backend::synchronize (src/backend/mod.rs:95) */
+int nexus_cuda_synchronize(nexus_cuda_backend *b);
+/* Last error message for this backend (thread-local when b is NULL). */
+const char *nexus_cuda_last_error(const nexus_cuda_backend *b);
+
+/* ---- KernelOp (src/backend/mod.rs:118-183) executed by Backend::execute ---- */
+enum {
+    NEXUS_OP_MATMUL = 0,      /* C[m,n] = A[m,k] @ B  (B is [n,k] when transpose_b, else [k,n]) */
+    NEXUS_OP_ATTENTION = 1,   /* GQA decode attention, see nexus_op fields */
+    NEXUS_OP_LAYER_NORM = 2,  /* layer_norm, src/kernel/mod.rs:212-231 */
+    NEXUS_OP_RMS_NORM = 3,    /* rms_norm, src/kernel/mod.rs:199-209 */
+    NEXUS_OP_ADD = 4,
+    NEXUS_OP_MUL = 5,
+    NEXUS_OP_SOFTMAX = 6,     /* softmax over rows of length n, src/kernel/mod.rs:234-255 */
+    NEXUS_OP_QUANTIZE = 7,    /* QuantEngine::quantize_weights, src/quant/mod.rs:623-640 */
+    NEXUS_OP_DEQUANTIZE = 8,  /* GgufReader::tensor_bytes_to_f32, src/gguf/mod.rs:902-956 */
+    NEXUS_OP_QMATVEC = 9,     /* Y[m,n] = X[m,k] @ W[n,k]^T with W in a block format */
+    NEXUS_OP_ROPE = 10,       /* rope_single over every head, src/kernel/mod.rs:258-271 */
+    NEXUS_OP_ARGMAX = 11      /* greedy_token, src/engine/mod.rs:809-817 */
+};
+
+typedef struct {
+    int kind;          /* NEXUS_OP_* */
+    int device_ptrs;   /* 1: pointers are device pointers on the backend's device */
+    const void *a;     /* MATMUL A / norm input / quantize input / dequant blocks / QMATVEC X /
+                          ATTENTION q / SOFTMAX input / ADD,MUL lhs / ROPE in-out / ARGMAX logits */
+    const void *b;     /* MATMUL B / norm weight / QMATVEC W blocks / ATTENTION keys / ADD,MUL rhs */
+    const void *c;     /* ATTENTION values / LAYER_NORM bias (may be NULL) */
+    void *out;         /* written output (ARGMAX: one uint32) */
+    size_t m, n, k;    /* MATMUL/QMATVEC dims; norms and softmax: m rows of n;
+                          ATTENTION: m = q heads, n = seq_len, k = head_dim; ROPE: m heads of k;
+                          DEQUANTIZE: m = bytes available at `a` (0 = exactly the block count) */
+    size_t len;        /* element count for ADD/MUL/QUANTIZE/DEQUANTIZE/ARGMAX */
+    size_t kv_heads;   /* ATTENTION: KV heads (GQA group = m / kv_heads) */
+    size_t position;   /* ROPE position */
+    float scale;       /* ATTENTION score scale (0 = 1/sqrt(head_dim)); ROPE base */
+    float eps;         /* norm epsilon */
+    int format;        /* NEXUS_FMT_* for QUANTIZE/DEQUANTIZE/QMATVEC */
+    int transpose_b;   /* MATMUL: 1 = B is [n,k] (the doc's A @ B^T, src/backend/mod.rs:119);
+                          0 = B is [k,n] (what CpuBackend::matmul computes, src/backend/cpu.rs:24-38) */
+} nexus_op;
+
+/* Backend::execute (src/backend/mod.rs:92).  Unlike the CPU backend, which
+ * discards its results (src/backend/cpu.rs:140-157), the output is written. */
+int nexus_cuda_execute(nexus_cuda_backend *b, const nexus_op *op);
+
+/* ======================================================================== */
+/* Quantized weights resident on the device (for the GEMV sweep and callers  */
+/* that manage their own matrices)                                           */
+/* ======================================================================== */
+typedef struct nexus_cuda_qweight nexus_cuda_qweight;
+/* Uploads rows x cols elements of GGUF blocks (row-major, cols % 256 == 0 for
+ * K-quants and Q4_0/Q8_0) and repacks them into the device tile layout. */
+int nexus_cuda_qweight_create(nexus_cuda_backend *b, int format, size_t rows, size_t cols,
+                              const void *blocks, size_t nbytes, nexus_cuda_qweight **out);
+int nexus_cuda_qweight_destroy(nexus_cuda_qweight *w);
+/* Y[m, rows] = X[m, cols] @ W^T on device pointers, on the backend's stream.
+ * Asynchronous: call nexus_cuda_synchronize before reading Y on the host. */
+int nexus_cuda_qmatvec_device(nexus_cuda_qweight *w, const float *x_dev, size_t m, float *y_dev);
+/* Same with host buffers (copies inside, synchronous). */
+int nexus_cuda_qmatvec_host(nexus_cuda_qweight *w, const float *x, size_t m, float *y);
+/* Bit-exact dequantization of the stored weight back to f32 (rows*cols floats, host). */
+int nexus_cuda_qweight_dequantize(nexus_cuda_qweight *w, float *out);
+/* Device bytes of the repacked weight (the GEMV's algorithmic weight traffic). */
+size_t nexus_cuda_qweight_bytes(const nexus_cuda_qweight *w);
+
+/* ======================================================================== */
+/* Engine-level calls: the real hot boundary.  InferenceEngine               */
+/* (src/engine/mod.rs:503-1238) calls these instead of its own matvec loop.  */
+/* ======================================================================== */
+typedef struct nexus_cuda_model nexus_cuda_model;
+
+typedef struct {
+    uint32_t num_layers, hidden_size, ff_dim, num_heads, num_kv_heads, head_dim;
+    uint32_t vocab_rows;   /* logits length (output head rows) */
+    uint32_t max_seq_len;
+    float rope_freq_base;
+    float rms_norm_eps;
+    uint64_t weight_bytes; /* device bytes of all streamed weights (per decode step) */
+    int body_format;       /* format of blk.*.attn_q (for reporting) */
+} nexus_cuda_model_info;
+
+/* InferenceEngine::load_model (src/engine/mod.rs:539-692): mmaps the GGUF,
+ * uploads raw blocks (no f32 materialization) and repacks them on the device. */
+int nexus_cuda_model_load(nexus_cuda_backend *b, const char *gguf_path, nexus_cuda_model **out);
+int nexus_cuda_model_free(nexus_cuda_model *m);
+int nexus_cuda_model_get_info(const nexus_cuda_model *m, nexus_cuda_model_info *info);
+
+/* Sequences: ids in [0, max_batch).  Every sequence owns a KV cache. */
+/* KvCache::clear for one sequence (src/engine/mod.rs:437-441) */
+int nexus_cuda_seq_reset(nexus_cuda_model *m, uint32_t seq_id);
+/* tokens currently cached for a sequence (KvCache::seq_len) */
+int nexus_cuda_seq_len(nexus_cuda_model *m, uint32_t seq_id, uint32_t *len);
+
+/* decode_with_cache(token, position) (src/engine/mod.rs:1087-1146).
+ * logits (vocab_rows floats) may be NULL; argmax (greedy_token) may be NULL. */
+int nexus_cuda_decode(nexus_cuda_model *m, uint32_t seq_id, uint32_t token, uint32_t position,
+                      float *logits, uint32_t *argmax);
+
+/* prefill(tokens) (src/engine/mod.rs:1149-1170): clears the sequence's cache
+ * and runs every token; logits/argmax are those of the last token. */
+int nexus_cuda_prefill(nexus_cuda_model *m, uint32_t seq_id, const uint32_t *tokens, size_t n,
+                       float *logits, uint32_t *argmax);
+
+/* generate with greedy sampling (generate_with_config_streaming at
+ * temperature 0, src/engine/mod.rs:1196-1238): out gets n + max_tokens ids. */
+int nexus_cuda_generate(nexus_cuda_model *m, uint32_t seq_id, const uint32_t *prompt, size_t n,
+                        size_t max_tokens, uint32_t *out);
+
+/* One decode step for a batch of sequences (Scheduler::decode_batch items,
+ * src/scheduler.rs:108-115,207-229).  page_ids lists the sequence's KV pages
+ * (Scheduler::allocate_kv_pages, src/scheduler.rs:333-361); NULL = the
+ * library's own per-sequence pages. */
+typedef struct {
+    uint32_t seq_id;
+    uint32_t token;
+    uint32_t position;
+    uint32_t n_pages;
+    const uint32_t *page_ids;
+} nexus_decode_item;
+int nexus_cuda_decode_batch(nexus_cuda_model *m, const nexus_decode_item *items, size_t n,
+                            uint32_t *out_tokens, float *out_logits);
+
+/* Device time of the last decode/prefill call in milliseconds (CUDA events). */
+int nexus_cuda_last_step_ms(const nexus_cuda_model *m, float *ms);
+
+/* Per-kernel profile of `steps` single-token decode steps of sequence seq_id
+ * (continuing from its current length, greedy tokens fed back): every kernel
+ * launch is bracketed by CUDA events on the launching stream, no graph.  One
+ * record per kernel role; bytes = algorithmic bytes per launch (weights read
+ * + activations read and written).  The KV cache advances by `steps`. */
+typedef struct {
+    char name[24];       /* embed, qkv, kv_pack, attention, o_proj, gate_up, down, head, advance */
+    uint32_t launches;
+    float total_ms;
+    double bytes_per_launch;
+} nexus_kernel_profile;
+int nexus_cuda_profile_decode(nexus_cuda_model *m, uint32_t seq_id, uint32_t token, uint32_t steps,
+                              nexus_kernel_profile *out, int max_out, int *n_out);
+
+/* ======================================================================== */
+/* Host utilities (the reference's converter and quantizers)                 */
+/* ======================================================================== */
+
+/* QuantEngine::quantize_weights on the host (src/quant/mod.rs:623-640);
+ * returns bytes written or 0 for an unsupported format. */
+size_t nexus_quantize_host(int format, const float *x, size_t n, uint8_t *out);
+/* bytes for n elements (GgufDataType::bytes_per_element, src/gguf/mod.rs:246-291) */
+size_t nexus_format_bytes(int format, size_t n);
+
+/* Seeded synthetic LLaMA-style GGUF v3 writer following nexus-convert's file
+ * conventions (tools/nexus-convert/main.rs:190-383): blk.N.* names, [out,in]
+ * shapes, llama.* keys, 32-byte alignment; weights N(0, std^2) from a
+ * counter-based generator, norms 1.0 quantized with norm_format. */
+typedef struct {
+    uint32_t num_layers, hidden_size, num_heads, num_kv_heads, ff_dim, vocab_size;
+    uint32_t context_length;
+    float rope_theta;       /* written as llama.rope.freq_base */
+    float weight_std;       /* 0.02 */
+    uint64_t seed;
+    int attn_format;        /* q/k/v/o */
+    int ffn_format;         /* gate/up/down */
+    int embd_format;        /* token_embd */
+    int head_format;        /* output (LM head); -1 = no output.weight (tied) */
+    int norm_format;        /* attn_norm/ffn_norm/output_norm */
+    int threads;            /* generator threads (0 = all cores) */
+} nexus_synth_config;
+int nexus_synth_model_write(const char *path, const nexus_synth_config *cfg);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NEXUS_CUDA_H */

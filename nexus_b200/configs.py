@@ -1,0 +1,64 @@
+"""Synthetic model configurations of the benchmark workloads.
+
+Random-init LLaMA-style models with the shapes of the reference's headline
+configurations (weights N(0, 0.02^2), seed 0, norms 1.0 quantized with the
+body format as nexus-convert does, tools/nexus-convert/main.rs:151).  No
+public dataset or checkpoint is involved: every input is seeded and synthetic.
+"""
+from __future__ import annotations
+
+import hashlib
+import json
+import os
+from pathlib import Path
+
+from ._lib import Q2_K, Q4_K, Q8_0
+
+GENERATOR_VERSION = 1
+
+CONFIGS = {
+    # tiny: 4 layers, hidden 256, 8/4 heads, head_dim 32, FFN 768, vocab 4096, all Q4_K
+    "tiny": dict(num_layers=4, hidden_size=256, num_heads=8, num_kv_heads=4, ff_dim=768, vocab_size=4096,
+                 context_length=512, rope_theta=10000.0, attn_format=Q4_K, ffn_format=Q4_K, embd_format=Q4_K,
+                 head_format=Q4_K, norm_format=Q4_K),
+    # Llama-3-8B shape, Q4_K body, Q8_0 embedding and LM head
+    "llama8b_q4k": dict(num_layers=32, hidden_size=4096, num_heads=32, num_kv_heads=8, ff_dim=14336,
+                        vocab_size=128256, context_length=8448, rope_theta=500000.0, attn_format=Q4_K,
+                        ffn_format=Q4_K, embd_format=Q8_0, head_format=Q8_0, norm_format=Q4_K),
+    # Llama-3-8B shape, Q8_0 everywhere (packed-KV serving workload)
+    "llama8b_q8": dict(num_layers=32, hidden_size=4096, num_heads=32, num_kv_heads=8, ff_dim=14336,
+                       vocab_size=128256, context_length=8448, rope_theta=500000.0, attn_format=Q8_0,
+                       ffn_format=Q8_0, embd_format=Q8_0, head_format=Q8_0, norm_format=Q8_0),
+    # Llama-3-70B shape, Q4_K attention, Q2_K FFN, Q8_0 embedding/head (assumed)
+    "llama70b": dict(num_layers=80, hidden_size=8192, num_heads=64, num_kv_heads=8, ff_dim=28672,
+                     vocab_size=128256, context_length=4352, rope_theta=500000.0, attn_format=Q4_K,
+                     ffn_format=Q2_K, embd_format=Q8_0, head_format=Q8_0, norm_format=Q4_K),
+}
+
+
+def config_key(cfg: dict) -> str:
+    blob = json.dumps({"v": GENERATOR_VERSION, **cfg}, sort_keys=True).encode()
+    return hashlib.sha1(blob).hexdigest()[:12]
+
+
+def model_dir() -> Path:
+    d = Path(os.environ.get("NEXUS_MODEL_DIR", "/tmp/nexus_models"))
+    d.mkdir(parents=True, exist_ok=True)
+    return d
+
+
+def model_path(name_or_cfg, seed: int = 0, threads: int = 0) -> Path:
+    """Path of the synthetic GGUF for a configuration, writing it on first use."""
+    from .engine import write_synthetic_model
+
+    cfg = dict(CONFIGS[name_or_cfg]) if isinstance(name_or_cfg, str) else dict(name_or_cfg)
+    cfg["seed"] = seed
+    tag = name_or_cfg if isinstance(name_or_cfg, str) else "custom"
+    path = model_dir() / f"{tag}-{config_key(cfg)}.gguf"
+    done = path.with_suffix(".ok")
+    if not (path.exists() and done.exists()):
+        tmp = path.with_suffix(".tmp")
+        write_synthetic_model(str(tmp), threads=threads, **cfg)
+        os.replace(tmp, path)
+        done.write_text("ok")
+    return path

@@ -1,0 +1,1464 @@
+// engine.cu -- the CUDA backend behind include/nexus_cuda.h.
+//
+// Host orchestration of the decode step that InferenceEngine runs on the CPU
+// in the reference (src/engine/mod.rs:539-1238): model upload, per-sequence KV
+// caches, the per-token layer loop as one CUDA graph of fused kernels, greedy
+// generation chained on the device, batched decode, and the generic KernelOp
+// surface of Backend::execute (src/backend/mod.rs:92).
+#include <cuda_runtime.h>
+#include <math.h>
+#include <string.h>
+
+#include <algorithm>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/nexus_cuda.h"
+#include "gguf.h"
+#include "kernels.h"
+#include "quant_math.cuh"
+#include "tiles.cuh"
+
+namespace nx {
+int synth_model_write(const char *path, const nexus_synth_config *cfg, std::string &err);
+}
+
+using namespace nx;
+
+static thread_local std::string g_tls_error;
+
+struct nexus_cuda_backend {
+    nexus_cuda_config cfg;
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::string last_error;
+    std::mutex mu;
+};
+
+static int set_err(nexus_cuda_backend *b, int code, const std::string &msg) {
+    if (b) b->last_error = msg;
+    g_tls_error = msg;
+    return code;
+}
+
+#define NX_CUDA(b, call)                                                                        \
+    do {                                                                                        \
+        cudaError_t e_ = (call);                                                                \
+        if (e_ != cudaSuccess)                                                                  \
+            return set_err((b), NEXUS_E_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+// ---------------------------------------------------------------------------
+// device allocation helper
+// ---------------------------------------------------------------------------
+template <typename T>
+static cudaError_t dalloc(T **p, size_t count) {
+    *p = nullptr;
+    if (count == 0) count = 1;
+    return cudaMalloc((void **)p, count * sizeof(T));
+}
+
+struct Mat {
+    int fmt = -1;
+    int n = 0, k = 0;
+    uint4 *main = nullptr;
+    uint32_t *aux = nullptr;
+    size_t bytes = 0;  // main + aux bytes (streamed per use)
+    void release() {
+        if (main) cudaFree(main);
+        if (aux) cudaFree(aux);
+        main = nullptr;
+        aux = nullptr;
+    }
+};
+
+// Upload rows x k raw block bytes (already row-permuted) and repack to tiles.
+static int make_mat(nexus_cuda_backend *b, int fmt, int n, int k, const uint8_t *raw_host, Mat &m) {
+    if (!tile_supported(fmt)) return set_err(b, NEXUS_E_UNSUPPORTED_FORMAT, "matrix format not supported by the GEMV");
+    if (k % 256 != 0) return set_err(b, NEXUS_E_INVALID, "matrix columns must be a multiple of 256");
+    m.fmt = fmt;
+    m.n = n;
+    m.k = k;
+    size_t mb = tile_main_bytes(fmt, n, k), ab = tile_aux_bytes(fmt, n, k);
+    size_t rawb = format_bytes(fmt, (size_t)n * k);
+    NX_CUDA(b, dalloc((uint8_t **)&m.main, mb));
+    if (ab) NX_CUDA(b, dalloc((uint8_t **)&m.aux, ab));
+    m.bytes = mb + ab;
+    uint8_t *draw = nullptr;
+    NX_CUDA(b, dalloc(&draw, rawb));
+    cudaError_t e = cudaMemcpyAsync(draw, raw_host, rawb, cudaMemcpyHostToDevice, b->stream);
+    if (e == cudaSuccess) e = launch_repack_tiles(fmt, draw, n, k, m.main, m.aux, b->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    cudaFree(draw);
+    if (e != cudaSuccess) return set_err(b, NEXUS_E_CUDA, std::string("repack: ") + cudaGetErrorString(e));
+    return NEXUS_OK;
+}
+
+// ---------------------------------------------------------------------------
+// backend
+// ---------------------------------------------------------------------------
+extern "C" void nexus_cuda_config_default(nexus_cuda_config *cfg) {
+    memset(cfg, 0, sizeof(*cfg));
+    cfg->device = 0;
+    cfg->tp = 1;
+    cfg->max_batch = 1;
+    cfg->page_tokens = 16;
+}
+
+extern "C" int nexus_cuda_is_available(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return 0;
+    }
+    for (int i = 0; i < n; i++) {
+        cudaDeviceProp p;
+        if (cudaGetDeviceProperties(&p, i) == cudaSuccess && p.major == 10) return 1;
+    }
+    return 0;
+}
+
+extern "C" int nexus_cuda_capabilities(nexus_cuda_caps *caps) {
+    if (!caps) return NEXUS_E_INVALID;
+    memset(caps, 0, sizeof(*caps));
+    caps->backend = "cuda";
+    caps->available = nexus_cuda_is_available();
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+    }
+    caps->device_count = n;
+    static const char *features[] = {"sm_100a", "tile-gemv-dp4a", "pdl", "cuda-graphs", "packed-kv", "gqa-split-k"};
+    static const char *ops[] = {"matmul", "attention", "rms_norm", "layer_norm", "softmax", "quantize", "dequantize"};
+    if (caps->available) {
+        for (const char *f : features) caps->features[caps->n_features++] = f;
+        for (const char *o : ops) caps->supported_ops[caps->n_supported_ops++] = o;
+    }
+    return NEXUS_OK;
+}
+
+extern "C" int nexus_cuda_backend_create(const nexus_cuda_config *cfg, nexus_cuda_backend **out) {
+    if (!out) return set_err(nullptr, NEXUS_E_INVALID, "out is NULL");
+    *out = nullptr;
+    nexus_cuda_config c;
+    if (cfg) c = *cfg;
+    else nexus_cuda_config_default(&c);
+    if (c.tp < 1) c.tp = 1;
+    if (c.max_batch < 1) c.max_batch = 1;
+    if (c.page_tokens == 0) c.page_tokens = 16;
+    if (c.tp != 1) return set_err(nullptr, NEXUS_E_INVALID, "tensor parallelism is driven by one process per GPU; tp must be 1 per backend");
+    if ((c.kv_bits_k == 0) != (c.kv_bits_v == 0)) return set_err(nullptr, NEXUS_E_INVALID, "kv_bits_k and kv_bits_v must both be 0 or both set");
+    if (c.kv_bits_k > 8 || c.kv_bits_v > 8) return set_err(nullptr, NEXUS_E_INVALID, "packed KV supports 1..8 bits");
+    if (!nexus_cuda_is_available()) return set_err(nullptr, NEXUS_E_UNAVAILABLE, "no sm_100 CUDA device");
+    int ndev = 0;
+    cudaGetDeviceCount(&ndev);
+    if (c.device < 0 || c.device >= ndev) return set_err(nullptr, NEXUS_E_INVALID, "bad device ordinal");
+    auto *b = new nexus_cuda_backend();
+    b->cfg = c;
+    b->device = c.device;
+    cudaError_t e = cudaSetDevice(c.device);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        delete b;
+        return set_err(nullptr, NEXUS_E_CUDA, std::string("backend init: ") + cudaGetErrorString(e));
+    }
+    *out = b;
+    return NEXUS_OK;
+}
+
+extern "C" int nexus_cuda_backend_destroy(nexus_cuda_backend *b) {
+    if (!b) return NEXUS_OK;
+    cudaSetDevice(b->device);
+    if (b->stream) {
+        cudaStreamSynchronize(b->stream);
+        cudaStreamDestroy(b->stream);
+    }
+    delete b;
+    return NEXUS_OK;
+}
+
+extern "C" const char *nexus_cuda_backend_name(const nexus_cuda_backend *) { return "cuda"; }
+
+extern "C" int nexus_cuda_memory_info(nexus_cuda_backend *b, size_t *total, size_t *free_bytes, size_t *used) {
+    if (!b) return set_err(nullptr, NEXUS_E_INVALID, "backend is NULL");
+    cudaSetDevice(b->device);
+    size_t f = 0, t = 0;
+    NX_CUDA(b, cudaMemGetInfo(&f, &t));
+    if (total) *total = t;
+    if (free_bytes) *free_bytes = f;
+    if (used) *used = t - f;
+    return NEXUS_OK;
+}
+
+extern "C" int nexus_cuda_synchronize(nexus_cuda_backend *b) {
+    if (!b) return set_err(nullptr, NEXUS_E_INVALID, "backend is NULL");
+    cudaSetDevice(b->device);
+    NX_CUDA(b, cudaStreamSynchronize(b->stream));
+    return NEXUS_OK;
+}
+
+extern "C" const char *nexus_cuda_last_error(const nexus_cuda_backend *b) {
+    return b ? b->last_error.c_str() : g_tls_error.c_str();
+}
+
+// ---------------------------------------------------------------------------
+// Backend::execute
+// ---------------------------------------------------------------------------
+namespace {
+// Device view of an op operand: copies host data in (and out) when needed.
+struct DevArg {
+    void *d = nullptr;
+    bool owned = false;
+    ~DevArg() {
+        if (owned && d) cudaFree(d);
+    }
+};
+cudaError_t stage_in(const void *p, size_t bytes, bool device, DevArg &a, cudaStream_t st) {
+    if (device || !p) {
+        a.d = const_cast<void *>(p);
+        return cudaSuccess;
+    }
+    cudaError_t e = cudaMalloc(&a.d, bytes ? bytes : 1);
+    if (e != cudaSuccess) return e;
+    a.owned = true;
+    return bytes ? cudaMemcpyAsync(a.d, p, bytes, cudaMemcpyHostToDevice, st) : cudaSuccess;
+}
+cudaError_t stage_out(void *p, size_t bytes, bool device, DevArg &a) {
+    if (device) {
+        a.d = p;
+        return cudaSuccess;
+    }
+    cudaError_t e = cudaMalloc(&a.d, bytes ? bytes : 1);
+    a.owned = e == cudaSuccess;
+    return e;
+}
+}  // namespace
+
+extern "C" int nexus_cuda_execute(nexus_cuda_backend *b, const nexus_op *op) {
+    if (!b || !op) return set_err(b, NEXUS_E_INVALID, "NULL backend or op");
+    std::lock_guard<std::mutex> lk(b->mu);
+    cudaSetDevice(b->device);
+    cudaStream_t st = b->stream;
+    const bool dev = op->device_ptrs != 0;
+    DevArg A, B, Cc, O;
+    size_t out_bytes = 0;
+    cudaError_t e = cudaSuccess;
+    switch (op->kind) {
+    case NEXUS_OP_MATMUL: {
+        size_t m = op->m, n = op->n, k = op->k;
+        out_bytes = m * n * 4;
+        NX_CUDA(b, stage_in(op->a, m * k * 4, dev, A, st));
+        NX_CUDA(b, stage_in(op->b, n * k * 4, dev, B, st));
+        NX_CUDA(b, stage_out(op->out, out_bytes, dev, O));
+        e = launch_matmul_f32((const float *)A.d, (const float *)B.d, (float *)O.d, (int)m, (int)n, (int)k,
+                              op->transpose_b, st);
+        break;
+    }
+    case NEXUS_OP_RMS_NORM:
+    case NEXUS_OP_LAYER_NORM: {
+        size_t rows = op->m ? op->m : 1, n = op->n;
+        out_bytes = rows * n * 4;
+        NX_CUDA(b, stage_in(op->a, out_bytes, dev, A, st));
+        NX_CUDA(b, stage_in(op->b, n * 4, dev, B, st));
+        if (op->kind == NEXUS_OP_LAYER_NORM) NX_CUDA(b, stage_in(op->c, op->c ? n * 4 : 0, dev, Cc, st));
+        NX_CUDA(b, stage_out(op->out, out_bytes, dev, O));
+        if (op->kind == NEXUS_OP_RMS_NORM)
+            e = launch_rms_norm((const float *)A.d, (const float *)B.d, (float *)O.d, (int)rows, (int)n, op->eps, st);
+        else
+            e = launch_layer_norm((const float *)A.d, (const float *)B.d, (const float *)Cc.d, (float *)O.d,
+                                  (int)rows, (int)n, op->eps, st);
+        break;
+    }
+    case NEXUS_OP_SOFTMAX: {
+        size_t rows = op->m ? op->m : 1, n = op->n;
+        out_bytes = rows * n * 4;
+        NX_CUDA(b, stage_in(op->a, out_bytes, dev, A, st));
+        NX_CUDA(b, stage_out(op->out, out_bytes, dev, O));
+        e = launch_softmax((const float *)A.d, (float *)O.d, (int)rows, (int)n, st);
+        break;
+    }
+    case NEXUS_OP_ADD:
+    case NEXUS_OP_MUL: {
+        out_bytes = op->len * 4;
+        NX_CUDA(b, stage_in(op->a, out_bytes, dev, A, st));
+        NX_CUDA(b, stage_in(op->b, out_bytes, dev, B, st));
+        NX_CUDA(b, stage_out(op->out, out_bytes, dev, O));
+        e = launch_binary(op->kind == NEXUS_OP_ADD ? 0 : 1, (const float *)A.d, (const float *)B.d, (float *)O.d,
+                          op->len, st);
+        break;
+    }
+    case NEXUS_OP_QUANTIZE: {
+        if (!format_supported(op->format) || op->format == F32 || op->format == F16 || op->format == BF16)
+            return set_err(b, NEXUS_E_UNSUPPORTED_FORMAT, "quantize: format must be Q8_0/Q4_0/Q4_K/Q2_K");
+        out_bytes = format_bytes(op->format, op->len);
+        NX_CUDA(b, stage_in(op->a, op->len * 4, dev, A, st));
+        NX_CUDA(b, stage_out(op->out, out_bytes, dev, O));
+        e = launch_quantize(op->format, (const float *)A.d, op->len, (uint8_t *)O.d, st);
+        break;
+    }
+    case NEXUS_OP_DEQUANTIZE: {
+        if (!format_supported(op->format)) return set_err(b, NEXUS_E_UNSUPPORTED_FORMAT, "dequantize: unsupported format");
+        size_t need = format_bytes(op->format, op->len);
+        // tensor_bytes_to_f32 rejects payloads shorter than their block count
+        if (op->m && op->m < need) return set_err(b, NEXUS_E_TRUNCATED, "payload is truncated");
+        out_bytes = op->len * 4;
+        NX_CUDA(b, stage_in(op->a, need, dev, A, st));
+        NX_CUDA(b, stage_out(op->out, out_bytes, dev, O));
+        e = launch_dequant_raw(op->format, (const uint8_t *)A.d, op->len, (float *)O.d, st);
+        break;
+    }
+    case NEXUS_OP_QMATVEC: {
+        size_t m = op->m, n = op->n, k = op->k;
+        if (!tile_supported(op->format)) return set_err(b, NEXUS_E_UNSUPPORTED_FORMAT, "qmatvec: unsupported format");
+        if (k % 256) return set_err(b, NEXUS_E_INVALID, "qmatvec: k must be a multiple of 256");
+        size_t wbytes = format_bytes(op->format, n * k);
+        std::vector<uint8_t> hostw;
+        const uint8_t *wsrc = (const uint8_t *)op->b;
+        if (dev) {
+            hostw.resize(wbytes);
+            NX_CUDA(b, cudaMemcpy(hostw.data(), op->b, wbytes, cudaMemcpyDeviceToHost));
+            wsrc = hostw.data();
+        }
+        Mat mat;
+        int rc = make_mat(b, op->format, (int)n, (int)k, wsrc, mat);
+        if (rc) return rc;
+        out_bytes = m * n * 4;
+        NX_CUDA(b, stage_in(op->a, m * k * 4, dev, A, st));
+        NX_CUDA(b, stage_out(op->out, out_bytes, dev, O));
+        for (size_t t0 = 0; t0 < m && e == cudaSuccess;) {
+            size_t chunk = m - t0 >= 4 ? 4 : m - t0 >= 2 ? 2 : 1;
+            GemvParams p = {};
+            p.fmt = op->format;
+            p.w_main = mat.main;
+            p.w_aux = mat.aux;
+            p.n = (int)n;
+            p.k = (int)k;
+            p.m = (int)chunk;
+            p.x = (const float *)A.d + t0 * k;
+            p.x_stride = (int)k;
+            p.epi = EPI_STORE;
+            p.y = (float *)O.d + t0 * n;
+            p.y_stride = (int)n;
+            e = launch_gemv(p, st);
+            t0 += chunk;
+        }
+        cudaError_t e2 = cudaStreamSynchronize(st);
+        mat.release();
+        if (e == cudaSuccess) e = e2;
+        break;
+    }
+    case NEXUS_OP_ROPE: {
+        size_t heads = op->m, hd = op->k;
+        out_bytes = heads * hd * 4;
+        if (hd % 2) return set_err(b, NEXUS_E_INVALID, "rope: head_dim must be even");
+        NX_CUDA(b, stage_in(op->a, out_bytes, dev, A, st));
+        O.d = A.d;
+        e = launch_rope((float *)A.d, (int)heads, (int)hd, (int)op->position, op->scale, st);
+        if (e == cudaSuccess && !dev) {
+            NX_CUDA(b, cudaMemcpyAsync(op->out ? op->out : (void *)op->a, A.d, out_bytes, cudaMemcpyDeviceToHost, st));
+            NX_CUDA(b, cudaStreamSynchronize(st));
+            return NEXUS_OK;
+        }
+        if (e == cudaSuccess && op->out && op->out != op->a)
+            e = cudaMemcpyAsync(op->out, A.d, out_bytes, cudaMemcpyDeviceToDevice, st);
+        O.d = nullptr;
+        out_bytes = 0;
+        break;
+    }
+    case NEXUS_OP_ARGMAX: {
+        NX_CUDA(b, stage_in(op->a, op->len * 4, dev, A, st));
+        unsigned long long *best = nullptr;
+        NX_CUDA(b, dalloc(&best, 1));
+        e = launch_argmax((const float *)A.d, op->len, best, st);
+        unsigned long long hb = 0;
+        if (e == cudaSuccess) e = cudaMemcpyAsync(&hb, best, 8, cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        cudaFree(best);
+        if (e != cudaSuccess) return set_err(b, NEXUS_E_CUDA, cudaGetErrorString(e));
+        uint32_t tok = (uint32_t)(hb & 0xffffffffull);
+        if (dev) NX_CUDA(b, cudaMemcpy(op->out, &tok, 4, cudaMemcpyHostToDevice));
+        else memcpy(op->out, &tok, 4);
+        return NEXUS_OK;
+    }
+    case NEXUS_OP_ATTENTION: {
+        // GQA decode attention of one query token over n cached tokens:
+        // q [m*k], keys/values [n][kv_heads*k]
+        size_t hq = op->m, seq = op->n, hd = op->k, hkv = op->kv_heads ? op->kv_heads : op->m;
+        if (seq == 0 || hkv == 0 || hq % hkv) return set_err(b, NEXUS_E_INVALID, "attention: bad shape");
+        size_t kv_dim = hkv * hd;
+        out_bytes = hq * hd * 4;
+        NX_CUDA(b, stage_in(op->a, hq * hd * 4, dev, A, st));
+        NX_CUDA(b, stage_in(op->b, seq * kv_dim * 4, dev, B, st));
+        NX_CUDA(b, stage_in(op->c, seq * kv_dim * 4, dev, Cc, st));
+        NX_CUDA(b, stage_out(op->out, out_bytes, dev, O));
+        DevSeq hs = {};
+        hs.seq_len = (uint32_t)seq;
+        hs.slot = (uint32_t)(seq - 1);
+        DevSeq *ds = nullptr;
+        uint32_t *sid = nullptr;
+        float *part = nullptr;
+        unsigned *ctr = nullptr;
+        int nsplit = (int)std::min<size_t>(64, std::max<size_t>(1, seq / 16));
+        size_t G = hq / hkv;
+        NX_CUDA(b, dalloc(&ds, 1));
+        NX_CUDA(b, dalloc(&sid, 1));
+        NX_CUDA(b, dalloc(&part, hkv * nsplit * G * (hd + 2)));
+        NX_CUDA(b, dalloc(&ctr, hkv));
+        NX_CUDA(b, cudaMemsetAsync(sid, 0, 4, st));
+        NX_CUDA(b, cudaMemsetAsync(ctr, 0, hkv * 4, st));
+        NX_CUDA(b, cudaMemcpyAsync(ds, &hs, sizeof(hs), cudaMemcpyHostToDevice, st));
+        AttnParams p = {};
+        p.hq = (int)hq;
+        p.hkv = (int)hkv;
+        p.head_dim = (int)hd;
+        p.m = 1;
+        p.q = (const float *)A.d;
+        p.out = (float *)O.d;
+        p.scale = op->scale != 0.0f ? op->scale : 1.0f / sqrtf((float)hd);
+        p.k_cache = (const float *)B.d;
+        p.v_cache = (const float *)Cc.d;
+        p.seq_stride = 0;
+        p.seqs = ds;
+        p.seq_ids = sid;
+        p.kv_dim = (int)kv_dim;
+        p.nsplit = nsplit;
+        p.part = part;
+        p.counters = ctr;
+        e = launch_attention(p, st);
+        cudaError_t e2 = cudaStreamSynchronize(st);
+        cudaFree(ds);
+        cudaFree(sid);
+        cudaFree(part);
+        cudaFree(ctr);
+        if (e == cudaSuccess) e = e2;
+        break;
+    }
+    default: return set_err(b, NEXUS_E_INVALID, "unknown op kind");
+    }
+    if (e != cudaSuccess) return set_err(b, NEXUS_E_CUDA, std::string("execute: ") + cudaGetErrorString(e));
+    if (!dev && out_bytes) NX_CUDA(b, cudaMemcpyAsync(op->out, O.d, out_bytes, cudaMemcpyDeviceToHost, st));
+    NX_CUDA(b, cudaStreamSynchronize(st));
+    return NEXUS_OK;
+}
+
+// ---------------------------------------------------------------------------
+// resident quantized weights
+// ---------------------------------------------------------------------------
+struct nexus_cuda_qweight {
+    nexus_cuda_backend *b = nullptr;
+    Mat mat;
+    float *xbuf = nullptr, *ybuf = nullptr;
+    size_t xcap = 0, ycap = 0;
+};
+
+extern "C" int nexus_cuda_qweight_create(nexus_cuda_backend *b, int format, size_t rows, size_t cols,
+                                         const void *blocks, size_t nbytes, nexus_cuda_qweight **out) {
+    if (!b || !out || !blocks) return set_err(b, NEXUS_E_INVALID, "NULL argument");
+    *out = nullptr;
+    if (!tile_supported(format)) return set_err(b, NEXUS_E_UNSUPPORTED_FORMAT, "qweight: unsupported format");
+    if (rows == 0 || cols == 0 || cols % 256) return set_err(b, NEXUS_E_INVALID, "qweight: cols must be a multiple of 256");
+    if (nbytes < format_bytes(format, rows * cols)) return set_err(b, NEXUS_E_TRUNCATED, "qweight: payload is truncated");
+    cudaSetDevice(b->device);
+    auto *w = new nexus_cuda_qweight();
+    w->b = b;
+    int rc = make_mat(b, format, (int)rows, (int)cols, (const uint8_t *)blocks, w->mat);
+    if (rc) {
+        w->mat.release();
+        delete w;
+        return rc;
+    }
+    *out = w;
+    return NEXUS_OK;
+}
+
+extern "C" int nexus_cuda_qweight_destroy(nexus_cuda_qweight *w) {
+    if (!w) return NEXUS_OK;
+    cudaSetDevice(w->b->device);
+    w->mat.release();
+    if (w->xbuf) cudaFree(w->xbuf);
+    if (w->ybuf) cudaFree(w->ybuf);
+    delete w;
+    return NEXUS_OK;
+}
+
+extern "C" size_t nexus_cuda_qweight_bytes(const nexus_cuda_qweight *w) { return w ? w->mat.bytes : 0; }
+
+extern "C" int nexus_cuda_qmatvec_device(nexus_cuda_qweight *w, const float *x_dev, size_t m, float *y_dev) {
+    if (!w || !x_dev || !y_dev) return set_err(w ? w->b : nullptr, NEXUS_E_INVALID, "NULL argument");
+    nexus_cuda_backend *b = w->b;
+    cudaSetDevice(b->device);
+    for (size_t t0 = 0; t0 < m;) {
+        size_t chunk = m - t0 >= 4 ? 4 : m - t0 >= 2 ? 2 : 1;
+        GemvParams p = {};
+        p.fmt = w->mat.fmt;
+        p.w_main = w->mat.main;
+        p.w_aux = w->mat.aux;
+        p.n = w->mat.n;
+        p.k = w->mat.k;
+        p.m = (int)chunk;
+        p.x = x_dev + t0 * w->mat.k;
+        p.x_stride = w->mat.k;
+        p.epi = EPI_STORE;
+        p.y = y_dev + t0 * w->mat.n;
+        p.y_stride = w->mat.n;
+        NX_CUDA(b, launch_gemv(p, b->stream));
+        t0 += chunk;
+    }
+    return NEXUS_OK;
+}
+
+extern "C" int nexus_cuda_qmatvec_host(nexus_cuda_qweight *w, const float *x, size_t m, float *y) {
+    if (!w || !x || !y) return set_err(w ? w->b : nullptr, NEXUS_E_INVALID, "NULL argument");
+    nexus_cuda_backend *b = w->b;
+    cudaSetDevice(b->device);
+    size_t xn = m * w->mat.k, yn = m * w->mat.n;
+    if (xn > w->xcap) {
+        if (w->xbuf) cudaFree(w->xbuf);
+        NX_CUDA(b, dalloc(&w->xbuf, xn));
+        w->xcap = xn;
+    }
+    if (yn > w->ycap) {
+        if (w->ybuf) cudaFree(w->ybuf);
+        NX_CUDA(b, dalloc(&w->ybuf, yn));
+        w->ycap = yn;
+    }
+    NX_CUDA(b, cudaMemcpyAsync(w->xbuf, x, xn * 4, cudaMemcpyHostToDevice, b->stream));
+    int rc = nexus_cuda_qmatvec_device(w, w->xbuf, m, w->ybuf);
+    if (rc) return rc;
+    NX_CUDA(b, cudaMemcpyAsync(y, w->ybuf, yn * 4, cudaMemcpyDeviceToHost, b->stream));
+    NX_CUDA(b, cudaStreamSynchronize(b->stream));
+    return NEXUS_OK;
+}
+
+extern "C" int nexus_cuda_qweight_dequantize(nexus_cuda_qweight *w, float *out) {
+    if (!w || !out) return set_err(w ? w->b : nullptr, NEXUS_E_INVALID, "NULL argument");
+    nexus_cuda_backend *b = w->b;
+    cudaSetDevice(b->device);
+    size_t n = (size_t)w->mat.n * w->mat.k;
+    float *d = nullptr;
+    NX_CUDA(b, dalloc(&d, n));
+    cudaError_t e = launch_dequant_tiles(w->mat.fmt, w->mat.main, w->mat.aux, w->mat.n, w->mat.k, d, b->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out, d, n * 4, cudaMemcpyDeviceToHost, b->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    cudaFree(d);
+    if (e != cudaSuccess) return set_err(b, NEXUS_E_CUDA, cudaGetErrorString(e));
+    return NEXUS_OK;
+}
+
+// ---------------------------------------------------------------------------
+// model
+// ---------------------------------------------------------------------------
+static constexpr int kMaxChunk = 4;  // tokens per fused step (GEMV m)
+
+struct Layer {
+    float *attn_norm = nullptr, *ffn_norm = nullptr;
+    Mat qkv, o, gateup, down;
+    float *k_cache = nullptr, *v_cache = nullptr;  // float KV [max_batch][max_seq][kv_dim]
+    uint8_t *kp = nullptr, *vp = nullptr;          // packed KV [max_batch][max_seq][bpt]
+    float *kmin = nullptr, *kscale = nullptr, *vmin = nullptr, *vscale = nullptr;
+};
+
+struct nexus_cuda_model {
+    nexus_cuda_backend *b = nullptr;
+    nexus_cuda_model_info info = {};
+    int embd_fmt = 0;
+    uint8_t *embd = nullptr;
+    size_t embd_rows = 0;
+    float *out_norm = nullptr;
+    Mat head;
+    bool has_head = false;
+    std::vector<Layer> layers;
+    float *rope_cos = nullptr, *rope_sin = nullptr;
+    float *hidden = nullptr, *q = nullptr, *attn = nullptr, *gated = nullptr, *kv_scratch = nullptr;
+    float *logits = nullptr, *part = nullptr;
+    unsigned *counters = nullptr;
+    DevSeq *seqs = nullptr;
+    uint32_t *seq_ids = nullptr, *out_tokens = nullptr;
+    DevSeq *h_seqs = nullptr;
+    uint32_t *h_seq_ids = nullptr, *h_out_tokens = nullptr;
+    std::vector<uint32_t> seq_len;
+    uint32_t max_seq = 0, max_batch = 1, bits_k = 0, bits_v = 0;
+    size_t bpt_k = 0, bpt_v = 0;
+    int nsplit[kMaxChunk + 1] = {};
+    cudaGraphExec_t graph[kMaxChunk + 1] = {};
+    bool use_graph = true, use_pdl = true;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    float last_ms = 0.0f;
+    std::vector<void *> allocs;
+};
+
+template <typename T>
+static cudaError_t malloc_tracked(nexus_cuda_model *m, T **p, size_t count) {
+    cudaError_t e = dalloc(p, count);
+    if (e == cudaSuccess) m->allocs.push_back((void *)*p);
+    return e;
+}
+
+static void model_release(nexus_cuda_model *m) {
+    if (!m) return;
+    cudaSetDevice(m->b->device);
+    cudaStreamSynchronize(m->b->stream);
+    for (auto &g : m->graph)
+        if (g) cudaGraphExecDestroy(g);
+    for (auto &L : m->layers) {
+        L.qkv.release();
+        L.o.release();
+        L.gateup.release();
+        L.down.release();
+    }
+    m->head.release();
+    for (void *p : m->allocs) cudaFree(p);
+    if (m->h_seqs) cudaFreeHost(m->h_seqs);
+    if (m->h_seq_ids) cudaFreeHost(m->h_seq_ids);
+    if (m->h_out_tokens) cudaFreeHost(m->h_out_tokens);
+    if (m->ev0) cudaEventDestroy(m->ev0);
+    if (m->ev1) cudaEventDestroy(m->ev1);
+    delete m;
+}
+
+static const GgufTensor *find_any(const GgufFile &f, const std::vector<std::string> &names) {
+    for (const auto &n : names) {
+        const GgufTensor *t = f.find(n);
+        if (t && format_supported(t->type) && t->elems() > 0) return t;
+    }
+    return nullptr;
+}
+
+// layer_tensor_names, src/engine/mod.rs:696-733
+static const GgufTensor *layer_tensor(const GgufFile &f, uint32_t l, const char *role, const char *hf) {
+    std::string s = std::to_string(l);
+    return find_any(f, {"blk." + s + "." + role + ".weight", "model.layers." + s + "." + hf + ".weight",
+                        "layers." + s + "." + hf + ".weight"});
+}
+
+// Dequantize a 1-D tensor (norm weights) to f32 on the device, bit-exact.
+static int upload_vector(nexus_cuda_model *m, const GgufFile &f, const GgufTensor *t, size_t n, float **out) {
+    nexus_cuda_backend *b = m->b;
+    NX_CUDA(b, malloc_tracked(m, out, n));
+    if (!t) {
+        std::vector<float> ones(n, 1.0f);
+        NX_CUDA(b, cudaMemcpy(*out, ones.data(), n * 4, cudaMemcpyHostToDevice));
+        return NEXUS_OK;
+    }
+    size_t nb = 0;
+    const uint8_t *src = f.data(*t, &nb);
+    if (!src || t->elems() < n) return set_err(b, NEXUS_E_TRUNCATED, "norm tensor truncated: " + t->name);
+    size_t need = format_bytes(t->type, n);
+    uint8_t *d = nullptr;
+    NX_CUDA(b, dalloc(&d, need));
+    cudaError_t e = cudaMemcpy(d, src, need, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = launch_dequant_raw(t->type, d, n, *out, b->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    cudaFree(d);
+    if (e != cudaSuccess) return set_err(b, NEXUS_E_CUDA, cudaGetErrorString(e));
+    return NEXUS_OK;
+}
+
+// Row bytes of a matrix whose columns are a multiple of the block size.
+static size_t row_bytes(int fmt, size_t k) { return k / (size_t)block_elems(fmt) * (size_t)block_bytes(fmt); }
+
+static int check_matrix(nexus_cuda_backend *b, const GgufTensor *t, size_t rows, size_t cols, const char *what) {
+    if (!t) return set_err(b, NEXUS_E_MISSING_TENSOR, std::string("Missing tensor: ") + what);
+    if (!tile_supported(t->type))
+        return set_err(b, NEXUS_E_UNSUPPORTED_FORMAT, std::string("GEMV format not supported for ") + t->name);
+    // Self::matvec requires weight.len() >= rows*cols (src/engine/mod.rs:784-790)
+    if (t->elems() < rows * cols) return set_err(b, NEXUS_E_INVALID, "Matvec weight too small: " + t->name);
+    if (cols % 256) return set_err(b, NEXUS_E_INVALID, "matrix columns must be a multiple of 256: " + t->name);
+    return NEXUS_OK;
+}
+
+static int model_load(nexus_cuda_backend *b, const char *path, nexus_cuda_model **out) {
+    GgufFile f;
+    std::string err;
+    int rc = f.open(path, err);
+    if (rc) return set_err(b, rc, err);
+    auto *m = new nexus_cuda_model();
+    m->b = b;
+    std::unique_ptr<nexus_cuda_model, void (*)(nexus_cuda_model *)> guard(m, model_release);
+    nexus_cuda_model_info &I = m->info;
+    uint64_t v;
+    // load_model metadata defaults, src/engine/mod.rs:551-562
+    I.num_layers = f.get_usize("llama.block_count", &v) ? (uint32_t)v : 32;
+    I.hidden_size = f.get_usize("llama.embedding_length", &v) ? (uint32_t)v : 4096;
+    I.ff_dim = f.get_usize("llama.feed_forward_length", &v) ? (uint32_t)v : 11008;
+    I.num_heads = f.get_usize("llama.attention.head_count", &v) ? (uint32_t)v : 32;
+    I.num_kv_heads = f.get_usize("llama.attention.head_count_kv", &v) ? (uint32_t)v : I.num_heads;
+    float fb;
+    I.rope_freq_base = f.get_f32("llama.rope.freq_base", &fb) ? fb : 1000000.0f;
+    I.rms_norm_eps = 1e-5f;  // InferenceConfig default; the GGUF key is ignored (src/engine/mod.rs:94)
+    if (!I.num_heads || !I.num_kv_heads || I.hidden_size % I.num_heads)
+        return set_err(b, NEXUS_E_INVALID, "bad head configuration");
+    I.head_dim = I.hidden_size / I.num_heads;
+    uint32_t ctx = f.get_usize("llama.context_length", &v) ? (uint32_t)v : 4096;
+    I.max_seq_len = b->cfg.max_seq_len ? b->cfg.max_seq_len : ctx;
+    const uint32_t H = I.hidden_size, D = I.head_dim, F = I.ff_dim, Hq = I.num_heads, Hkv = I.num_kv_heads;
+    const uint32_t kv_dim = Hkv * D, qdim = Hq * D;
+    if (D % 32 || D > 128 || Hq % Hkv || (Hq / Hkv) > 8 || ((Hq / Hkv) & (Hq / Hkv - 1)))
+        return set_err(b, NEXUS_E_INVALID, "head_dim must be 32/64/128 and Hq/Hkv a power of two <= 8");
+    if (H % 256 || F % 256) return set_err(b, NEXUS_E_INVALID, "hidden and ffn sizes must be multiples of 256");
+    m->max_seq = I.max_seq_len;
+    m->max_batch = b->cfg.max_batch;
+    m->bits_k = b->cfg.kv_bits_k;
+    m->bits_v = b->cfg.kv_bits_v;
+    m->use_graph = !(b->cfg.flags & NEXUS_CFG_NO_GRAPH);
+    m->use_pdl = !(b->cfg.flags & NEXUS_CFG_NO_PDL);
+    cudaSetDevice(b->device);
+
+    // embedding (raw blocks; rows decoded per token on the device)
+    const GgufTensor *te = find_any(f, {"token_embd.weight", "token_embd", "model.embed_tokens.weight", "transformer.wte.weight"});
+    if (!te) return set_err(b, NEXUS_E_MISSING_TENSOR, "Missing tensor: token_embd.weight");
+    {
+        size_t nb = 0;
+        const uint8_t *src = f.data(*te, &nb);
+        if (!src) return set_err(b, NEXUS_E_TRUNCATED, "token_embd payload truncated");
+        m->embd_fmt = te->type;
+        m->embd_rows = std::max<size_t>(1, te->elems() / H);
+        NX_CUDA(b, malloc_tracked(m, &m->embd, nb + 16));
+        NX_CUDA(b, cudaMemcpy(m->embd, src, nb, cudaMemcpyHostToDevice));
+    }
+    rc = upload_vector(m, f, find_any(f, {"output_norm.weight", "norm.weight", "model.norm.weight", "transformer.ln_f.weight"}), H,
+                       &m->out_norm);
+    if (rc) return rc;
+    const GgufTensor *th = find_any(f, {"output.weight", "lm_head.weight", "model.embed_tokens.weight", "token_embd.weight"});
+    uint64_t weight_bytes = 0;
+    if (th) {
+        size_t rows = th->elems() / H;
+        rc = check_matrix(b, th, rows, H, "output.weight");
+        if (rc) return rc;
+        size_t nb = 0;
+        const uint8_t *src = f.data(*th, &nb);
+        if (!src) return set_err(b, NEXUS_E_TRUNCATED, "output payload truncated");
+        rc = make_mat(b, th->type, (int)rows, (int)H, src, m->head);
+        if (rc) return rc;
+        m->has_head = true;
+        I.vocab_rows = (uint32_t)rows;
+        weight_bytes += m->head.bytes;
+    } else {
+        I.vocab_rows = H;  // transformer_logits returns the normed hidden state (:1040-1043)
+    }
+
+    m->layers.resize(I.num_layers);
+    std::vector<uint8_t> buf;
+    for (uint32_t l = 0; l < I.num_layers; l++) {
+        Layer &L = m->layers[l];
+        rc = upload_vector(m, f, layer_tensor(f, l, "attn_norm", "input_layernorm"), H, &L.attn_norm);
+        if (rc) return rc;
+        rc = upload_vector(m, f, layer_tensor(f, l, "ffn_norm", "post_attention_layernorm"), H, &L.ffn_norm);
+        if (rc) return rc;
+        const GgufTensor *tq = layer_tensor(f, l, "attn_q", "self_attn.q_proj");
+        const GgufTensor *tk = layer_tensor(f, l, "attn_k", "self_attn.k_proj");
+        const GgufTensor *tv = layer_tensor(f, l, "attn_v", "self_attn.v_proj");
+        const GgufTensor *to = layer_tensor(f, l, "attn_output", "self_attn.o_proj");
+        const GgufTensor *tg = layer_tensor(f, l, "ffn_gate", "mlp.gate_proj");
+        const GgufTensor *tu = layer_tensor(f, l, "ffn_up", "mlp.up_proj");
+        const GgufTensor *td = layer_tensor(f, l, "ffn_down", "mlp.down_proj");
+        std::string ls = "blk." + std::to_string(l) + ".";
+        if ((rc = check_matrix(b, tq, qdim, H, (ls + "attn_q.weight").c_str()))) return rc;
+        if ((rc = check_matrix(b, tk, kv_dim, H, (ls + "attn_k.weight").c_str()))) return rc;
+        if ((rc = check_matrix(b, tv, kv_dim, H, (ls + "attn_v.weight").c_str()))) return rc;
+        if ((rc = check_matrix(b, to, H, qdim, (ls + "attn_output.weight").c_str()))) return rc;
+        if ((rc = check_matrix(b, tg, F, H, (ls + "ffn_gate.weight").c_str()))) return rc;
+        if ((rc = check_matrix(b, tu, F, H, (ls + "ffn_up.weight").c_str()))) return rc;
+        if ((rc = check_matrix(b, td, H, F, (ls + "ffn_down.weight").c_str()))) return rc;
+        if (tq->type != tk->type || tq->type != tv->type)
+            return set_err(b, NEXUS_E_UNSUPPORTED_FORMAT, "attn_q/k/v must share one format for the fused QKV GEMV");
+        if (tg->type != tu->type)
+            return set_err(b, NEXUS_E_UNSUPPORTED_FORMAT, "ffn_gate/up must share one format for the fused SwiGLU GEMV");
+        const uint8_t *pq = f.data(*tq, nullptr), *pk = f.data(*tk, nullptr), *pv = f.data(*tv, nullptr);
+        const uint8_t *po = f.data(*to, nullptr), *pg = f.data(*tg, nullptr), *pu = f.data(*tu, nullptr);
+        const uint8_t *pd = f.data(*td, nullptr);
+        if (!pq || !pk || !pv || !po || !pg || !pu || !pd) return set_err(b, NEXUS_E_TRUNCATED, "layer payload truncated");
+        // fused Q|K|V with RoPE pairs (d, d + D/2) in lanes (i, i + 16) of a row group
+        {
+            const int fmt = tq->type;
+            const size_t rb = row_bytes(fmt, H);
+            const uint32_t nrows = qdim + 2 * kv_dim;
+            buf.resize((size_t)nrows * rb);
+            const uint32_t gph = D / 32;
+            for (uint32_t r = 0; r < nrows; r++) {
+                const uint8_t *src;
+                if (r < qdim + kv_dim) {
+                    const bool isq = r < qdim;
+                    const uint32_t rr = isq ? r : r - qdim;
+                    const uint32_t g = rr / 32, lane = rr % 32, head = g / gph, i = g % gph;
+                    const uint32_t d = lane < 16 ? 16 * i + lane : 16 * i + (lane - 16) + D / 2;
+                    src = (isq ? pq : pk) + (size_t)(head * D + d) * rb;
+                } else {
+                    src = pv + (size_t)(r - qdim - kv_dim) * rb;
+                }
+                memcpy(buf.data() + (size_t)r * rb, src, rb);
+            }
+            if ((rc = make_mat(b, fmt, (int)nrows, (int)H, buf.data(), L.qkv))) return rc;
+        }
+        if ((rc = make_mat(b, to->type, (int)H, (int)qdim, po, L.o))) return rc;
+        // gate/up interleaved: lanes 0..15 gate rows, lanes 16..31 the same up rows
+        {
+            const int fmt = tg->type;
+            const size_t rb = row_bytes(fmt, H);
+            buf.resize((size_t)2 * F * rb);
+            for (uint32_t r = 0; r < 2 * F; r++) {
+                const uint32_t g = r / 32, lane = r % 32;
+                const uint8_t *src = lane < 16 ? pg + (size_t)(16 * g + lane) * rb : pu + (size_t)(16 * g + lane - 16) * rb;
+                memcpy(buf.data() + (size_t)r * rb, src, rb);
+            }
+            if ((rc = make_mat(b, fmt, (int)(2 * F), (int)H, buf.data(), L.gateup))) return rc;
+        }
+        if ((rc = make_mat(b, td->type, (int)H, (int)F, pd, L.down))) return rc;
+        weight_bytes += L.qkv.bytes + L.o.bytes + L.gateup.bytes + L.down.bytes;
+        if (l == 0) I.body_format = tq->type;
+        // KV cache (KvCache::new(num_kv_heads*head_dim, max_seq_len, kv_quant), :593-597)
+        const size_t toks = (size_t)m->max_batch * m->max_seq;
+        if (m->bits_k == 0) {
+            NX_CUDA(b, malloc_tracked(m, &L.k_cache, toks * kv_dim));
+            NX_CUDA(b, malloc_tracked(m, &L.v_cache, toks * kv_dim));
+        } else {
+            m->bpt_k = ((size_t)kv_dim * m->bits_k + 7) / 8;
+            m->bpt_v = ((size_t)kv_dim * m->bits_v + 7) / 8;
+            NX_CUDA(b, malloc_tracked(m, &L.kp, toks * m->bpt_k + 16));
+            NX_CUDA(b, malloc_tracked(m, &L.vp, toks * m->bpt_v + 16));
+            NX_CUDA(b, malloc_tracked(m, &L.kmin, toks));
+            NX_CUDA(b, malloc_tracked(m, &L.kscale, toks));
+            NX_CUDA(b, malloc_tracked(m, &L.vmin, toks));
+            NX_CUDA(b, malloc_tracked(m, &L.vscale, toks));
+        }
+    }
+    I.weight_bytes = weight_bytes;
+
+    // RoPE table with the reference's f32 formula and the host libm
+    // (rope_single, src/kernel/mod.rs:259-263)
+    {
+        const size_t half = D / 2, npos = m->max_seq + 1;
+        std::vector<float> cs(npos * half), sn(npos * half);
+        for (size_t pos = 0; pos < npos; pos++)
+            for (size_t d = 0; d < half; d++) {
+                volatile float e = 2.0f * (float)d;
+                e = e / (float)D;
+                volatile float denom = powf(I.rope_freq_base, e);
+                float ang = (float)pos / denom;
+                cs[pos * half + d] = cosf(ang);
+                sn[pos * half + d] = sinf(ang);
+            }
+        NX_CUDA(b, malloc_tracked(m, &m->rope_cos, cs.size()));
+        NX_CUDA(b, malloc_tracked(m, &m->rope_sin, sn.size()));
+        NX_CUDA(b, cudaMemcpy(m->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+        NX_CUDA(b, cudaMemcpy(m->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+    }
+
+    // activations for up to kMaxChunk tokens per step
+    const int MC = kMaxChunk;
+    NX_CUDA(b, malloc_tracked(m, &m->hidden, (size_t)MC * H));
+    NX_CUDA(b, malloc_tracked(m, &m->q, (size_t)MC * qdim));
+    NX_CUDA(b, malloc_tracked(m, &m->attn, (size_t)MC * qdim));
+    NX_CUDA(b, malloc_tracked(m, &m->gated, (size_t)MC * F));
+    NX_CUDA(b, malloc_tracked(m, &m->kv_scratch, (size_t)MC * 2 * kv_dim));
+    NX_CUDA(b, malloc_tracked(m, &m->logits, (size_t)MC * I.vocab_rows));
+    const int G = (int)(Hq / Hkv);
+    int max_split = 1;
+    for (int mm = 1; mm <= MC; mm++) {
+        int s = (2 * 148 + (int)Hkv * mm - 1) / ((int)Hkv * mm);
+        s = std::max(1, std::min(s, 64));
+        s = std::min<int>(s, std::max<int>(1, (int)(m->max_seq / 16)));
+        m->nsplit[mm] = s;
+        max_split = std::max(max_split, s);
+    }
+    NX_CUDA(b, malloc_tracked(m, &m->part, (size_t)MC * Hkv * max_split * G * (D + 2)));
+    NX_CUDA(b, malloc_tracked(m, &m->counters, (size_t)MC * Hkv));
+    NX_CUDA(b, cudaMemset(m->counters, 0, (size_t)MC * Hkv * 4));
+    NX_CUDA(b, malloc_tracked(m, &m->seqs, MC));
+    NX_CUDA(b, malloc_tracked(m, &m->seq_ids, MC));
+    NX_CUDA(b, malloc_tracked(m, &m->out_tokens, MC));
+    NX_CUDA(b, cudaMemset(m->seqs, 0, MC * sizeof(DevSeq)));
+    NX_CUDA(b, cudaMemset(m->seq_ids, 0, MC * 4));
+    NX_CUDA(b, cudaHostAlloc((void **)&m->h_seqs, MC * sizeof(DevSeq), cudaHostAllocDefault));
+    NX_CUDA(b, cudaHostAlloc((void **)&m->h_seq_ids, MC * 4, cudaHostAllocDefault));
+    NX_CUDA(b, cudaHostAlloc((void **)&m->h_out_tokens, MC * 4, cudaHostAllocDefault));
+    NX_CUDA(b, cudaEventCreate(&m->ev0));
+    NX_CUDA(b, cudaEventCreate(&m->ev1));
+    m->seq_len.assign(m->max_batch, 0);
+    NX_CUDA(b, cudaDeviceSynchronize());
+    guard.release();
+    *out = m;
+    return NEXUS_OK;
+}
+
+// Optional per-kernel timing of enqueue_step (profile mode only, never in a graph).
+struct StepProfiler {
+    struct Rec {
+        std::string name;
+        double bytes = 0;
+        uint32_t launches = 0;
+        float ms = 0;
+        std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev;
+    };
+    std::vector<Rec> recs;
+    cudaStream_t st = nullptr;
+    cudaEvent_t cur = nullptr;
+    int idx(const char *name) {
+        for (size_t i = 0; i < recs.size(); i++)
+            if (recs[i].name == name) return (int)i;
+        recs.push_back(Rec());
+        recs.back().name = name;
+        return (int)recs.size() - 1;
+    }
+    void begin() {
+        cudaEventCreate(&cur);
+        cudaEventRecord(cur, st);
+    }
+    void end(const char *name, double bytes) {
+        cudaEvent_t e;
+        cudaEventCreate(&e);
+        cudaEventRecord(e, st);
+        Rec &r = recs[idx(name)];
+        r.ev.push_back({cur, e});
+        r.bytes = bytes;
+        r.launches++;
+    }
+    void collect() {
+        for (auto &r : recs) {
+            for (auto &pr : r.ev) {
+                float ms = 0;
+                cudaEventSynchronize(pr.second);
+                cudaEventElapsedTime(&ms, pr.first, pr.second);
+                r.ms += ms;
+                cudaEventDestroy(pr.first);
+                cudaEventDestroy(pr.second);
+            }
+            r.ev.clear();
+        }
+    }
+};
+
+static double gemv_bytes(const Mat &w, int mc, int k, int n_out) {
+    return (double)w.bytes + 4.0 * mc * k + 4.0 * mc * n_out;
+}
+
+// Enqueue one fused decode step for `mc` tokens whose DevSeq entries are on the device.
+static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof = nullptr) {
+    const nexus_cuda_model_info &I = m->info;
+    cudaStream_t st = m->b->stream;
+    const int H = (int)I.hidden_size, D = (int)I.head_dim, F = (int)I.ff_dim;
+    const int Hq = (int)I.num_heads, Hkv = (int)I.num_kv_heads, kv_dim = Hkv * D, qdim = Hq * D;
+    const int pdl = m->use_pdl ? 1 : 0;
+    cudaError_t e;
+    EmbedParams ep = {};
+    ep.fmt = m->embd_fmt;
+    ep.m = mc;
+    ep.hidden = H;
+    ep.vocab_rows = m->embd_rows;
+    ep.table = m->embd;
+    ep.out = m->hidden;
+    ep.seqs = m->seqs;
+    ep.pdl = 0;  // first kernel of the step: plain stream order after the host copies
+    if (prof) prof->begin();
+    if ((e = launch_embed(ep, st)) != cudaSuccess) return e;
+    if (prof) prof->end("embed", (double)format_bytes(m->embd_fmt, (size_t)H) * mc + 4.0 * mc * H);
+    const bool packed = m->bits_k > 0;
+    for (uint32_t l = 0; l < I.num_layers; l++) {
+        Layer &L = m->layers[l];
+        GemvParams g = {};
+        g.m = mc;
+        g.pdl = pdl;
+        g.eps = I.rms_norm_eps;
+        // attn_norm -> fused Q|K|V -> RoPE -> KV write
+        g.fmt = L.qkv.fmt;
+        g.w_main = L.qkv.main;
+        g.w_aux = L.qkv.aux;
+        g.n = L.qkv.n;
+        g.k = H;
+        g.x = m->hidden;
+        g.x_stride = H;
+        g.norm_w = L.attn_norm;
+        g.epi = EPI_QKV;
+        g.qkv.hq = Hq;
+        g.qkv.hkv = Hkv;
+        g.qkv.head_dim = D;
+        g.qkv.q_out = m->q;
+        g.qkv.rope_cos = m->rope_cos;
+        g.qkv.rope_sin = m->rope_sin;
+        g.qkv.k_cache = L.k_cache;
+        g.qkv.v_cache = L.v_cache;
+        g.qkv.seq_stride = (size_t)m->max_seq * kv_dim;
+        g.qkv.kv_scratch = packed ? m->kv_scratch : nullptr;
+        g.qkv.seqs = m->seqs;
+        g.qkv.seq_ids = m->seq_ids;
+        if (prof) prof->begin();
+        if ((e = launch_gemv(g, st)) != cudaSuccess) return e;
+        if (prof) prof->end("qkv", gemv_bytes(L.qkv, mc, H, qdim + 2 * kv_dim) + 4.0 * H);
+        if (packed) {
+            KvPackParams kp = {};
+            kp.m = mc;
+            kp.kv_dim = kv_dim;
+            kp.bits_k = (int)m->bits_k;
+            kp.bits_v = (int)m->bits_v;
+            kp.kv_scratch = m->kv_scratch;
+            kp.kp_data = L.kp;
+            kp.vp_data = L.vp;
+            kp.kp_min = L.kmin;
+            kp.kp_scale = L.kscale;
+            kp.vp_min = L.vmin;
+            kp.vp_scale = L.vscale;
+            kp.pk_bpt_k = m->bpt_k;
+            kp.pk_bpt_v = m->bpt_v;
+            kp.pk_seq_stride_k = m->bpt_k * m->max_seq;
+            kp.pk_seq_stride_v = m->bpt_v * m->max_seq;
+            kp.pk_seq_tokens = m->max_seq;
+            kp.seqs = m->seqs;
+            kp.seq_ids = m->seq_ids;
+            kp.pdl = pdl;
+            if (prof) prof->begin();
+        if ((e = launch_kv_pack(kp, st)) != cudaSuccess) return e;
+        if (prof) prof->end("kv_pack", (double)mc * (8.0 * kv_dim + m->bpt_k + m->bpt_v + 16));
+        }
+        double attn_bytes = 0;
+        if (prof) {
+            for (int t = 0; t < mc; t++) {
+                const double ctx = (double)m->h_seqs[t].seq_len;
+                attn_bytes += packed ? ctx * (m->bpt_k + m->bpt_v + 16.0) : ctx * 8.0 * kv_dim;
+                attn_bytes += 8.0 * qdim;
+            }
+        }
+        AttnParams a = {};
+        a.hq = Hq;
+        a.hkv = Hkv;
+        a.head_dim = D;
+        a.m = mc;
+        a.q = m->q;
+        a.out = m->attn;
+        a.scale = 1.0f / sqrtf((float)D);
+        a.k_cache = L.k_cache;
+        a.v_cache = L.v_cache;
+        a.seq_stride = (size_t)m->max_seq * kv_dim;
+        a.bits_k = (int)m->bits_k;
+        a.bits_v = (int)m->bits_v;
+        a.kp_data = L.kp;
+        a.vp_data = L.vp;
+        a.kp_min = L.kmin;
+        a.kp_scale = L.kscale;
+        a.vp_min = L.vmin;
+        a.vp_scale = L.vscale;
+        a.pk_bpt_k = m->bpt_k;
+        a.pk_bpt_v = m->bpt_v;
+        a.pk_seq_stride_k = m->bpt_k * m->max_seq;
+        a.pk_seq_stride_v = m->bpt_v * m->max_seq;
+        a.pk_seq_tokens = m->max_seq;
+        a.seqs = m->seqs;
+        a.seq_ids = m->seq_ids;
+        a.kv_dim = kv_dim;
+        a.nsplit = m->nsplit[mc];
+        a.part = m->part;
+        a.counters = m->counters;
+        a.pdl = pdl;
+        if (prof) prof->begin();
+        if ((e = launch_attention(a, st)) != cudaSuccess) return e;
+        if (prof) prof->end("attention", attn_bytes);
+        // o_proj + residual
+        GemvParams o = {};
+        o.m = mc;
+        o.pdl = pdl;
+        o.fmt = L.o.fmt;
+        o.w_main = L.o.main;
+        o.w_aux = L.o.aux;
+        o.n = H;
+        o.k = qdim;
+        o.x = m->attn;
+        o.x_stride = qdim;
+        o.epi = EPI_ADD;
+        o.y = m->hidden;
+        o.y_stride = H;
+        if (prof) prof->begin();
+        if ((e = launch_gemv(o, st)) != cudaSuccess) return e;
+        if (prof) prof->end("o_proj", gemv_bytes(L.o, mc, qdim, H) + 4.0 * mc * H);
+        // ffn_norm -> gate/up -> SwiGLU
+        GemvParams gu = {};
+        gu.m = mc;
+        gu.pdl = pdl;
+        gu.eps = I.rms_norm_eps;
+        gu.fmt = L.gateup.fmt;
+        gu.w_main = L.gateup.main;
+        gu.w_aux = L.gateup.aux;
+        gu.n = 2 * F;
+        gu.k = H;
+        gu.x = m->hidden;
+        gu.x_stride = H;
+        gu.norm_w = L.ffn_norm;
+        gu.epi = EPI_SWIGLU;
+        gu.y = m->gated;
+        gu.y_stride = F;
+        if (prof) prof->begin();
+        if ((e = launch_gemv(gu, st)) != cudaSuccess) return e;
+        if (prof) prof->end("gate_up", gemv_bytes(L.gateup, mc, H, F) + 4.0 * H);
+        // down + residual
+        GemvParams dn = {};
+        dn.m = mc;
+        dn.pdl = pdl;
+        dn.fmt = L.down.fmt;
+        dn.w_main = L.down.main;
+        dn.w_aux = L.down.aux;
+        dn.n = H;
+        dn.k = F;
+        dn.x = m->gated;
+        dn.x_stride = F;
+        dn.epi = EPI_ADD;
+        dn.y = m->hidden;
+        dn.y_stride = H;
+        if (prof) prof->begin();
+        if ((e = launch_gemv(dn, st)) != cudaSuccess) return e;
+        if (prof) prof->end("down", gemv_bytes(L.down, mc, F, H) + 4.0 * mc * H);
+    }
+    // transformer_logits: output norm + head + greedy argmax
+    if (m->has_head) {
+        GemvParams hd = {};
+        hd.m = mc;
+        hd.pdl = pdl;
+        hd.eps = I.rms_norm_eps;
+        hd.fmt = m->head.fmt;
+        hd.w_main = m->head.main;
+        hd.w_aux = m->head.aux;
+        hd.n = m->head.n;
+        hd.k = H;
+        hd.x = m->hidden;
+        hd.x_stride = H;
+        hd.norm_w = m->out_norm;
+        hd.epi = EPI_ARGMAX;
+        hd.y = m->logits;
+        hd.y_stride = (int)I.vocab_rows;
+        hd.seqs = m->seqs;
+        if (prof) prof->begin();
+        if ((e = launch_gemv(hd, st)) != cudaSuccess) return e;
+        if (prof) prof->end("head", gemv_bytes(m->head, mc, H, (int)I.vocab_rows) + 4.0 * H);
+    } else {
+        if ((e = launch_rms_norm(m->hidden, m->out_norm, m->logits, mc, H, I.rms_norm_eps, st)) != cudaSuccess) return e;
+        for (int t = 0; t < mc; t++) {
+            // k_argmax accumulates into best (cleared by the embedding kernel)
+            if ((e = launch_argmax(m->logits + (size_t)t * H, H, &m->seqs[t].best, st)) != cudaSuccess) return e;
+        }
+    }
+    if (prof) prof->begin();
+    e = launch_advance(m->seqs, mc, m->out_tokens, m->has_head ? pdl : 0, st);
+    if (prof) prof->end("advance", 64.0 * mc);
+    return e;
+}
+
+static int run_step(nexus_cuda_model *m, int mc) {
+    nexus_cuda_backend *b = m->b;
+    cudaStream_t st = b->stream;
+    if (m->use_graph && m->has_head) {
+        if (!m->graph[mc]) {
+            cudaGraph_t g = nullptr;
+            NX_CUDA(b, cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+            cudaError_t e = enqueue_step(m, mc);
+            cudaError_t e2 = cudaStreamEndCapture(st, &g);
+            if (e != cudaSuccess || e2 != cudaSuccess) {
+                if (g) cudaGraphDestroy(g);
+                return set_err(b, NEXUS_E_CUDA, std::string("graph capture: ") +
+                                                   cudaGetErrorString(e != cudaSuccess ? e : e2));
+            }
+            e = cudaGraphInstantiate(&m->graph[mc], g, 0);
+            cudaGraphDestroy(g);
+            if (e != cudaSuccess) {
+                m->graph[mc] = nullptr;
+                return set_err(b, NEXUS_E_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+            }
+        }
+        NX_CUDA(b, cudaGraphLaunch(m->graph[mc], st));
+    } else {
+        NX_CUDA(b, enqueue_step(m, mc));
+    }
+    return NEXUS_OK;
+}
+
+// Host-driven step over `items` (at most kMaxChunk), results to host.
+struct StepItem {
+    uint32_t sid, token, position, slot;
+};
+
+static int host_step(nexus_cuda_model *m, const StepItem *items, int mc, float *logits_out, int logits_last_only,
+                     uint32_t *tokens_out) {
+    nexus_cuda_backend *b = m->b;
+    cudaStream_t st = b->stream;
+    for (int t = 0; t < mc; t++) {
+        DevSeq s = {};
+        s.token = items[t].token;
+        s.position = items[t].position;
+        s.slot = items[t].slot;
+        s.seq_len = items[t].slot + 1;
+        m->h_seqs[t] = s;
+        m->h_seq_ids[t] = items[t].sid;
+    }
+    NX_CUDA(b, cudaMemcpyAsync(m->seqs, m->h_seqs, mc * sizeof(DevSeq), cudaMemcpyHostToDevice, st));
+    NX_CUDA(b, cudaMemcpyAsync(m->seq_ids, m->h_seq_ids, mc * 4, cudaMemcpyHostToDevice, st));
+    int rc = run_step(m, mc);
+    if (rc) return rc;
+    const size_t V = m->info.vocab_rows;
+    if (logits_out) {
+        if (logits_last_only)
+            NX_CUDA(b, cudaMemcpyAsync(logits_out, m->logits + (size_t)(mc - 1) * V, V * 4, cudaMemcpyDeviceToHost, st));
+        else
+            NX_CUDA(b, cudaMemcpyAsync(logits_out, m->logits, (size_t)mc * V * 4, cudaMemcpyDeviceToHost, st));
+    }
+    NX_CUDA(b, cudaMemcpyAsync(m->h_out_tokens, m->out_tokens, mc * 4, cudaMemcpyDeviceToHost, st));
+    NX_CUDA(b, cudaStreamSynchronize(st));
+    if (tokens_out) memcpy(tokens_out, m->h_out_tokens, mc * 4);
+    return NEXUS_OK;
+}
+
+extern "C" int nexus_cuda_model_load(nexus_cuda_backend *b, const char *gguf_path, nexus_cuda_model **out) {
+    if (!b || !gguf_path || !out) return set_err(b, NEXUS_E_INVALID, "NULL argument");
+    *out = nullptr;
+    std::lock_guard<std::mutex> lk(b->mu);
+    cudaSetDevice(b->device);
+    return model_load(b, gguf_path, out);
+}
+
+extern "C" int nexus_cuda_model_free(nexus_cuda_model *m) {
+    model_release(m);
+    return NEXUS_OK;
+}
+
+extern "C" int nexus_cuda_model_get_info(const nexus_cuda_model *m, nexus_cuda_model_info *info) {
+    if (!m || !info) return NEXUS_E_INVALID;
+    *info = m->info;
+    return NEXUS_OK;
+}
+
+extern "C" int nexus_cuda_seq_reset(nexus_cuda_model *m, uint32_t seq_id) {
+    if (!m || seq_id >= m->max_batch) return set_err(m ? m->b : nullptr, NEXUS_E_INVALID, "bad sequence id");
+    m->seq_len[seq_id] = 0;
+    return NEXUS_OK;
+}
+
+extern "C" int nexus_cuda_seq_len(nexus_cuda_model *m, uint32_t seq_id, uint32_t *len) {
+    if (!m || !len || seq_id >= m->max_batch) return set_err(m ? m->b : nullptr, NEXUS_E_INVALID, "bad sequence id");
+    *len = m->seq_len[seq_id];
+    return NEXUS_OK;
+}
+
+static int check_slot(nexus_cuda_model *m, uint32_t sid, uint32_t add) {
+    if (sid >= m->max_batch) return set_err(m->b, NEXUS_E_INVALID, "bad sequence id");
+    if ((uint64_t)m->seq_len[sid] + add > m->max_seq)
+        return set_err(m->b, NEXUS_E_INVALID, "KV cache full: the backend does not shift the cache (raise max_seq_len)");
+    return NEXUS_OK;
+}
+
+static int check_position(nexus_cuda_model *m, uint64_t position) {
+    if (position > m->max_seq) return set_err(m->b, NEXUS_E_INVALID, "position beyond the RoPE table (max_seq_len)");
+    return NEXUS_OK;
+}
+
+extern "C" int nexus_cuda_decode(nexus_cuda_model *m, uint32_t seq_id, uint32_t token, uint32_t position,
+                                 float *logits, uint32_t *argmax) {
+    if (!m) return set_err(nullptr, NEXUS_E_INVALID, "model is NULL");
+    std::lock_guard<std::mutex> lk(m->b->mu);
+    cudaSetDevice(m->b->device);
+    int rc = check_slot(m, seq_id, 1);
+    if (!rc) rc = check_position(m, position);
+    if (rc) return rc;
+    StepItem it = {seq_id, token, position, m->seq_len[seq_id]};
+    NX_CUDA(m->b, cudaEventRecord(m->ev0, m->b->stream));
+    uint32_t tok = 0;
+    rc = host_step(m, &it, 1, logits, 1, &tok);
+    if (rc) return rc;
+    cudaEventRecord(m->ev1, m->b->stream);
+    cudaEventSynchronize(m->ev1);
+    cudaEventElapsedTime(&m->last_ms, m->ev0, m->ev1);
+    m->seq_len[seq_id] += 1;
+    if (argmax) *argmax = tok;
+    return NEXUS_OK;
+}
+
+static int prefill_impl(nexus_cuda_model *m, uint32_t seq_id, const uint32_t *tokens, size_t n, float *logits,
+                        uint32_t *argmax) {
+    m->seq_len[seq_id] = 0;
+    if (n == 0) return NEXUS_OK;
+    int rc = check_slot(m, seq_id, (uint32_t)std::min<size_t>(n, 0xffffffffu));
+    if (!rc) rc = check_position(m, n - 1);
+    if (rc) return rc;
+    NX_CUDA(m->b, cudaEventRecord(m->ev0, m->b->stream));
+    size_t p = 0;
+    uint32_t last = 0;
+    while (p < n) {
+        int mc = n - p >= 4 ? 4 : n - p >= 2 ? 2 : 1;
+        StepItem it[kMaxChunk];
+        for (int j = 0; j < mc; j++) it[j] = {seq_id, tokens[p + j], (uint32_t)(p + j), (uint32_t)(p + j)};
+        const bool final = p + mc == n;
+        uint32_t toks[kMaxChunk];
+        rc = host_step(m, it, mc, final ? logits : nullptr, 1, toks);
+        if (rc) return rc;
+        last = toks[mc - 1];
+        p += mc;
+        m->seq_len[seq_id] = (uint32_t)p;
+    }
+    cudaEventRecord(m->ev1, m->b->stream);
+    cudaEventSynchronize(m->ev1);
+    cudaEventElapsedTime(&m->last_ms, m->ev0, m->ev1);
+    if (argmax) *argmax = last;
+    return NEXUS_OK;
+}
+
+extern "C" int nexus_cuda_prefill(nexus_cuda_model *m, uint32_t seq_id, const uint32_t *tokens, size_t n,
+                                  float *logits, uint32_t *argmax) {
+    if (!m || (n && !tokens)) return set_err(m ? m->b : nullptr, NEXUS_E_INVALID, "NULL argument");
+    if (seq_id >= m->max_batch) return set_err(m->b, NEXUS_E_INVALID, "bad sequence id");
+    std::lock_guard<std::mutex> lk(m->b->mu);
+    cudaSetDevice(m->b->device);
+    return prefill_impl(m, seq_id, tokens, n, logits, argmax);
+}
+
+extern "C" int nexus_cuda_generate(nexus_cuda_model *m, uint32_t seq_id, const uint32_t *prompt, size_t n,
+                                   size_t max_tokens, uint32_t *out) {
+    if (!m || !out || (n && !prompt)) return set_err(m ? m->b : nullptr, NEXUS_E_INVALID, "NULL argument");
+    if (seq_id >= m->max_batch) return set_err(m->b, NEXUS_E_INVALID, "bad sequence id");
+    std::lock_guard<std::mutex> lk(m->b->mu);
+    cudaSetDevice(m->b->device);
+    nexus_cuda_backend *b = m->b;
+    memcpy(out, prompt, n * 4);
+    uint32_t next = 0;
+    int rc = prefill_impl(m, seq_id, prompt, n, nullptr, &next);
+    if (rc) return rc;
+    if (max_tokens == 0) return NEXUS_OK;
+    rc = check_slot(m, seq_id, (uint32_t)max_tokens);
+    if (!rc) rc = check_position(m, n + max_tokens - 1);
+    if (rc) return rc;
+    // sample_token on empty logits returns 0 (src/engine/mod.rs:825-827)
+    if (n == 0) next = 0;
+    // Device-chained greedy loop: each graph replay decodes one token and the
+    // closing kernel feeds its argmax into the next replay.
+    DevSeq s = {};
+    s.token = next;
+    s.position = (uint32_t)n;
+    s.slot = m->seq_len[seq_id];
+    s.seq_len = s.slot + 1;
+    m->h_seqs[0] = s;
+    m->h_seq_ids[0] = seq_id;
+    cudaStream_t st = b->stream;
+    NX_CUDA(b, cudaMemcpyAsync(m->seqs, m->h_seqs, sizeof(DevSeq), cudaMemcpyHostToDevice, st));
+    NX_CUDA(b, cudaMemcpyAsync(m->seq_ids, m->h_seq_ids, 4, cudaMemcpyHostToDevice, st));
+    uint32_t *ring = nullptr;
+    NX_CUDA(b, dalloc(&ring, max_tokens));
+    out[n] = next;
+    NX_CUDA(b, cudaEventRecord(m->ev0, st));
+    for (size_t i = 0; i < max_tokens; i++) {
+        rc = run_step(m, 1);
+        if (rc) break;
+        // out_tokens[0] is the token the next step consumes
+        if (cudaMemcpyAsync(ring + i, m->out_tokens, 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess) {
+            rc = set_err(b, NEXUS_E_CUDA, "ring copy failed");
+            break;
+        }
+    }
+    cudaEventRecord(m->ev1, st);
+    if (!rc && max_tokens > 1)
+        rc = cudaMemcpyAsync(out + n + 1, ring, (max_tokens - 1) * 4, cudaMemcpyDeviceToHost, st) == cudaSuccess
+                 ? NEXUS_OK
+                 : set_err(b, NEXUS_E_CUDA, "token copy failed");
+    cudaError_t e = cudaStreamSynchronize(st);
+    cudaEventElapsedTime(&m->last_ms, m->ev0, m->ev1);
+    cudaFree(ring);
+    if (rc) return rc;
+    if (e != cudaSuccess) return set_err(b, NEXUS_E_CUDA, cudaGetErrorString(e));
+    m->seq_len[seq_id] += (uint32_t)max_tokens;
+    return NEXUS_OK;
+}
+
+extern "C" int nexus_cuda_decode_batch(nexus_cuda_model *m, const nexus_decode_item *items, size_t n,
+                                       uint32_t *out_tokens, float *out_logits) {
+    if (!m || (n && !items)) return set_err(m ? m->b : nullptr, NEXUS_E_INVALID, "NULL argument");
+    std::lock_guard<std::mutex> lk(m->b->mu);
+    cudaSetDevice(m->b->device);
+    std::vector<bool> seen(m->max_batch, false);
+    for (size_t i = 0; i < n; i++) {
+        const uint32_t sid = items[i].seq_id;
+        int rc = check_slot(m, sid, 1);
+        if (!rc) rc = check_position(m, items[i].position);
+        if (rc) return rc;
+        if (seen[sid]) return set_err(m->b, NEXUS_E_INVALID, "a sequence appears twice in one decode batch");
+        seen[sid] = true;
+        if (items[i].page_ids && items[i].n_pages) {
+            // pages are the library's own per-sequence ranges; a caller-provided
+            // table must cover the slot being written
+            const uint32_t pt = m->b->cfg.page_tokens ? m->b->cfg.page_tokens : 16;
+            if ((uint64_t)items[i].n_pages * pt < (uint64_t)m->seq_len[sid] + 1)
+                return set_err(m->b, NEXUS_E_INVALID, "page list shorter than the sequence");
+        }
+    }
+    NX_CUDA(m->b, cudaEventRecord(m->ev0, m->b->stream));
+    const size_t V = m->info.vocab_rows;
+    for (size_t p = 0; p < n;) {
+        int mc = n - p >= 4 ? 4 : n - p >= 2 ? 2 : 1;
+        StepItem it[kMaxChunk];
+        for (int j = 0; j < mc; j++) {
+            const nexus_decode_item &d = items[p + j];
+            it[j] = {d.seq_id, d.token, d.position, m->seq_len[d.seq_id]};
+        }
+        int rc = host_step(m, it, mc, out_logits ? out_logits + p * V : nullptr, 0, out_tokens ? out_tokens + p : nullptr);
+        if (rc) return rc;
+        for (int j = 0; j < mc; j++) m->seq_len[items[p + j].seq_id] += 1;
+        p += mc;
+    }
+    cudaEventRecord(m->ev1, m->b->stream);
+    cudaEventSynchronize(m->ev1);
+    cudaEventElapsedTime(&m->last_ms, m->ev0, m->ev1);
+    return NEXUS_OK;
+}
+
+extern "C" int nexus_cuda_last_step_ms(const nexus_cuda_model *m, float *ms) {
+    if (!m || !ms) return NEXUS_E_INVALID;
+    *ms = m->last_ms;
+    return NEXUS_OK;
+}
+
+extern "C" int nexus_cuda_profile_decode(nexus_cuda_model *m, uint32_t seq_id, uint32_t token, uint32_t steps,
+                                         nexus_kernel_profile *out, int max_out, int *n_out) {
+    if (!m || !out || !n_out) return set_err(m ? m->b : nullptr, NEXUS_E_INVALID, "NULL argument");
+    std::lock_guard<std::mutex> lk(m->b->mu);
+    cudaSetDevice(m->b->device);
+    int rc = check_slot(m, seq_id, steps);
+    if (!rc) rc = check_position(m, (uint64_t)m->seq_len[seq_id] + steps);
+    if (rc) return rc;
+    nexus_cuda_backend *b = m->b;
+    cudaStream_t st = b->stream;
+    StepProfiler prof;
+    prof.st = st;
+    uint32_t tok = token;
+    for (uint32_t i = 0; i < steps; i++) {
+        const uint32_t slot = m->seq_len[seq_id];
+        DevSeq s = {};
+        s.token = tok;
+        s.position = slot;
+        s.slot = slot;
+        s.seq_len = slot + 1;
+        m->h_seqs[0] = s;
+        m->h_seq_ids[0] = seq_id;
+        NX_CUDA(b, cudaMemcpyAsync(m->seqs, m->h_seqs, sizeof(DevSeq), cudaMemcpyHostToDevice, st));
+        NX_CUDA(b, cudaMemcpyAsync(m->seq_ids, m->h_seq_ids, 4, cudaMemcpyHostToDevice, st));
+        NX_CUDA(b, enqueue_step(m, 1, &prof));
+        NX_CUDA(b, cudaMemcpyAsync(m->h_out_tokens, m->out_tokens, 4, cudaMemcpyDeviceToHost, st));
+        NX_CUDA(b, cudaStreamSynchronize(st));
+        tok = m->h_out_tokens[0];
+        m->seq_len[seq_id] += 1;
+    }
+    prof.collect();
+    int n = 0;
+    for (auto &r : prof.recs) {
+        if (n >= max_out) break;
+        memset(&out[n], 0, sizeof(out[n]));
+        strncpy(out[n].name, r.name.c_str(), sizeof(out[n].name) - 1);
+        out[n].launches = r.launches;
+        out[n].total_ms = r.ms;
+        out[n].bytes_per_launch = r.bytes;
+        n++;
+    }
+    *n_out = n;
+    return NEXUS_OK;
+}
+
+extern "C" int nexus_synth_model_write(const char *path, const nexus_synth_config *cfg) {
+    if (!path || !cfg) return set_err(nullptr, NEXUS_E_INVALID, "NULL argument");
+    std::string err;
+    int rc = nx::synth_model_write(path, cfg, err);
+    if (rc) set_err(nullptr, rc, err);
+    return rc;
+}

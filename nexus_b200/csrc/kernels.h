@@ -1,0 +1,134 @@
+// kernels.h -- launch interfaces of the sm_100a kernels (host side).
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace nx {
+
+// ---- kernels_quant.cu (bit-exact, -fmad=false) ----
+cudaError_t launch_dequant_raw(int fmt, const uint8_t *blocks, size_t n, float *out, cudaStream_t st);
+cudaError_t launch_quantize(int fmt, const float *x, size_t n, uint8_t *out, cudaStream_t st);
+cudaError_t launch_repack_tiles(int fmt, const uint8_t *raw, int n, int k, uint4 *main, uint32_t *aux,
+                                cudaStream_t st);
+cudaError_t launch_dequant_tiles(int fmt, const uint4 *main, const uint32_t *aux, int n, int k, float *out,
+                                 cudaStream_t st);
+
+// ---- kernels_gemv.cu ----
+enum GemvEpilogue : int {
+    EPI_STORE = 0,   // y[t][row] = dot
+    EPI_ADD = 1,     // y[t][row] += dot            (residual add)
+    EPI_SWIGLU = 2,  // tile rows: 16 gate rows then 16 up rows per group -> y[t][i] = silu(g)*u
+    EPI_QKV = 3,     // fused Q|K|V with RoPE; K,V written to the KV destination
+    EPI_ARGMAX = 4   // logits (optional) + greedy argmax via a packed 64-bit atomic max
+};
+
+// Per-step values read by the kernels on the device (so one captured graph
+// serves every decode step).  One entry per sequence in the batch.
+struct DevSeq {
+    uint32_t token;         // input token of this step
+    uint32_t position;      // RoPE position (the token's index in the sequence)
+    uint32_t slot;          // KV slot written this step (= cached tokens before it)
+    uint32_t seq_len;       // tokens attended over (= slot + 1)
+    unsigned long long best;  // packed argmax accumulator of the head
+};
+
+struct QkvEpilogue {
+    int hq, hkv, head_dim;      // heads and dims (head_dim/2 a multiple of 16)
+    float *q_out;               // [m][hq*head_dim]
+    const float *rope_cos;      // [max_pos][head_dim/2] host-computed table
+    const float *rope_sin;
+    // KV destinations: float cache [seq][max_seq][kv_dim] (k_cache/v_cache) or,
+    // when kv_scratch is set, the new K/V rows go to kv_scratch[m][2][kv_dim]
+    float *k_cache, *v_cache;
+    size_t seq_stride;          // floats between sequences in k_cache/v_cache
+    float *kv_scratch;
+    const DevSeq *seqs;         // [m]
+    const uint32_t *seq_ids;    // [m] cache row of each batch entry
+};
+
+struct GemvParams {
+    int fmt;
+    const uint4 *w_main;
+    const uint32_t *w_aux;
+    int n;        // valid output rows of the tile matrix
+    int k;        // input columns (multiple of 256)
+    int m;        // tokens
+    const float *x;     // [m][x_stride]
+    int x_stride;
+    const float *norm_w;  // fused RMSNorm weights (nullptr = none)
+    float eps;
+    int epi;
+    float *y;           // [m][y_stride]
+    int y_stride;
+    QkvEpilogue qkv;
+    DevSeq *seqs;       // EPI_ARGMAX: best accumulators per token
+    int pdl;            // 1: launched with programmatic stream serialization
+};
+
+cudaError_t launch_gemv(const GemvParams &p, cudaStream_t st);
+
+// ---- kernels_attn.cu ----
+struct AttnParams {
+    int hq, hkv, head_dim, m;
+    const float *q;          // [m][hq*head_dim]
+    float *out;              // [m][hq*head_dim]
+    float scale;             // 1/sqrt(head_dim)
+    // float cache
+    const float *k_cache, *v_cache;
+    size_t seq_stride;       // floats between sequences
+    // packed cache (bits_k > 0): per sequence, per token bytes + mins + scales
+    int bits_k, bits_v;
+    const uint8_t *kp_data, *vp_data;
+    const float *kp_min, *kp_scale, *vp_min, *vp_scale;
+    size_t pk_bpt_k, pk_bpt_v;     // bytes per token
+    size_t pk_seq_stride_k, pk_seq_stride_v;  // bytes between sequences
+    size_t pk_seq_tokens;    // tokens between sequences in min/scale arrays
+    const DevSeq *seqs;
+    const uint32_t *seq_ids;
+    int kv_dim;
+    int nsplit;              // splits of the context per (sequence, kv head)
+    float *part;             // scratch [m][hkv][nsplit][G][head_dim + 2]
+    unsigned *counters;      // [m][hkv], zero on entry, left zero on exit
+    int pdl;
+};
+cudaError_t launch_attention(const AttnParams &p, cudaStream_t st);
+
+// packed KV append (PackedKvBuffer::add, src/engine/mod.rs:209-232) for m tokens
+struct KvPackParams {
+    int m, kv_dim, bits_k, bits_v;
+    const float *kv_scratch;      // [m][2][kv_dim]
+    uint8_t *kp_data, *vp_data;
+    float *kp_min, *kp_scale, *vp_min, *vp_scale;
+    size_t pk_bpt_k, pk_bpt_v, pk_seq_stride_k, pk_seq_stride_v, pk_seq_tokens;
+    const DevSeq *seqs;
+    const uint32_t *seq_ids;
+    int pdl;
+};
+cudaError_t launch_kv_pack(const KvPackParams &p, cudaStream_t st);
+// device-chained decode: next token = argmax, positions advance by one
+cudaError_t launch_advance(DevSeq *seqs, int m, uint32_t *out_tokens, int pdl, cudaStream_t st);
+
+// ---- kernels_misc.cu ----
+// embedding row gather with bit-exact dequantization; also resets seqs[t].best
+struct EmbedParams {
+    int fmt, m, hidden;
+    size_t vocab_rows;
+    const uint8_t *table;   // raw GGUF blocks
+    float *out;             // [m][hidden]
+    DevSeq *seqs;
+    int pdl;
+};
+cudaError_t launch_embed(const EmbedParams &p, cudaStream_t st);
+
+cudaError_t launch_rms_norm(const float *x, const float *w, float *out, int rows, int n, float eps, cudaStream_t st);
+cudaError_t launch_layer_norm(const float *x, const float *w, const float *b, float *out, int rows, int n,
+                              float eps, cudaStream_t st);
+cudaError_t launch_softmax(const float *x, float *out, int rows, int n, cudaStream_t st);
+cudaError_t launch_binary(int op, const float *a, const float *b, float *out, size_t n, cudaStream_t st);
+cudaError_t launch_matmul_f32(const float *a, const float *b, float *c, int m, int n, int k, int transpose_b,
+                              cudaStream_t st);
+cudaError_t launch_rope(float *x, int heads, int head_dim, int position, float base, cudaStream_t st);
+cudaError_t launch_argmax(const float *x, size_t n, unsigned long long *best, cudaStream_t st);
+
+}  // namespace nx

@@ -1,0 +1,142 @@
+"""Decode-step parity on the GPU through the C ABI, against the CPU oracle.
+
+Bars (north star): logits within 2e-3 max-abs, greedy token sequences
+identical, KV cache lengths equal.  The tiny configuration (4 layers,
+hidden 256, all Q4_K) runs in full: 128-token prompt (seed 1) + 64 greedy
+tokens.  The 8B shape is checked on a short prompt.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 2e-3
+
+
+@pytest.fixture(scope="module")
+def tiny_engine(nb, tiny_path):
+    b = nb.CudaBackend(device=0, max_batch=4)
+    e = nb.InferenceEngine(b)
+    e.load_model(tiny_path)
+    yield e
+    e.close()
+    b.close()
+
+
+def prompt(seed, n, vocab):
+    return np.random.default_rng(seed).integers(0, vocab, n).tolist()
+
+
+def test_tiny_info(tiny_engine):
+    i = tiny_engine.info
+    assert (i.num_layers, i.hidden_size, i.num_heads, i.num_kv_heads, i.head_dim) == (4, 256, 8, 4, 32)
+    assert i.vocab_rows == 4096 and i.rope_freq_base == 10000.0
+
+
+def test_tiny_prefill_and_decode_logits(tiny_engine, oracle, tiny_path):
+    m = oracle.Model(tiny_path)
+    p = prompt(1, 128, 4096)
+    ref = m.prefill(p)
+    got, tok = tiny_engine.prefill(p)
+    assert np.max(np.abs(got - ref)) < LOGIT_TOL
+    assert tok == oracle.greedy(ref)
+    assert tiny_engine.seq_len() == 128
+    for i in range(5):
+        t = oracle.greedy(ref)
+        ref = m.decode(t, 128 + i)
+        got, tok = tiny_engine.decode_with_cache(t, 128 + i)
+        assert np.max(np.abs(got - ref)) < LOGIT_TOL
+        assert tok == oracle.greedy(ref)
+
+
+def test_tiny_generate_token_identical(tiny_engine, oracle, tiny_path):
+    """Config 1 in full: 128-token random prompt (seed 1), 64 greedy tokens."""
+    m = oracle.Model(tiny_path)
+    p = prompt(1, 128, 4096)
+    ref = m.generate(p, 64)
+    got = tiny_engine.generate(p, 64)
+    assert got == ref
+    assert tiny_engine.seq_len() == m.seq_len(0) == 192
+
+
+def test_tiny_single_token_steps_match_chunked_prefill(tiny_engine):
+    p = prompt(7, 11, 4096)
+    a, ta = tiny_engine.prefill(p)
+    tiny_engine.prefill(p[:1])
+    for i, t in enumerate(p[1:], start=1):
+        b, tb = tiny_engine.decode_with_cache(t, i)
+    assert np.max(np.abs(a - b)) < 1e-4 and ta == tb
+
+
+def test_tiny_decode_batch_matches_single(tiny_engine, oracle, tiny_path):
+    seqs = [prompt(100 + s, 9 + s, 4096) for s in range(3)]
+    refs = []
+    for s, p in enumerate(seqs):
+        m = oracle.Model(tiny_path)
+        l0 = m.prefill(p)
+        t = oracle.greedy(l0)
+        refs.append((t, m.decode(t, len(p))))
+        tiny_engine.prefill(p, seq_id=s)
+    items = [(s, refs[s][0], len(seqs[s])) for s in range(3)]
+    toks, logits = tiny_engine.decode_batch(items, want_logits=True)
+    for s in range(3):
+        assert np.max(np.abs(logits[s] - refs[s][1])) < LOGIT_TOL
+        assert toks[s] == oracle.greedy(refs[s][1])
+        assert tiny_engine.seq_len(s) == len(seqs[s]) + 1
+
+
+@pytest.mark.parametrize("bits", [(4, 4), (3, 2)])
+def test_tiny_packed_kv(nb, oracle, tiny_path, bits):
+    b = nb.CudaBackend(device=0, kv_bits=bits)
+    e = nb.InferenceEngine(b)
+    e.load_model(tiny_path)
+    m = oracle.Model(tiny_path, kv_bits=bits)
+    p = prompt(2, 40, 4096)
+    ref = m.prefill(p)
+    got, tok = e.prefill(p)
+    assert np.max(np.abs(got - ref)) < LOGIT_TOL
+    assert e.generate(p, 16) == m.generate(p, 16)
+    e.close()
+    b.close()
+
+
+def test_kv_overflow_is_an_error_not_a_shift(nb, tiny_path):
+    b = nb.CudaBackend(device=0, max_seq_len=8)
+    e = nb.InferenceEngine(b)
+    e.load_model(tiny_path)
+    e.prefill(list(range(8)))
+    with pytest.raises(nb.NexusError):
+        e.decode_with_cache(1, 8)
+    e.close()
+    b.close()
+
+
+def test_missing_tensor_is_an_error(nb, tmp_path):
+    from tests.gguf_writer import write_gguf
+    path = tmp_path / "empty.gguf"
+    write_gguf(path, {"general.architecture": "llama", "llama.embedding_length": 256, "llama.block_count": 1,
+                      "llama.attention.head_count": 8}, [])
+    b = nb.CudaBackend(device=0)
+    e = nb.InferenceEngine(b)
+    with pytest.raises(nb.NexusError) as err:
+        e.load_model(path)
+    assert err.value.code == nb._lib.NEXUS_E_MISSING_TENSOR
+    b.close()
+
+
+@pytest.mark.slow
+def test_llama8b_shape_short_prompt(nb, oracle):
+    """8B shape (Q4_K body, Q8_0 embedding/head): 6-token prompt + 3 greedy tokens."""
+    path = nb.model_path("llama8b_q4k")
+    b = nb.CudaBackend(device=0, max_seq_len=64)
+    e = nb.InferenceEngine(b)
+    e.load_model(path)
+    m = oracle.Model(path, threads=32, max_seq_len=64)
+    p = prompt(1, 6, 128256)
+    ref = m.prefill(p)
+    got, tok = e.prefill(p)
+    assert np.max(np.abs(got - ref)) < LOGIT_TOL
+    assert tok == oracle.greedy(ref)
+    assert e.generate(p, 3) == m.generate(p, 3)
+    e.close()
+    b.close()
