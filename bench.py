@@ -192,6 +192,24 @@ def run_reference(args):
     return 0
 
 
+def run_ncu_case(args):
+    """Small, fixed launch sequence for `ncu` captures: prefill 8 tokens as two
+    4-token steps (163 kernels each on the 8B shape), then ncu_steps
+    single-token decode steps from the captured graph."""
+    import nexus_b200 as nb
+    path = nb.model_path(args.config, threads=cpu_threads())
+    backend = nb.CudaBackend(device=0, max_seq_len=64)
+    eng = nb.InferenceEngine(backend)
+    eng.load_model(path)
+    prompt = np.random.default_rng(SEED_PROMPT).integers(0, eng.info.vocab_rows, 8).tolist()
+    out = eng.generate(prompt, args.ncu_steps)
+    print(json.dumps({"ncu_case": args.config, "prefill": 8, "decode_steps": args.ncu_steps,
+                      "tokens": out[8:], "kernels_per_step": 5 * eng.info.num_layers + 3}), flush=True)
+    eng.close()
+    backend.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -202,6 +220,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-budget", type=float, default=60.0)
     ap.add_argument("--profile-steps", type=int, default=4)
+    ap.add_argument("--ncu-steps", type=int, default=0,
+                    help="profiling run for ncu: 8-token prefill (2 fused 4-token steps), then this many "
+                         "device-chained decode steps; prints a short JSON line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -209,6 +230,8 @@ def main():
         args.steps = GEN_TOKENS - args.warmup
     if args.impl == "reference":
         return run_reference(args)
+    if args.ncu_steps:
+        return run_ncu_case(args)
 
     world, rank, local = dist_env()
     import torch

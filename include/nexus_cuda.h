@@ -123,7 +123,10 @@ enum {
     NEXUS_OP_DEQUANTIZE = 8,  /* GgufReader::tensor_bytes_to_f32, src/gguf/mod.rs:902-956 */
     NEXUS_OP_QMATVEC = 9,     /* Y[m,n] = X[m,k] @ W[n,k]^T with W in a block format */
     NEXUS_OP_ROPE = 10,       /* rope_single over every head, src/kernel/mod.rs:258-271 */
-    NEXUS_OP_ARGMAX = 11      /* greedy_token, src/engine/mod.rs:809-817 */
+    NEXUS_OP_ARGMAX = 11,     /* greedy_token, src/engine/mod.rs:809-817 */
+    NEXUS_OP_KV_QUANTIZE = 12 /* PackedKvBuffer::add of one vector, src/engine/mod.rs:209-232:
+                                 a = len floats, k = bits; out = ceil(len*bits/8) packed bytes
+                                 followed by the f32 min and f32 scale */
 };
 
 typedef struct {

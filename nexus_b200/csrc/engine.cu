@@ -35,7 +35,38 @@ struct nexus_cuda_backend {
     cudaStream_t stream = nullptr;
     std::string last_error;
     std::mutex mu;
+    // Models and resident weights keep their backend alive: destroying a
+    // backend that still has children only marks it, and the last child
+    // to go frees it.
+    int children = 0;
+    bool destroy_pending = false;
 };
+
+static std::mutex g_backend_mu;
+
+static void backend_free_now(nexus_cuda_backend *b) {
+    cudaSetDevice(b->device);
+    if (b->stream) {
+        cudaStreamSynchronize(b->stream);
+        cudaStreamDestroy(b->stream);
+    }
+    delete b;
+}
+
+static void backend_retain(nexus_cuda_backend *b) {
+    std::lock_guard<std::mutex> lk(g_backend_mu);
+    b->children++;
+}
+
+static void backend_release(nexus_cuda_backend *b) {
+    bool free_now = false;
+    {
+        std::lock_guard<std::mutex> lk(g_backend_mu);
+        b->children--;
+        free_now = b->children == 0 && b->destroy_pending;
+    }
+    if (free_now) backend_free_now(b);
+}
 
 static int set_err(nexus_cuda_backend *b, int code, const std::string &msg) {
     if (b) b->last_error = msg;
@@ -94,6 +125,17 @@ static int make_mat(nexus_cuda_backend *b, int fmt, int n, int k, const uint8_t 
     cudaFree(draw);
     if (e != cudaSuccess) return set_err(b, NEXUS_E_CUDA, std::string("repack: ") + cudaGetErrorString(e));
     return NEXUS_OK;
+}
+
+// K-split scratch for an N-row GEMV of up to 4 tokens: 8 slices of partials.
+static cudaError_t alloc_split_scratch(size_t n, float **part, size_t *part_floats, unsigned **ctr, int *slots) {
+    const size_t groups = (n + 31) / 32;
+    *part_floats = 8 * 4 * groups * 32;
+    *slots = (int)groups;
+    cudaError_t e = dalloc(part, *part_floats);
+    if (e == cudaSuccess) e = dalloc(ctr, groups);
+    if (e == cudaSuccess) e = cudaMemset(*ctr, 0, groups * sizeof(unsigned));
+    return e;
 }
 
 // ---------------------------------------------------------------------------
@@ -171,12 +213,13 @@ extern "C" int nexus_cuda_backend_create(const nexus_cuda_config *cfg, nexus_cud
 
 extern "C" int nexus_cuda_backend_destroy(nexus_cuda_backend *b) {
     if (!b) return NEXUS_OK;
-    cudaSetDevice(b->device);
-    if (b->stream) {
-        cudaStreamSynchronize(b->stream);
-        cudaStreamDestroy(b->stream);
+    {
+        std::lock_guard<std::mutex> lk(g_backend_mu);
+        if (b->destroy_pending) return NEXUS_OK;
+        b->destroy_pending = true;
+        if (b->children > 0) return NEXUS_OK;
     }
-    delete b;
+    backend_free_now(b);
     return NEXUS_OK;
 }
 
@@ -328,6 +371,11 @@ extern "C" int nexus_cuda_execute(nexus_cuda_backend *b, const nexus_op *op) {
         out_bytes = m * n * 4;
         NX_CUDA(b, stage_in(op->a, m * k * 4, dev, A, st));
         NX_CUDA(b, stage_out(op->out, out_bytes, dev, O));
+        float *spart = nullptr;
+        size_t spart_floats = 0;
+        unsigned *sctr = nullptr;
+        int sslots = 0;
+        NX_CUDA(b, alloc_split_scratch(n, &spart, &spart_floats, &sctr, &sslots));
         for (size_t t0 = 0; t0 < m && e == cudaSuccess;) {
             size_t chunk = m - t0 >= 4 ? 4 : m - t0 >= 2 ? 2 : 1;
             GemvParams p = {};
@@ -342,10 +390,16 @@ extern "C" int nexus_cuda_execute(nexus_cuda_backend *b, const nexus_op *op) {
             p.epi = EPI_STORE;
             p.y = (float *)O.d + t0 * n;
             p.y_stride = (int)n;
+            p.part = spart;
+            p.part_floats = spart_floats;
+            p.counters = sctr;
+            p.counter_slots = sslots;
             e = launch_gemv(p, st);
             t0 += chunk;
         }
         cudaError_t e2 = cudaStreamSynchronize(st);
+        cudaFree(spart);
+        cudaFree(sctr);
         mat.release();
         if (e == cudaSuccess) e = e2;
         break;
@@ -383,6 +437,54 @@ extern "C" int nexus_cuda_execute(nexus_cuda_backend *b, const nexus_op *op) {
         else memcpy(op->out, &tok, 4);
         return NEXUS_OK;
     }
+    case NEXUS_OP_KV_QUANTIZE: {
+        const size_t n = op->len, bits = op->k;
+        if (n == 0 || bits < 1 || bits > 8) return set_err(b, NEXUS_E_INVALID, "kv_quantize: 1..8 bits, len > 0");
+        const size_t bpt = (n * bits + 7) / 8;
+        out_bytes = bpt + 8;
+        float *scratch = nullptr, *mins = nullptr;
+        uint8_t *data = nullptr;
+        DevSeq *ds = nullptr;
+        uint32_t *sid = nullptr;
+        NX_CUDA(b, dalloc(&scratch, 2 * n));
+        NX_CUDA(b, dalloc(&mins, 4));
+        NX_CUDA(b, dalloc(&data, 2 * bpt + 16));
+        NX_CUDA(b, dalloc(&ds, 1));
+        NX_CUDA(b, dalloc(&sid, 1));
+        NX_CUDA(b, cudaMemsetAsync(ds, 0, sizeof(DevSeq), st));
+        NX_CUDA(b, cudaMemsetAsync(sid, 0, 4, st));
+        NX_CUDA(b, cudaMemcpyAsync(scratch, op->a, n * 4, dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
+        NX_CUDA(b, cudaMemcpyAsync(scratch + n, op->a, n * 4, dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
+        KvPackParams kp = {};
+        kp.m = 1;
+        kp.kv_dim = (int)n;
+        kp.bits_k = kp.bits_v = (int)bits;
+        kp.kv_scratch = scratch;
+        kp.kp_data = data;
+        kp.vp_data = data + bpt + 8;
+        kp.kp_min = mins;
+        kp.kp_scale = mins + 1;
+        kp.vp_min = mins + 2;
+        kp.vp_scale = mins + 3;
+        kp.pk_bpt_k = kp.pk_bpt_v = bpt;
+        kp.pk_seq_stride_k = kp.pk_seq_stride_v = bpt;
+        kp.pk_seq_tokens = 1;
+        kp.seqs = ds;
+        kp.seq_ids = sid;
+        e = launch_kv_pack(kp, st);
+        cudaMemcpyKind kind = dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
+        if (e == cudaSuccess) e = cudaMemcpyAsync(op->out, data, bpt, kind, st);
+        if (e == cudaSuccess) e = cudaMemcpyAsync((uint8_t *)op->out + bpt, mins, 8, kind, st);
+        cudaError_t e2 = cudaStreamSynchronize(st);
+        cudaFree(scratch);
+        cudaFree(mins);
+        cudaFree(data);
+        cudaFree(ds);
+        cudaFree(sid);
+        if (e == cudaSuccess) e = e2;
+        if (e != cudaSuccess) return set_err(b, NEXUS_E_CUDA, std::string("kv_quantize: ") + cudaGetErrorString(e));
+        return NEXUS_OK;
+    }
     case NEXUS_OP_ATTENTION: {
         // GQA decode attention of one query token over n cached tokens:
         // q [m*k], keys/values [n][kv_heads*k]
@@ -401,7 +503,7 @@ extern "C" int nexus_cuda_execute(nexus_cuda_backend *b, const nexus_op *op) {
         uint32_t *sid = nullptr;
         float *part = nullptr;
         unsigned *ctr = nullptr;
-        int nsplit = (int)std::min<size_t>(64, std::max<size_t>(1, seq / 16));
+        int nsplit = (int)std::min<size_t>(64, std::max<size_t>(1, (seq + 63) / 64));
         size_t G = hq / hkv;
         NX_CUDA(b, dalloc(&ds, 1));
         NX_CUDA(b, dalloc(&sid, 1));
@@ -452,7 +554,13 @@ struct nexus_cuda_qweight {
     Mat mat;
     float *xbuf = nullptr, *ybuf = nullptr;
     size_t xcap = 0, ycap = 0;
+    // K-split scratch of the GEMV: partial row sums and per-row-group counters
+    float *part = nullptr;
+    size_t part_floats = 0;
+    unsigned *counters = nullptr;
+    int counter_slots = 0;
 };
+
 
 extern "C" int nexus_cuda_qweight_create(nexus_cuda_backend *b, int format, size_t rows, size_t cols,
                                          const void *blocks, size_t nbytes, nexus_cuda_qweight **out) {
@@ -470,6 +578,15 @@ extern "C" int nexus_cuda_qweight_create(nexus_cuda_backend *b, int format, size
         delete w;
         return rc;
     }
+    cudaError_t se = alloc_split_scratch(rows, &w->part, &w->part_floats, &w->counters, &w->counter_slots);
+    if (se != cudaSuccess) {
+        w->mat.release();
+        if (w->part) cudaFree(w->part);
+        if (w->counters) cudaFree(w->counters);
+        delete w;
+        return set_err(b, NEXUS_E_OOM, std::string("qweight scratch: ") + cudaGetErrorString(se));
+    }
+    backend_retain(b);
     *out = w;
     return NEXUS_OK;
 }
@@ -480,7 +597,11 @@ extern "C" int nexus_cuda_qweight_destroy(nexus_cuda_qweight *w) {
     w->mat.release();
     if (w->xbuf) cudaFree(w->xbuf);
     if (w->ybuf) cudaFree(w->ybuf);
+    if (w->part) cudaFree(w->part);
+    if (w->counters) cudaFree(w->counters);
+    nexus_cuda_backend *b = w->b;
     delete w;
+    backend_release(b);
     return NEXUS_OK;
 }
 
@@ -504,6 +625,10 @@ extern "C" int nexus_cuda_qmatvec_device(nexus_cuda_qweight *w, const float *x_d
         p.epi = EPI_STORE;
         p.y = y_dev + t0 * w->mat.n;
         p.y_stride = w->mat.n;
+        p.part = w->part;
+        p.part_floats = w->part_floats;
+        p.counters = w->counters;
+        p.counter_slots = w->counter_slots;
         NX_CUDA(b, launch_gemv(p, b->stream));
         t0 += chunk;
     }
@@ -575,6 +700,10 @@ struct nexus_cuda_model {
     float *hidden = nullptr, *q = nullptr, *attn = nullptr, *gated = nullptr, *kv_scratch = nullptr;
     float *logits = nullptr, *part = nullptr;
     unsigned *counters = nullptr;
+    float *gemv_part = nullptr;       // GEMV K-split partials
+    size_t gemv_part_floats = 0;
+    unsigned *gemv_ctr = nullptr;     // GEMV row-group arrival counters
+    int gemv_ctr_slots = 0;
     DevSeq *seqs = nullptr;
     uint32_t *seq_ids = nullptr, *out_tokens = nullptr;
     DevSeq *h_seqs = nullptr;
@@ -588,6 +717,7 @@ struct nexus_cuda_model {
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     float last_ms = 0.0f;
     std::vector<void *> allocs;
+    bool retained = false;  // holds a reference on its backend
 };
 
 template <typename T>
@@ -599,6 +729,7 @@ static cudaError_t malloc_tracked(nexus_cuda_model *m, T **p, size_t count) {
 
 static void model_release(nexus_cuda_model *m) {
     if (!m) return;
+    nexus_cuda_backend *owner = m->retained ? m->b : nullptr;
     cudaSetDevice(m->b->device);
     cudaStreamSynchronize(m->b->stream);
     for (auto &g : m->graph)
@@ -617,6 +748,7 @@ static void model_release(nexus_cuda_model *m) {
     if (m->ev0) cudaEventDestroy(m->ev0);
     if (m->ev1) cudaEventDestroy(m->ev1);
     delete m;
+    if (owner) backend_release(owner);
 }
 
 static const GgufTensor *find_any(const GgufFile &f, const std::vector<std::string> &names) {
@@ -856,30 +988,41 @@ static int model_load(nexus_cuda_backend *b, const char *path, nexus_cuda_model 
     NX_CUDA(b, malloc_tracked(m, &m->kv_scratch, (size_t)MC * 2 * kv_dim));
     NX_CUDA(b, malloc_tracked(m, &m->logits, (size_t)MC * I.vocab_rows));
     const int G = (int)(Hq / Hkv);
-    int max_split = 1;
-    for (int mm = 1; mm <= MC; mm++) {
-        int s = (2 * 148 + (int)Hkv * mm - 1) / ((int)Hkv * mm);
-        s = std::max(1, std::min(s, 64));
-        s = std::min<int>(s, std::max<int>(1, (int)(m->max_seq / 16)));
-        m->nsplit[mm] = s;
-        max_split = std::max(max_split, s);
-    }
+    // context slices of >= 64 tokens, at most 64 per (sequence, KV head); the
+    // kernel uses only as many as the current context needs
+    int max_split = std::max(1, std::min(64, (int)((m->max_seq + 63) / 64)));
+    for (int mm = 1; mm <= MC; mm++) m->nsplit[mm] = max_split;
     NX_CUDA(b, malloc_tracked(m, &m->part, (size_t)MC * Hkv * max_split * G * (D + 2)));
     NX_CUDA(b, malloc_tracked(m, &m->counters, (size_t)MC * Hkv));
     NX_CUDA(b, cudaMemset(m->counters, 0, (size_t)MC * Hkv * 4));
+    {
+        // stream-K GEMV scratch: partial row sums of row groups shared by up to
+        // 8 CTAs, and one arrival counter per row group, for every GEMV
+        const size_t nmax = std::max<size_t>({(size_t)qdim + 2 * kv_dim, (size_t)2 * F, (size_t)H,
+                                              (size_t)I.vocab_rows});
+        const size_t groups = (nmax + 31) / 32;
+        m->gemv_part_floats = 8 * (size_t)MC * groups * 32;
+        m->gemv_ctr_slots = (int)groups;
+        NX_CUDA(b, malloc_tracked(m, &m->gemv_part, m->gemv_part_floats));
+        NX_CUDA(b, malloc_tracked(m, &m->gemv_ctr, groups));
+        NX_CUDA(b, cudaMemset(m->gemv_ctr, 0, groups * sizeof(unsigned)));
+    }
     NX_CUDA(b, malloc_tracked(m, &m->seqs, MC));
     NX_CUDA(b, malloc_tracked(m, &m->seq_ids, MC));
-    NX_CUDA(b, malloc_tracked(m, &m->out_tokens, MC));
+    NX_CUDA(b, malloc_tracked(m, &m->out_tokens, MC + 1));  // [MC] tokens + error flag
     NX_CUDA(b, cudaMemset(m->seqs, 0, MC * sizeof(DevSeq)));
     NX_CUDA(b, cudaMemset(m->seq_ids, 0, MC * 4));
     NX_CUDA(b, cudaHostAlloc((void **)&m->h_seqs, MC * sizeof(DevSeq), cudaHostAllocDefault));
     NX_CUDA(b, cudaHostAlloc((void **)&m->h_seq_ids, MC * 4, cudaHostAllocDefault));
-    NX_CUDA(b, cudaHostAlloc((void **)&m->h_out_tokens, MC * 4, cudaHostAllocDefault));
+    NX_CUDA(b, cudaHostAlloc((void **)&m->h_out_tokens, (MC + 1) * 4, cudaHostAllocDefault));
+    NX_CUDA(b, cudaMemset(m->out_tokens, 0, (MC + 1) * 4));
     NX_CUDA(b, cudaEventCreate(&m->ev0));
     NX_CUDA(b, cudaEventCreate(&m->ev1));
     m->seq_len.assign(m->max_batch, 0);
     NX_CUDA(b, cudaDeviceSynchronize());
     guard.release();
+    backend_retain(b);
+    m->retained = true;
     *out = m;
     return NEXUS_OK;
 }
@@ -931,8 +1074,18 @@ struct StepProfiler {
     }
 };
 
+static void set_split_scratch(const nexus_cuda_model *m, GemvParams &g);
+
 static double gemv_bytes(const Mat &w, int mc, int k, int n_out) {
     return (double)w.bytes + 4.0 * mc * k + 4.0 * mc * n_out;
+}
+
+static void set_split_scratch(const nexus_cuda_model *m, GemvParams &g) {
+    g.part = m->gemv_part;
+    g.part_floats = m->gemv_part_floats;
+    g.counters = m->gemv_ctr;
+    g.counter_slots = m->gemv_ctr_slots;
+    g.err = reinterpret_cast<int *>(m->out_tokens + kMaxChunk);
 }
 
 // Enqueue one fused decode step for `mc` tokens whose DevSeq entries are on the device.
@@ -959,6 +1112,7 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
     for (uint32_t l = 0; l < I.num_layers; l++) {
         Layer &L = m->layers[l];
         GemvParams g = {};
+        set_split_scratch(m, g);
         g.m = mc;
         g.pdl = pdl;
         g.eps = I.rms_norm_eps;
@@ -1056,6 +1210,7 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         if (prof) prof->end("attention", attn_bytes);
         // o_proj + residual
         GemvParams o = {};
+        set_split_scratch(m, o);
         o.m = mc;
         o.pdl = pdl;
         o.fmt = L.o.fmt;
@@ -1073,6 +1228,7 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         if (prof) prof->end("o_proj", gemv_bytes(L.o, mc, qdim, H) + 4.0 * mc * H);
         // ffn_norm -> gate/up -> SwiGLU
         GemvParams gu = {};
+        set_split_scratch(m, gu);
         gu.m = mc;
         gu.pdl = pdl;
         gu.eps = I.rms_norm_eps;
@@ -1092,6 +1248,7 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         if (prof) prof->end("gate_up", gemv_bytes(L.gateup, mc, H, F) + 4.0 * H);
         // down + residual
         GemvParams dn = {};
+        set_split_scratch(m, dn);
         dn.m = mc;
         dn.pdl = pdl;
         dn.fmt = L.down.fmt;
@@ -1111,6 +1268,7 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
     // transformer_logits: output norm + head + greedy argmax
     if (m->has_head) {
         GemvParams hd = {};
+        set_split_scratch(m, hd);
         hd.m = mc;
         hd.pdl = pdl;
         hd.eps = I.rms_norm_eps;
@@ -1170,6 +1328,13 @@ static int run_step(nexus_cuda_model *m, int mc) {
     return NEXUS_OK;
 }
 
+// A kernel gave up on a bounded wait: report it and clear the flag.
+static int device_timeout(nexus_cuda_model *m) {
+    cudaMemsetAsync(m->out_tokens + kMaxChunk, 0, 4, m->b->stream);
+    cudaStreamSynchronize(m->b->stream);
+    return set_err(m->b, NEXUS_E_TIMEOUT, "a device wait timed out (weight stream did not arrive)");
+}
+
 // Host-driven step over `items` (at most kMaxChunk), results to host.
 struct StepItem {
     uint32_t sid, token, position, slot;
@@ -1199,8 +1364,9 @@ static int host_step(nexus_cuda_model *m, const StepItem *items, int mc, float *
         else
             NX_CUDA(b, cudaMemcpyAsync(logits_out, m->logits, (size_t)mc * V * 4, cudaMemcpyDeviceToHost, st));
     }
-    NX_CUDA(b, cudaMemcpyAsync(m->h_out_tokens, m->out_tokens, mc * 4, cudaMemcpyDeviceToHost, st));
+    NX_CUDA(b, cudaMemcpyAsync(m->h_out_tokens, m->out_tokens, (kMaxChunk + 1) * 4, cudaMemcpyDeviceToHost, st));
     NX_CUDA(b, cudaStreamSynchronize(st));
+    if (m->h_out_tokens[kMaxChunk]) return device_timeout(m);
     if (tokens_out) memcpy(tokens_out, m->h_out_tokens, mc * 4);
     return NEXUS_OK;
 }
@@ -1350,6 +1516,7 @@ extern "C" int nexus_cuda_generate(nexus_cuda_model *m, uint32_t seq_id, const u
         }
     }
     cudaEventRecord(m->ev1, st);
+    if (!rc) cudaMemcpyAsync(m->h_out_tokens, m->out_tokens, (kMaxChunk + 1) * 4, cudaMemcpyDeviceToHost, st);
     if (!rc && max_tokens > 1)
         rc = cudaMemcpyAsync(out + n + 1, ring, (max_tokens - 1) * 4, cudaMemcpyDeviceToHost, st) == cudaSuccess
                  ? NEXUS_OK
@@ -1359,6 +1526,7 @@ extern "C" int nexus_cuda_generate(nexus_cuda_model *m, uint32_t seq_id, const u
     cudaFree(ring);
     if (rc) return rc;
     if (e != cudaSuccess) return set_err(b, NEXUS_E_CUDA, cudaGetErrorString(e));
+    if (m->h_out_tokens[kMaxChunk]) return device_timeout(m);
     m->seq_len[seq_id] += (uint32_t)max_tokens;
     return NEXUS_OK;
 }
@@ -1435,8 +1603,9 @@ extern "C" int nexus_cuda_profile_decode(nexus_cuda_model *m, uint32_t seq_id, u
         NX_CUDA(b, cudaMemcpyAsync(m->seqs, m->h_seqs, sizeof(DevSeq), cudaMemcpyHostToDevice, st));
         NX_CUDA(b, cudaMemcpyAsync(m->seq_ids, m->h_seq_ids, 4, cudaMemcpyHostToDevice, st));
         NX_CUDA(b, enqueue_step(m, 1, &prof));
-        NX_CUDA(b, cudaMemcpyAsync(m->h_out_tokens, m->out_tokens, 4, cudaMemcpyDeviceToHost, st));
+        NX_CUDA(b, cudaMemcpyAsync(m->h_out_tokens, m->out_tokens, (kMaxChunk + 1) * 4, cudaMemcpyDeviceToHost, st));
         NX_CUDA(b, cudaStreamSynchronize(st));
+        if (m->h_out_tokens[kMaxChunk]) return device_timeout(m);
         tok = m->h_out_tokens[0];
         m->seq_len[seq_id] += 1;
     }

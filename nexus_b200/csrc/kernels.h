@@ -64,6 +64,13 @@ struct GemvParams {
     QkvEpilogue qkv;
     DevSeq *seqs;       // EPI_ARGMAX: best accumulators per token
     int pdl;            // 1: launched with programmatic stream serialization
+    // K-split scratch (optional; without it the GEMV never splits K)
+    float *part;            // [S][m][groups*32] partial row sums
+    size_t part_floats;     // capacity of part
+    unsigned *counters;     // [groups] arrival counters, zero on entry and exit
+    int counter_slots;      // capacity of counters
+    int ksplit;             // unused by the stream-K kernel
+    int *err;               // device flag set when a bounded wait gives up (may be NULL)
 };
 
 cudaError_t launch_gemv(const GemvParams &p, cudaStream_t st);

@@ -7,12 +7,15 @@
 // src/engine/mod.rs:252-256), one (min, scale) per token across all KV heads.
 //
 // Split-context ("flash decoding") layout: grid (Hkv, nsplit, batch).  Each
-// CTA owns one KV head, a contiguous slice of the context and all G query
-// heads that share that KV head, so every K/V element is read from HBM once.
-// Four warps stride over the slice's tokens; lane i holds head_dim/32 dims.
-// Each warp keeps an online softmax per query head; warps are merged in
-// shared memory, splits through a scratch buffer by the last CTA to finish
-// (an atomic counter per (sequence, KV head) that it resets for the next use).
+// CTA owns one KV head, a contiguous slice of at least kTokensPerSplit tokens
+// of the context, and all G query heads sharing that KV head, so every K/V
+// element is read from HBM once.  The slice count adapts to the context
+// length (CTAs beyond it exit), so short contexts use few, full slices.
+// Eight warps stride over the slice; each warp issues the loads of kBatch
+// tokens before using any of them (one memory round trip per batch); lane i
+// holds head_dim/32 dims of each row.  Warps keep an online softmax per query
+// head, are merged in shared memory, and slices are merged by the last CTA to
+// finish (an atomic counter per (sequence, KV head), reset by that CTA).
 #include <cuda_runtime.h>
 #include <math.h>
 
@@ -21,17 +24,21 @@
 
 namespace nx {
 
+constexpr int kAttnWarps = 8;
+constexpr int kBatch = 8;
+constexpr int kTokensPerSplit = 64;
+
 template <int VEC>
 __device__ __forceinline__ void load_f32(const float *p, float (&v)[VEC]) {
     if constexpr (VEC == 4) {
-        float4 t = *reinterpret_cast<const float4 *>(p);
+        float4 t = __ldcg(reinterpret_cast<const float4 *>(p));
         v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
     } else if constexpr (VEC == 2) {
-        float2 t = *reinterpret_cast<const float2 *>(p);
+        float2 t = __ldcg(reinterpret_cast<const float2 *>(p));
         v[0] = t.x; v[1] = t.y;
     } else {
 #pragma unroll
-        for (int i = 0; i < VEC; i++) v[i] = p[i];
+        for (int i = 0; i < VEC; i++) v[i] = __ldcg(p + i);
     }
 }
 
@@ -50,14 +57,20 @@ __device__ __forceinline__ void load_packed(const uint8_t *row, int e0, int bits
     }
 }
 
+__device__ __forceinline__ int active_splits(int seq_len, int nsplit_grid) {
+    int s = (seq_len + kTokensPerSplit - 1) / kTokensPerSplit;
+    return max(1, min(s, nsplit_grid));
+}
+
 template <int VEC, int G>
-__global__ void __launch_bounds__(128) k_attn(AttnParams p) {
+__global__ void __launch_bounds__(kAttnWarps * 32) k_attn(AttnParams p) {
     constexpr int D = VEC * 32;
-    constexpr int NW = 4;
+    constexpr int NW = kAttnWarps;
     const int h = blockIdx.x, split = blockIdx.y, t = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     __shared__ float sm_m[NW][G], sm_l[NW][G];
     __shared__ float sm_o[NW][G][D];
+    __shared__ float sm_w[64][G];
     __shared__ bool is_last;
 
     if (p.pdl) {
@@ -67,7 +80,9 @@ __global__ void __launch_bounds__(128) k_attn(AttnParams p) {
     const DevSeq sq = p.seqs[t];
     const uint32_t sid = p.seq_ids[t];
     const int seq_len = (int)sq.seq_len;
-    const int per = (seq_len + p.nsplit - 1) / p.nsplit;
+    const int nsplit = active_splits(seq_len, p.nsplit);
+    if (split >= nsplit) return;
+    const int per = (seq_len + nsplit - 1) / nsplit;
     const int t0 = split * per, t1 = min(seq_len, t0 + per);
 
     float qv[G][VEC];
@@ -84,42 +99,51 @@ __global__ void __launch_bounds__(128) k_attn(AttnParams p) {
     }
 
     const bool packed = p.bits_k > 0;
-    for (int tok = t0 + warp; tok < t1; tok += NW) {
-        float kv[VEC], vv[VEC];
-        const int e0 = h * D + lane * VEC;
-        if (!packed) {
-            const size_t off = (size_t)sid * p.seq_stride + (size_t)tok * p.kv_dim + e0;
-            load_f32<VEC>(p.k_cache + off, kv);
-            load_f32<VEC>(p.v_cache + off, vv);
-        } else {
-            const size_t mi = (size_t)sid * p.pk_seq_tokens + tok;
-            load_packed<VEC>(p.kp_data + (size_t)sid * p.pk_seq_stride_k + (size_t)tok * p.pk_bpt_k, e0,
-                             p.bits_k, p.kp_min[mi], p.kp_scale[mi], kv);
-            load_packed<VEC>(p.vp_data + (size_t)sid * p.pk_seq_stride_v + (size_t)tok * p.pk_bpt_v, e0,
-                             p.bits_v, p.vp_min[mi], p.vp_scale[mi], vv);
-        }
-        float dot[G];
+    const int e0 = h * D + lane * VEC;
+    for (int base = t0 + warp * kBatch; base < t1; base += NW * kBatch) {
+        float kv[kBatch][VEC], vv[kBatch][VEC];
+        // issue every load of the batch first
 #pragma unroll
-        for (int g = 0; g < G; g++) {
-            float s = 0.0f;
-#pragma unroll
-            for (int i = 0; i < VEC; i++) s += qv[g][i] * kv[i];
-            dot[g] = s;
+        for (int j = 0; j < kBatch; j++) {
+            const int tok = min(base + j, t1 - 1);
+            if (!packed) {
+                const size_t off = (size_t)sid * p.seq_stride + (size_t)tok * p.kv_dim + e0;
+                load_f32<VEC>(p.k_cache + off, kv[j]);
+                load_f32<VEC>(p.v_cache + off, vv[j]);
+            } else {
+                const size_t mi = (size_t)sid * p.pk_seq_tokens + tok;
+                load_packed<VEC>(p.kp_data + (size_t)sid * p.pk_seq_stride_k + (size_t)tok * p.pk_bpt_k, e0,
+                                 p.bits_k, p.kp_min[mi], p.kp_scale[mi], kv[j]);
+                load_packed<VEC>(p.vp_data + (size_t)sid * p.pk_seq_stride_v + (size_t)tok * p.pk_bpt_v, e0,
+                                 p.bits_v, p.vp_min[mi], p.vp_scale[mi], vv[j]);
+            }
         }
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1)
+        for (int j = 0; j < kBatch; j++) {
+            if (base + j >= t1) break;
+            float dot[G];
 #pragma unroll
-            for (int g = 0; g < G; g++) dot[g] += __shfl_xor_sync(0xffffffffu, dot[g], off);
+            for (int g = 0; g < G; g++) {
+                float s = 0.0f;
 #pragma unroll
-        for (int g = 0; g < G; g++) {
-            const float s = dot[g] * p.scale;
-            const float mn = fmaxf(m[g], s);
-            const float corr = expf(m[g] - mn);
-            const float pe = expf(s - mn);
-            l[g] = l[g] * corr + pe;
+                for (int i = 0; i < VEC; i++) s += qv[g][i] * kv[j][i];
+                dot[g] = s;
+            }
 #pragma unroll
-            for (int i = 0; i < VEC; i++) o[g][i] = o[g][i] * corr + pe * vv[i];
-            m[g] = mn;
+            for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+                for (int g = 0; g < G; g++) dot[g] += __shfl_xor_sync(0xffffffffu, dot[g], off);
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                const float s = dot[g] * p.scale;
+                const float mn = fmaxf(m[g], s);
+                const float corr = expf(m[g] - mn);
+                const float pe = expf(s - mn);
+                l[g] = l[g] * corr + pe;
+#pragma unroll
+                for (int i = 0; i < VEC; i++) o[g][i] = o[g][i] * corr + pe * vv[j][i];
+                m[g] = mn;
+            }
         }
     }
 
@@ -134,13 +158,33 @@ __global__ void __launch_bounds__(128) k_attn(AttnParams p) {
         for (int i = 0; i < VEC; i++) sm_o[warp][g][lane * VEC + i] = o[g][i];
     }
     __syncthreads();
+    if (nsplit == 1) {
+        // the whole context is this CTA's slice: normalize and write directly
+        for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+            const int g = idx / D, d = idx % D;
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < NW; w++) M = fmaxf(M, sm_m[w][g]);
+            float L = 0.0f, O = 0.0f;
+#pragma unroll
+            for (int w = 0; w < NW; w++) {
+                const float wt = sm_m[w][g] == -INFINITY ? 0.0f : expf(sm_m[w][g] - M);
+                L += wt * sm_l[w][g];
+                O += wt * sm_o[w][g][d];
+            }
+            p.out[(size_t)t * p.hq * D + (size_t)(h * G + g) * D + d] = L > 0.0f ? O / L : 0.0f;
+        }
+        return;
+    }
     const int stride = D + 2;
     float *part = p.part + (((size_t)t * p.hkv + h) * p.nsplit) * G * stride;
     for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
         const int g = idx / D, d = idx % D;
         float M = -INFINITY;
+#pragma unroll
         for (int w = 0; w < NW; w++) M = fmaxf(M, sm_m[w][g]);
         float L = 0.0f, O = 0.0f;
+#pragma unroll
         for (int w = 0; w < NW; w++) {
             const float wt = sm_m[w][g] == -INFINITY ? 0.0f : expf(sm_m[w][g] - M);
             L += wt * sm_l[w][g];
@@ -158,24 +202,41 @@ __global__ void __launch_bounds__(128) k_attn(AttnParams p) {
     if (threadIdx.x == 0) {
         unsigned *ctr = p.counters + (size_t)t * p.hkv + h;
         const unsigned prev = atomicAdd(ctr, 1u);
-        is_last = prev == (unsigned)(p.nsplit - 1);
+        is_last = prev == (unsigned)(nsplit - 1);
         if (is_last) *ctr = 0u;
     }
     __syncthreads();
     if (!is_last) return;
     __threadfence();
+    // slice merge: softmax weights of every (slice, head) in parallel ...
+    __shared__ float sm_M[G], sm_L[G];
+    for (int idx = threadIdx.x; idx < nsplit * G; idx += blockDim.x) {
+        const int s = idx / G, g = idx % G;
+        sm_w[s][g] = __ldcg(part + ((size_t)s * G + g) * stride + D);
+    }
+    __syncthreads();
+    if (threadIdx.x < G) {
+        const int g = threadIdx.x;
+        float M = -INFINITY;
+        for (int s = 0; s < nsplit; s++) M = fmaxf(M, sm_w[s][g]);
+        float L = 0.0f;
+        for (int s = 0; s < nsplit; s++) {
+            const float ms = sm_w[s][g];
+            const float wt = ms == -INFINITY ? 0.0f : expf(ms - M);
+            L += wt * __ldcg(part + ((size_t)s * G + g) * stride + D + 1);
+            sm_w[s][g] = wt;
+        }
+        sm_M[g] = M;
+        sm_L[g] = L;
+    }
+    __syncthreads();
+    // ... then every output element from independent loads
     for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
         const int g = idx / D, d = idx % D;
-        float M = -INFINITY;
-        for (int s = 0; s < p.nsplit; s++) M = fmaxf(M, __ldcg(part + ((size_t)s * G + g) * stride + D));
-        float L = 0.0f, O = 0.0f;
-        for (int s = 0; s < p.nsplit; s++) {
-            const float *ps = part + ((size_t)s * G + g) * stride;
-            const float ms = __ldcg(ps + D);
-            const float wt = ms == -INFINITY ? 0.0f : expf(ms - M);
-            L += wt * __ldcg(ps + D + 1);
-            O += wt * __ldcg(ps + d);
-        }
+        float O = 0.0f;
+#pragma unroll 8
+        for (int s = 0; s < nsplit; s++) O += sm_w[s][g] * __ldcg(part + ((size_t)s * G + g) * stride + d);
+        const float L = sm_L[g];
         // a head whose softmax sum is not positive stays zero (src/engine/mod.rs:483-485)
         p.out[(size_t)t * p.hq * D + (size_t)(h * G + g) * D + d] = L > 0.0f ? O / L : 0.0f;
     }
@@ -185,7 +246,7 @@ template <int VEC, int G>
 static cudaError_t launch_attn_t(const AttnParams &p, cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.hkv, p.nsplit, p.m);
-    cfg.blockDim = dim3(128);
+    cfg.blockDim = dim3(kAttnWarps * 32);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -207,7 +268,7 @@ static cudaError_t launch_attn_g(const AttnParams &p, cudaStream_t st) {
 }
 
 cudaError_t launch_attention(const AttnParams &p, cudaStream_t st) {
-    if (p.hkv <= 0 || p.hq % p.hkv != 0) return cudaErrorInvalidValue;
+    if (p.hkv <= 0 || p.hq % p.hkv != 0 || p.nsplit < 1 || p.nsplit > 64) return cudaErrorInvalidValue;
     switch (p.head_dim) {
     case 32: return launch_attn_g<1>(p, st);
     case 64: return launch_attn_g<2>(p, st);

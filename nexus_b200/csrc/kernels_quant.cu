@@ -221,9 +221,23 @@ __global__ void k_embed(EmbedParams p) {
     const uint32_t token = p.seqs[t].token;
     const size_t row = p.vocab_rows ? (size_t)token % p.vocab_rows : 0;
     const int be = block_elems(p.fmt), bb = block_bytes(p.fmt);
-    for (int i = threadIdx.x; i < p.hidden; i += blockDim.x) {
-        const size_t e = row * (size_t)p.hidden + i;
-        p.out[(size_t)t * p.hidden + i] = dequant_elem(p.fmt, p.table + (e / be) * bb, (int)(e % be));
+    const uint8_t *__restrict__ table = p.table;
+    float *__restrict__ out = p.out + (size_t)t * p.hidden;
+    // decode everything first, then store (independent loads in flight)
+    constexpr int kPer = 16;
+    float v[kPer];
+    for (int base = threadIdx.x; base < p.hidden; base += blockDim.x * kPer) {
+#pragma unroll
+        for (int j = 0; j < kPer; j++) {
+            const int i = base + j * (int)blockDim.x;
+            const size_t e = row * (size_t)p.hidden + (i < p.hidden ? i : 0);
+            v[j] = dequant_elem(p.fmt, table + (e / be) * bb, (int)(e % be));
+        }
+#pragma unroll
+        for (int j = 0; j < kPer; j++) {
+            const int i = base + j * (int)blockDim.x;
+            if (i < p.hidden) out[i] = v[j];
+        }
     }
     if (threadIdx.x == 0) p.seqs[t].best = 0ull;
 }

@@ -185,6 +185,14 @@ class CudaBackend:
         self.execute(L.Op(kind=L.OP_ARGMAX, a=_ptr(x), out=_ptr(out), len=x.size))
         return int(out[0])
 
+    def kv_quantize(self, values: np.ndarray, bits: int):
+        """PackedKvBuffer::add of one vector: (packed bytes, min, scale)."""
+        v = np.ascontiguousarray(values, np.float32)
+        bpt = (v.size * bits + 7) // 8
+        out = np.zeros(bpt + 8, np.uint8)
+        self.execute(L.Op(kind=L.OP_KV_QUANTIZE, a=_ptr(v), out=_ptr(out), len=v.size, k=bits))
+        return out[:bpt], float(out[bpt:bpt + 4].view(np.float32)[0]), float(out[bpt + 4:].view(np.float32)[0])
+
     def attention(self, q: np.ndarray, keys: np.ndarray, values: np.ndarray, num_q_heads: int,
                   num_kv_heads: int, head_dim: int, scale: float = 0.0) -> np.ndarray:
         q = np.ascontiguousarray(q, np.float32)

@@ -87,6 +87,10 @@ def test_tiny_decode_batch_matches_single(tiny_engine, oracle, tiny_path):
 
 @pytest.mark.parametrize("bits", [(4, 4), (3, 2)])
 def test_tiny_packed_kv(nb, oracle, tiny_path, bits):
+    """Packed low-bit KV.  Packing itself is bit-exact (test_kv_quantize_bit_exact);
+    here K/V come from the GEMV, whose ~1e-5 relative rounding difference can
+    move a value across a quantization boundary (one step = range/(2^bits-1)),
+    so the logit bound is the float-KV bound plus the effect of such flips."""
     b = nb.CudaBackend(device=0, kv_bits=bits)
     e = nb.InferenceEngine(b)
     e.load_model(tiny_path)
@@ -94,10 +98,14 @@ def test_tiny_packed_kv(nb, oracle, tiny_path, bits):
     p = prompt(2, 40, 4096)
     ref = m.prefill(p)
     got, tok = e.prefill(p)
-    assert np.max(np.abs(got - ref)) < LOGIT_TOL
-    assert e.generate(p, 16) == m.generate(p, 16)
+    err = float(np.max(np.abs(got - ref)))
+    print(f"packed kv {bits}: max |logit diff| = {err:.3e}")
+    assert err < 2e-2, err
+    assert tok == oracle.greedy(ref)
+    gen, refgen = e.generate(p, 16), m.generate(p, 16)
     e.close()
     b.close()
+    assert gen == refgen
 
 
 def test_kv_overflow_is_an_error_not_a_shift(nb, tiny_path):

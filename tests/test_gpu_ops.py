@@ -148,9 +148,12 @@ def test_matmul_op(backend, transpose_b):
 def test_rope_and_argmax_ops(backend, oracle):
     rng = np.random.default_rng(53)
     x = rng.standard_normal(8 * 128).astype(np.float32)
+    # the generic op evaluates powf/cosf/sinf on the device (the decode path uses
+    # a host table with glibc's values); at position 511 the angles reach 511 rad
+    # and the two libms differ by a few ulp
     for pos in (0, 1, 511):
         got = backend.rope(x, pos, 128, 500000.0)
-        assert np.max(np.abs(got - oracle.rope_single(x, pos, 128, 500000.0))) < 1e-5
+        assert np.max(np.abs(got - oracle.rope_single(x, pos, 128, 500000.0))) < 1e-4
     logits = rng.standard_normal(128256).astype(np.float32)
     assert backend.argmax(logits) == oracle.greedy(logits)
     tie = np.array([1.0, 3.0, 3.0, np.nan, np.inf], np.float32)
@@ -181,3 +184,20 @@ def test_dequantize_truncated_payload_is_an_error(backend, oracle, nb):
     with pytest.raises(nb.NexusError) as e:
         backend.dequantize(nb.Q4_K, q[:-1], 512)
     assert e.value.code == nb._lib.NEXUS_E_TRUNCATED
+
+
+@pytest.mark.parametrize("bits", [2, 3, 4, 6, 8])
+def test_kv_quantize_bit_exact(backend, oracle, bits):
+    """Device packing of one KV vector equals PackedKvBuffer::add bit for bit."""
+    rng = np.random.default_rng(60 + bits)
+    for n, scale in ((1024, 1.0), (128, 0.05), (8, 3.0)):
+        v = (rng.standard_normal(n) * scale).astype(np.float32)
+        data, mn, sc = backend.kv_quantize(v, bits)
+        ref = oracle.PackedKv(bits, n, 1)
+        ref.add(0, v)
+        rdata, rmin, rscale = ref.raw(1)
+        assert np.array_equal(data, rdata)
+        assert np.float32(mn) == rmin[0] and np.float32(sc) == rscale[0]
+    const = np.full(64, 0.75, np.float32)  # range <= 1e-8 -> scale 1.0
+    data, mn, sc = backend.kv_quantize(const, bits)
+    assert sc == 1.0 and np.float32(mn) == np.float32(0.75) and not data.any()
