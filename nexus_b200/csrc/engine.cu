@@ -141,6 +141,16 @@ static cudaError_t alloc_split_scratch(size_t n, float **part, size_t *part_floa
 // ---------------------------------------------------------------------------
 // backend
 // ---------------------------------------------------------------------------
+// Internal accessors for other translation units of the library.
+int nexus_backend_stream_device(nexus_cuda_backend *b, cudaStream_t *stream, int *device) {
+    if (!b) return NEXUS_E_INVALID;
+    *stream = b->stream;
+    *device = b->device;
+    return NEXUS_OK;
+}
+
+int nexus_backend_fail(nexus_cuda_backend *b, int code, const char *msg) { return set_err(b, code, msg); }
+
 extern "C" void nexus_cuda_config_default(nexus_cuda_config *cfg) {
     memset(cfg, 0, sizeof(*cfg));
     cfg->device = 0;

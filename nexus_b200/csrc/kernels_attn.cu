@@ -77,6 +77,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attn(AttnParams p) {
         pdl_launch_dependents();
         pdl_wait();
     }
+    // q and the step descriptor are independent loads: issue both first
+    float qv[G][VEC];
+#pragma unroll
+    for (int g = 0; g < G; g++)
+        load_f32<VEC>(p.q + (size_t)t * p.hq * D + (size_t)(h * G + g) * D + lane * VEC, qv[g]);
     const DevSeq sq = p.seqs[t];
     const uint32_t sid = p.seq_ids[t];
     const int seq_len = (int)sq.seq_len;
@@ -84,11 +89,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attn(AttnParams p) {
     if (split >= nsplit) return;
     const int per = (seq_len + nsplit - 1) / nsplit;
     const int t0 = split * per, t1 = min(seq_len, t0 + per);
-
-    float qv[G][VEC];
-#pragma unroll
-    for (int g = 0; g < G; g++)
-        load_f32<VEC>(p.q + (size_t)t * p.hq * D + (size_t)(h * G + g) * D + lane * VEC, qv[g]);
     float m[G], l[G], o[G][VEC];
 #pragma unroll
     for (int g = 0; g < G; g++) {
@@ -208,11 +208,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attn(AttnParams p) {
     __syncthreads();
     if (!is_last) return;
     __threadfence();
-    // slice merge: softmax weights of every (slice, head) in parallel ...
+    // slice merge: maxima and sums of every (slice, head) in parallel ...
     __shared__ float sm_M[G], sm_L[G];
+    __shared__ float sm_ls[64][G];
     for (int idx = threadIdx.x; idx < nsplit * G; idx += blockDim.x) {
         const int s = idx / G, g = idx % G;
         sm_w[s][g] = __ldcg(part + ((size_t)s * G + g) * stride + D);
+        sm_ls[s][g] = __ldcg(part + ((size_t)s * G + g) * stride + D + 1);
     }
     __syncthreads();
     if (threadIdx.x < G) {
@@ -223,7 +225,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attn(AttnParams p) {
         for (int s = 0; s < nsplit; s++) {
             const float ms = sm_w[s][g];
             const float wt = ms == -INFINITY ? 0.0f : expf(ms - M);
-            L += wt * __ldcg(part + ((size_t)s * G + g) * stride + D + 1);
+            L += wt * sm_ls[s][g];
             sm_w[s][g] = wt;
         }
         sm_M[g] = M;

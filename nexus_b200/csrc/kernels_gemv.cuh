@@ -17,20 +17,20 @@
 // representation of x (|error| <= max|x|/65534 per super-block), which keeps
 // per-output relative error near 1e-5, far inside the 1e-3 parity bound.
 //
-// Parallel layout.  The tile matrix is a sequence of items (row group g,
-// super-block s) in group-major order, and that sequence is contiguous in
-// memory.  Each CTA (one per SM) owns one contiguous run of items ("stream-K")
-// and streams its bytes into a shared-memory ring with TMA bulk copies
-// (cp.async.bulk + mbarrier transaction counts).  The first ring stages are
-// issued before griddepcontrol.wait, so under programmatic dependent launch a
-// GEMV streams its first weights while the previous kernel is still running.
-// Lane i of every warp owns row 32g+i; the warps of a CTA take the items of a
-// ring stage (P warps share an item, each taking 1/P of its blocks); warp 0
-// sums item partials in item order and applies the epilogue when a row group
-// ends.  A row group split between CTAs is finished by the last of them to
-// arrive (self-resetting counter), which adds the per-CTA partials in CTA
-// order -- deterministic, no float atomics.  The input is prepared (16-bit
-// quantization, RMSNorm folded into the per-super-block scale) once per CTA.
+// Parallel layout.  An item is one (row group g of 32 rows, super-block s)
+// tile: C*512 contiguous bytes (tiles.cuh).  Warps form teams of S warps; a
+// team owns whole row groups and its S warps split each group's super-blocks.
+// Every warp streams its own item sequence -- across the row groups its team
+// owns -- through a private two-slot shared-memory ring filled by TMA bulk
+// copies (cp.async.bulk + mbarrier), so a warp always has the next item in
+// flight and no CTA-wide barrier sits in the main loop.  Lane i owns row
+// 32g+i.  The S partial sums of a row group meet in shared memory behind a
+// named barrier of the team, and the team's first warp adds them in warp
+// order and applies the epilogue (deterministic).  CTAs are persistent, one
+// per SM, and prepare the input (16-bit quantization, RMSNorm folded into
+// the per-super-block scale) once.  The first ring slots are filled before
+// griddepcontrol.wait, so under programmatic dependent launch a GEMV streams
+// weights while the previous kernel finishes.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -341,17 +341,15 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, int g, int t,
 }
 
 
-// Ring geometry per format: items (super-block tiles) per stage and warps per item.
+
 template <int FMT>
 struct Ring {
     static constexpr int C = Fmt<FMT>::C;
     static constexpr int ITEM_BYTES = C * 512;
-    // ~18-20 KB per stage, 4 stages (about 74 KB in flight per CTA)
-    static constexpr int IPS = FMT == 8 ? 2 : FMT == 10 ? 8 : 4;
-    static constexpr int W = 8;
-    static constexpr int P = W / IPS;  // warps sharing one item
-    static constexpr int NST = 4;
-    static constexpr int STAGE_BYTES = IPS * ITEM_BYTES;
+    static constexpr int AUX_BYTES = Fmt<FMT>::AUX ? 128 : 0;
+    static constexpr int W = 8;        // warps per CTA
+    static constexpr int NST = 2;      // ring slots per warp
+    static constexpr int SLOT_BYTES = ITEM_BYTES + AUX_BYTES;
 };
 
 constexpr unsigned kMbarSpinLimit = 1u << 20;
@@ -359,47 +357,56 @@ constexpr unsigned kMbarSpinLimit = 1u << 20;
 template <int FMT, int M, int EPI>
 __global__ void __launch_bounds__(256, 1) k_gemv(GemvParams p) {
     using R = Ring<FMT>;
-    constexpr int W = R::W, IPS = R::IPS, P = R::P, NST = R::NST;
+    constexpr int W = R::W, NST = R::NST;
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ unsigned long long full[NST];
-    __shared__ int s_ok;
+    __shared__ unsigned long long full[W][NST];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int k = p.k, n_sb = k >> 8;
     const int groups = (p.n + 31) / 32;
-    const long long T = (long long)groups * n_sb;
-    const int G = gridDim.x, c = blockIdx.x;
-    const long long i0 = (long long)c * T / G, i1 = (long long)(c + 1) * T / G;
-    const int nstages = (int)((i1 - i0 + IPS - 1) / IPS);
+    const int S = p.ksplit;             // warps per team (1, 2, 4 or 8)
+    const int teams = W / S;
+    const int team = warp / S, r = warp % S;
+    const int total_teams = gridDim.x * teams;
+    const int gteam = blockIdx.x * teams + team;
+    // this warp's super-blocks of every group: [s0, s1)
+    const int per = (n_sb + S - 1) / S;
+    const int s0 = min(n_sb, r * per), s1 = min(n_sb, s0 + per);
+    const int n_item = s1 - s0;
+    const int my_groups = gteam < groups ? (groups - gteam + total_teams - 1) / total_teams : 0;
+    const int n_total = my_groups * n_item;   // items this warp streams
 
-    uint8_t *ring = smem;                                              // NST * STAGE_BYTES
-    uint32_t *aux_ring = reinterpret_cast<uint32_t *>(ring + NST * R::STAGE_BYTES);  // NST * IPS * 32 (Q2_K)
-    uint8_t *xs = ring + NST * R::STAGE_BYTES + (Fmt<FMT>::AUX ? NST * IPS * 128 : 0);
+    uint8_t *ring = smem + (size_t)warp * NST * R::SLOT_BYTES;
+    uint8_t *xs = smem + (size_t)W * NST * R::SLOT_BYTES;
     const size_t tok_bytes = tok_smem_bytes(k);
-    float *red = reinterpret_cast<float *>(xs + tok_bytes * M);        // [W][M][32]
-    float *misc = red + W * M * 32;                                    // [W*M]
+    float *red = reinterpret_cast<float *>(xs + tok_bytes * M);      // [W][2][M][32]
+    float *misc = red + W * 2 * M * 32;                              // [W*M]
 
-    auto issue = [&](int st) {  // one thread: stage st into ring slot st % NST
-        const long long a = i0 + (long long)st * IPS;
-        const long long b = min(i1, a + IPS);
-        const unsigned bytes = (unsigned)((b - a) * R::ITEM_BYTES);
-        const unsigned abytes = Fmt<FMT>::AUX ? (unsigned)((b - a) * 128) : 0u;
-        unsigned long long *bar = &full[st % NST];
-        mbar_expect_tx(bar, bytes + abytes);
-        tma_load_1d(ring + (size_t)(st % NST) * R::STAGE_BYTES,
-                    reinterpret_cast<const uint8_t *>(p.w_main) + (size_t)a * R::ITEM_BYTES, bytes, bar);
+    auto item_addr = [&](int j, long long &item) {
+        const int gi = j / n_item, si = j % n_item;
+        const long long g = (long long)gteam + (long long)gi * total_teams;
+        item = g * n_sb + s0 + si;
+    };
+    auto issue = [&](int j) {  // lane 0: item j of this warp into slot j % NST
+        long long item;
+        item_addr(j, item);
+        unsigned long long *bar = &full[warp][j % NST];
+        uint8_t *dst = ring + (size_t)(j % NST) * R::SLOT_BYTES;
+        mbar_expect_tx(bar, R::ITEM_BYTES + R::AUX_BYTES);
+        tma_load_1d(dst, reinterpret_cast<const uint8_t *>(p.w_main) + (size_t)item * R::ITEM_BYTES, R::ITEM_BYTES,
+                    bar);
         if constexpr (Fmt<FMT>::AUX)
-            tma_load_1d(aux_ring + (size_t)(st % NST) * IPS * 32,
-                        reinterpret_cast<const uint8_t *>(p.w_aux) + (size_t)a * 128, abytes, bar);
+            tma_load_1d(dst + R::ITEM_BYTES, reinterpret_cast<const uint8_t *>(p.w_aux) + (size_t)item * 128, 128,
+                        bar);
     };
 
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < NST; i++) mbar_init(&full[i], 1);
+    if (lane == 0) {
+        for (int i = 0; i < NST; i++) mbar_init(&full[warp][i], 1);
         mbar_init_fence();
     }
-    __syncthreads();
-    // Stream the first stages of weights before waiting on the previous grid.
-    if (threadIdx.x == 0)
-        for (int st = 0; st < NST && st < nstages; st++) issue(st);
+    __syncwarp();
+    // Stream the first items before waiting on the previous grid.
+    if (lane == 0)
+        for (int j = 0; j < NST && j < n_total; j++) issue(j);
     if (p.pdl) {
         pdl_launch_dependents();
         pdl_wait();
@@ -436,74 +443,36 @@ __global__ void __launch_bounds__(256, 1) k_gemv(GemvParams p) {
         __syncthreads();
     }
 
-    // warp 0 state: running sum of the current row group
-    int cur_g = -1;
-    float gacc[M];
+    // All warps of a team run the same number of groups, so the team barrier
+    // below is reached the same number of times by each of them.
+    int j = 0;
+    for (int gi = 0; gi < my_groups; gi++) {
+        const int g = gteam + gi * total_teams;
+        float acc[M];
 #pragma unroll
-    for (int t = 0; t < M; t++) gacc[t] = 0.0f;
-
-    auto flush = [&](int g) {  // warp 0: row group g is complete in this CTA's range
-        const long long g0 = (long long)g * n_sb, g1 = g0 + n_sb;
-        if (g0 >= i0 && g1 <= i1) {
-#pragma unroll
-            for (int t = 0; t < M; t++) gemv_epilogue<EPI>(p, g, t, lane, gacc[t]);
-            return;
-        }
-        // shared with neighbouring CTAs: owner(i) = floor(((i+1)G - 1) / T)
-        const int cf = (int)(((g0 + 1) * G - 1) / T), cl = (int)((g1 * G - 1) / T);
-        const int slot = c - cf, count = cl - cf + 1;
-        const size_t npad = (size_t)groups * 32;
-        const int row = 32 * g + lane;
-#pragma unroll
-        for (int t = 0; t < M; t++) p.part[((size_t)slot * M + t) * npad + row] = gacc[t];
-        __threadfence();
-        __syncwarp();
-        unsigned last = 0;
-        if (lane == 0) {
-            const unsigned prev = atomicAdd(&p.counters[g], 1u);
-            last = prev == (unsigned)(count - 1);
-            if (last) p.counters[g] = 0u;
-        }
-        if (__shfl_sync(0xffffffffu, last, 0)) {
-            __threadfence();
-#pragma unroll
-            for (int t = 0; t < M; t++) {
-                float sum = 0.0f;
-                for (int sl = 0; sl < count; sl++) sum += __ldcg(p.part + ((size_t)sl * M + t) * npad + row);
-                gemv_epilogue<EPI>(p, g, t, lane, sum);
-            }
-        }
-    };
-
-    const int it = warp / P, part = warp % P;
-    for (int st = 0; st < nstages; st++) {
-        // wait for the stage's bytes (bounded: a copy that never lands is reported)
-        bool ok = true;
-        {
+        for (int t = 0; t < M; t++) acc[t] = 0.0f;
+        for (int si = 0; si < n_item; si++, j++) {
+            const int slot = j % NST;
+            // bounded wait for the item's bytes: a copy that never lands is reported
             unsigned n = 0;
-            while (!mbar_try_wait(&full[st % NST], (unsigned)((st / NST) & 1))) {
+            bool ok = true;
+            while (!mbar_try_wait(&full[warp][slot], (unsigned)((j / NST) & 1))) {
                 if (++n > kMbarSpinLimit) {
                     ok = false;
                     break;
                 }
             }
-        }
-        if (!__syncthreads_and(ok)) {
-            if (threadIdx.x == 0 && p.err) atomicExch(p.err, 1);
-            return;
-        }
-        const long long a = i0 + (long long)st * IPS;
-        const int nit = (int)min((long long)IPS, i1 - a);
-        float v[M];
-#pragma unroll
-        for (int t = 0; t < M; t++) v[t] = 0.0f;
-        if (it < nit) {
-            const long long item = a + it;
-            const int s_sb = (int)(item % n_sb);
-            const uint4 *cbase = reinterpret_cast<const uint4 *>(ring + (size_t)(st % NST) * R::STAGE_BYTES) +
-                                 (size_t)it * R::C * 32 + lane;
+            if (!ok) {
+                if (lane == 0 && p.err) atomicExch(p.err, 1);
+                acc[0] = __int_as_float(0x7fc00000);  // NaN marks the row group as failed
+                j = n_total;                            // stop issuing
+                break;
+            }
+            const int s_sb = s0 + si;
+            const uint4 *cbase = reinterpret_cast<const uint4 *>(ring + (size_t)slot * R::SLOT_BYTES) + lane;
             uint32_t auxw = 0;
-            if constexpr (Fmt<FMT>::AUX) auxw = aux_ring[(size_t)(st % NST) * IPS * 32 + it * 32 + lane];
+            if constexpr (Fmt<FMT>::AUX)
+                auxw = reinterpret_cast<const uint32_t *>(ring + (size_t)slot * R::SLOT_BYTES + R::ITEM_BYTES)[lane];
 #pragma unroll
             for (int t = 0; t < M; t++) {
                 const uint8_t *tb = xs + tok_bytes * t;
@@ -512,49 +481,50 @@ __global__ void __launch_bounds__(256, 1) k_gemv(GemvParams p) {
                 xsb.zl = reinterpret_cast<const uint4 *>(tb + k) + 16 * s_sb;
                 xsb.sz = reinterpret_cast<const int *>(tb + 2 * k) + 16 * s_sb;
                 xsb.u = reinterpret_cast<const float *>(tb + 2 * k + 4 * (k / 16))[s_sb];
-                v[t] = sb_dot<FMT, P>(cbase, auxw, xsb, part);
+                acc[t] += sb_dot<FMT, 1>(cbase, auxw, xsb, 0);
             }
+            // every lane is done with the slot: refill it with item j + NST
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0 && j + NST < n_total) issue(j + NST);
         }
+        if (S == 1) {
 #pragma unroll
-        for (int t = 0; t < M; t++) red[(warp * M + t) * 32 + lane] = v[t];
-        fence_proxy_async_smem();
-        __syncthreads();
-        // every warp is done with ring slot st % NST: refill it
-        if (threadIdx.x == 0 && st + NST < nstages) issue(st + NST);
-        if (warp == 0) {
-            for (int j = 0; j < nit; j++) {
-                const int g = (int)((a + j) / n_sb);
-                if (g != cur_g) {
-                    if (cur_g >= 0) flush(cur_g);
-                    cur_g = g;
+            for (int t = 0; t < M; t++) gemv_epilogue<EPI>(p, g, t, lane, acc[t]);
+        } else {
+            // team reduction: partials meet in shared memory, the team's first warp adds them in order
+            float *tred = red + (size_t)(team * S) * 2 * M * 32;   // [S][2][M][32]
+            const int buf = gi & 1;
 #pragma unroll
-                    for (int t = 0; t < M; t++) gacc[t] = 0.0f;
-                }
+            for (int t = 0; t < M; t++) tred[((r * 2 + buf) * M + t) * 32 + lane] = acc[t];
+            asm volatile("bar.sync %0, %1;" ::"r"(1 + team), "r"(S * 32) : "memory");
+            if (r == 0) {
 #pragma unroll
                 for (int t = 0; t < M; t++) {
-                    float sv = 0.0f;
-#pragma unroll
-                    for (int q = 0; q < P; q++) sv += red[((j * P + q) * M + t) * 32 + lane];
-                    gacc[t] += sv;
+                    float tot = 0.0f;
+                    for (int q = 0; q < S; q++) tot += tred[((q * 2 + buf) * M + t) * 32 + lane];
+                    gemv_epilogue<EPI>(p, g, t, lane, tot);
                 }
             }
         }
-        __syncthreads();
     }
-    if (warp == 0 && cur_g >= 0) flush(cur_g);
 }
 
 // ---------------------------------------------------------------------------
+template <int FMT>
+static size_t gemv_smem_bytes(int k, int m) {
+    using R = Ring<FMT>;
+    return (size_t)R::W * R::NST * R::SLOT_BYTES + tok_smem_bytes(k) * m + (size_t)4 * R::W * 2 * m * 32 +
+           (size_t)4 * R::W * m;
+}
+
 template <int FMT, int M, int EPI>
 static cudaError_t launch_fmt_m_epi(const GemvParams &pin, cudaStream_t st) {
     using R = Ring<FMT>;
     GemvParams p = pin;
     const int groups = (p.n + 31) / 32;
     const int n_sb = p.k / 256;
-    const long long T = (long long)groups * n_sb;
-    const size_t tok_bytes = tok_smem_bytes(p.k);
-    const size_t smem = (size_t)R::NST * R::STAGE_BYTES + (Fmt<FMT>::AUX ? (size_t)R::NST * R::IPS * 128 : 0) +
-                        tok_bytes * M + (size_t)4 * R::W * M * 32 + (size_t)4 * R::W * M;
+    const size_t smem = gemv_smem_bytes<FMT>(p.k, M);
     auto fn = k_gemv<FMT, M, EPI>;
     if (smem > 220 * 1024) return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -563,20 +533,21 @@ static cudaError_t launch_fmt_m_epi(const GemvParams &pin, cudaStream_t st) {
     cudaGetDevice(&dev);
     static int sm_count[16] = {};
     if (dev < 16 && sm_count[dev] == 0) cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
-    int grid = dev < 16 && sm_count[dev] ? sm_count[dev] : 148;
-    if ((long long)grid > T) grid = (int)T;
-    // A row group spans at most ceil(n_sb / floor(T/grid)) + 1 CTAs; their
-    // partials need scratch slots and the group a counter.
-    auto max_share = [&](int gr) -> long long {
-        const long long per = T / gr;
-        return per >= n_sb ? 2 : (n_sb + per - 1) / per + 1;
-    };
-    while (grid > 1 && (!p.part || !p.counters || groups > p.counter_slots ||
-                        (size_t)max_share(grid) * M * groups * 32 > p.part_floats)) {
-        if (T % grid == 0 && (T / grid) % n_sb == 0) break;  // every CTA owns whole row groups
-        grid = grid > 8 ? grid - grid / 8 : grid - 1;
-    }
-    if (grid < 1) grid = 1;
+    const int sms = dev < 16 && sm_count[dev] ? sm_count[dev] : 148;
+    // Team size: the smallest that gives every warp of the GPU a row group,
+    // keeping at least two super-blocks per warp.  One CTA per team set of
+    // row groups while they all fit at once (no tail imbalance); beyond that
+    // the CTAs are persistent.
+    int S = 1;
+    while (S < R::W && (long long)groups * S < (long long)sms * R::W && n_sb >= 2 * S) S *= 2;
+    p.ksplit = S;
+    const int teams = R::W / S;
+    int per_sm = 1;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, R::W * 32, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) per_sm = 1;
+    int grid = (groups + teams - 1) / teams;
+    if (grid > per_sm * sms) grid = per_sm * sms;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(R::W * 32);
@@ -602,8 +573,30 @@ static cudaError_t launch_epi(const GemvParams &p, cudaStream_t st) {
     }
 }
 
+// Tokens [t0, t0 + m) of a batch: per-token pointers move, shared ones stay.
+static GemvParams token_slice(const GemvParams &p, int t0, int m) {
+    GemvParams q = p;
+    q.m = m;
+    q.x = p.x + (size_t)t0 * p.x_stride;
+    if (p.y) q.y = p.y + (size_t)t0 * p.y_stride;
+    if (p.seqs) q.seqs = p.seqs + t0;
+    if (p.qkv.seqs) q.qkv.seqs = p.qkv.seqs + t0;
+    if (p.qkv.seq_ids) q.qkv.seq_ids = p.qkv.seq_ids + t0;
+    if (p.qkv.q_out) q.qkv.q_out = p.qkv.q_out + (size_t)t0 * p.qkv.hq * p.qkv.head_dim;
+    if (p.qkv.kv_scratch) q.qkv.kv_scratch = p.qkv.kv_scratch + (size_t)t0 * 2 * p.qkv.hkv * p.qkv.head_dim;
+    return q;
+}
+
 template <int FMT>
 cudaError_t launch_gemv_fmt(const GemvParams &p, cudaStream_t st) {
+    // A batch whose prepared inputs do not fit next to the weight rings runs
+    // as two launches of half the tokens.
+    if (p.m > 1 && gemv_smem_bytes<FMT>(p.k, p.m) > 220 * 1024) {
+        const int h = p.m / 2;
+        cudaError_t e = launch_gemv_fmt<FMT>(token_slice(p, 0, h), st);
+        if (e != cudaSuccess) return e;
+        return launch_gemv_fmt<FMT>(token_slice(p, h, p.m - h), st);
+    }
     switch (p.m) {
     case 1: return launch_epi<FMT, 1>(p, st);
     case 2: return launch_epi<FMT, 2>(p, st);

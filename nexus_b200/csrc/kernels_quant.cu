@@ -211,7 +211,9 @@ cudaError_t launch_dequant_tiles(int fmt, const uint4 *main, const uint32_t *aux
 // ---------------------------------------------------------------------------
 
 // Token embedding row (src/engine/mod.rs:1090-1097): row token % rows, decoded
-// with the reference formula.  Also clears the step's argmax accumulator.
+// with the reference formula.  One thread per block of the row: the block's
+// bytes are loaded first (independent loads), then decoded.  Also clears the
+// step's argmax accumulator.
 __global__ void k_embed(EmbedParams p) {
     const int t = blockIdx.x;
     if (p.pdl) {
@@ -221,22 +223,22 @@ __global__ void k_embed(EmbedParams p) {
     const uint32_t token = p.seqs[t].token;
     const size_t row = p.vocab_rows ? (size_t)token % p.vocab_rows : 0;
     const int be = block_elems(p.fmt), bb = block_bytes(p.fmt);
-    const uint8_t *__restrict__ table = p.table;
     float *__restrict__ out = p.out + (size_t)t * p.hidden;
-    // decode everything first, then store (independent loads in flight)
-    constexpr int kPer = 16;
-    float v[kPer];
-    for (int base = threadIdx.x; base < p.hidden; base += blockDim.x * kPer) {
-#pragma unroll
-        for (int j = 0; j < kPer; j++) {
-            const int i = base + j * (int)blockDim.x;
-            const size_t e = row * (size_t)p.hidden + (i < p.hidden ? i : 0);
-            v[j] = dequant_elem(p.fmt, table + (e / be) * bb, (int)(e % be));
+    const size_t e0 = row * (size_t)p.hidden;
+    if (e0 % be == 0 && p.hidden % be == 0) {
+        const int nblk = p.hidden / be;
+        const uint8_t *__restrict__ base = p.table + (e0 / be) * bb;
+        for (int b = threadIdx.x; b < nblk; b += blockDim.x) {
+            uint8_t blk[144];
+            const uint8_t *src = base + (size_t)b * bb;
+#pragma unroll 16
+            for (int i = 0; i < bb; i++) blk[i] = src[i];
+            for (int j = 0; j < be; j++) out[b * be + j] = dequant_elem(p.fmt, blk, j);
         }
-#pragma unroll
-        for (int j = 0; j < kPer; j++) {
-            const int i = base + j * (int)blockDim.x;
-            if (i < p.hidden) out[i] = v[j];
+    } else {
+        for (int i = threadIdx.x; i < p.hidden; i += blockDim.x) {
+            const size_t e = e0 + i;
+            out[i] = dequant_elem(p.fmt, p.table + (e / be) * bb, (int)(e % be));
         }
     }
     if (threadIdx.x == 0) p.seqs[t].best = 0ull;
