@@ -248,6 +248,24 @@ typedef struct {
 int nexus_cuda_profile_decode(nexus_cuda_model *m, uint32_t seq_id, uint32_t token, uint32_t steps,
                               nexus_kernel_profile *out, int max_out, int *n_out);
 
+/* GQA decode attention that allocates nothing (no counterpart in the
+ * reference).  For callers that must not allocate device memory while they
+ * run -- inside a CUDA stream capture, in serving loops that cannot take the
+ * device-wide synchronization of cudaMalloc/cudaFree, or in embedders whose
+ * device memory comes from their own pool.  Same computation as
+ * nexus_cuda_execute with NEXUS_OP_ATTENTION on device pointers: q is
+ * num_q_heads*head_dim floats, k/v are seq_len rows of num_kv_heads*head_dim
+ * floats, out is num_q_heads*head_dim floats, all device memory owned by the
+ * caller; scale 0 means 1/sqrt(head_dim).  Its scratch lives in one fixed
+ * 1 MiB device array per GPU, held until the process exits; shapes needing
+ * more return NEXUS_E_INVALID.  All calls share that array: calls that
+ * overlap on the GPU race, so order them on one stream.  The first call on a
+ * device looks up the array's address and should come before any stream
+ * capture.  Synchronous on the backend's stream. */
+int nexus_cuda_attention_noalloc(nexus_cuda_backend *b, const float *q_dev, const float *k_dev,
+                                 const float *v_dev, float *out_dev, size_t num_q_heads,
+                                 size_t num_kv_heads, size_t head_dim, size_t seq_len, float scale);
+
 /* ======================================================================== */
 /* Host utilities (the reference's converter and quantizers)                 */
 /* ======================================================================== */

@@ -116,6 +116,8 @@ SIGNATURES = [
     ("nexus_cuda_last_step_ms", C.c_int, [P, C.POINTER(C.c_float)]),
     ("nexus_cuda_profile_decode", C.c_int, [P, C.c_uint32, C.c_uint32, C.c_uint32, C.POINTER(KernelProfile),
                                             C.c_int, C.POINTER(C.c_int)]),
+    ("nexus_cuda_attention_noalloc", C.c_int, [P, P, P, P, P, C.c_size_t, C.c_size_t, C.c_size_t, C.c_size_t,
+                                               C.c_float]),
     ("nexus_quantize_host", C.c_size_t, [C.c_int, P, C.c_size_t, P]),
     ("nexus_format_bytes", C.c_size_t, [C.c_int, C.c_size_t]),
     ("nexus_synth_model_write", C.c_int, [C.c_char_p, C.POINTER(SynthConfig)]),

@@ -33,6 +33,7 @@ UNITS = {
     "kernels_attn.cu": [],
     "kernels_misc.cu": [],
     "engine.cu": [],
+    "noalloc.cu": [],
 }
 CXX_UNITS = ["host.cpp"]
 
