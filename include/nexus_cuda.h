@@ -173,6 +173,12 @@ int nexus_cuda_qmatvec_host(nexus_cuda_qweight *w, const float *x, size_t m, flo
 int nexus_cuda_qweight_dequantize(nexus_cuda_qweight *w, float *out);
 /* Device bytes of the repacked weight (the GEMV's algorithmic weight traffic). */
 size_t nexus_cuda_qweight_bytes(const nexus_cuda_qweight *w);
+/* Times `iters` GEMV launches on device buffers: each launch is bracketed by
+ * CUDA events on the backend stream, and flush_bytes of a scratch buffer are
+ * written between launches so every launch starts with a cold L2.  avg_ms is
+ * the mean launch time. */
+int nexus_cuda_qmatvec_bench(nexus_cuda_qweight *w, const float *x_dev, size_t m, float *y_dev, int iters,
+                             size_t flush_bytes, float *avg_ms);
 
 /* ======================================================================== */
 /* Engine-level calls: the real hot boundary.  InferenceEngine               */

@@ -12,7 +12,9 @@ import os
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-LIB_PATH = HERE / "libnexus_cuda.so"
+# NEXUS_CUDA_LIB selects another build of the library (e.g. one built with
+# different kernel parameters by nexus_b200/build.py --out ...)
+LIB_PATH = Path(os.environ.get("NEXUS_CUDA_LIB", str(HERE / "libnexus_cuda.so")))
 
 # status codes
 NEXUS_OK = 0
@@ -104,6 +106,7 @@ SIGNATURES = [
     ("nexus_cuda_qmatvec_host", C.c_int, [P, P, C.c_size_t, P]),
     ("nexus_cuda_qweight_dequantize", C.c_int, [P, P]),
     ("nexus_cuda_qweight_bytes", C.c_size_t, [P]),
+    ("nexus_cuda_qmatvec_bench", C.c_int, [P, P, C.c_size_t, P, C.c_int, C.c_size_t, C.POINTER(C.c_float)]),
     ("nexus_cuda_model_load", C.c_int, [P, C.c_char_p, C.POINTER(P)]),
     ("nexus_cuda_model_free", C.c_int, [P]),
     ("nexus_cuda_model_get_info", C.c_int, [P, C.POINTER(ModelInfo)]),
@@ -131,7 +134,7 @@ def load() -> C.CDLL:
     global _lib
     if _lib is not None:
         return _lib
-    if os.environ.get("NEXUS_NO_BUILD") != "1":
+    if os.environ.get("NEXUS_NO_BUILD") != "1" and "NEXUS_CUDA_LIB" not in os.environ:
         from . import build as _build
         _build.build()
     if not LIB_PATH.exists():

@@ -64,35 +64,49 @@ def up_to_date() -> bool:
     return all(p.stat().st_mtime <= t for p in sources() + [Path(__file__)])
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    if not force and up_to_date():
+def build(force: bool = False, verbose: bool = False, out: Path | None = None, build_dir: Path | None = None,
+          extra_cu_flags: list[str] | None = None) -> Path:
+    """Compile the library (into `out`, default nexus_b200/libnexus_cuda.so);
+    extra_cu_flags are added to every CUDA unit (e.g. -DNX_GEMV_WARPS=16)."""
+    lib_out = Path(out) if out else LIB
+    bdir = Path(build_dir) if build_dir else BUILD
+    if out is None and not force and not extra_cu_flags and up_to_date():
         return LIB
-    BUILD.mkdir(exist_ok=True)
+    bdir.mkdir(parents=True, exist_ok=True)
     nv = nvcc()
     jobs = []
     objs = []
     for unit, extra in UNITS.items():
-        obj = BUILD / (unit + ".o")
+        obj = bdir / (unit + ".o")
         objs.append(obj)
-        jobs.append(([nv, "-c", str(CSRC / unit), "-o", str(obj)] + CU_COMMON + extra, BUILD / (unit + ".log")))
+        jobs.append(([nv, "-c", str(CSRC / unit), "-o", str(obj)] + CU_COMMON + extra + list(extra_cu_flags or []),
+                     bdir / (unit + ".log")))
     for unit in CXX_UNITS:
-        obj = BUILD / (unit + ".o")
+        obj = bdir / (unit + ".o")
         objs.append(obj)
         jobs.append((["g++", "-c", str(CSRC / unit), "-o", str(obj), "-O2", "-std=c++17", "-fPIC",
-                      "-ffp-contract=off", "-fno-fast-math", "-I/usr/local/cuda/include"], BUILD / (unit + ".log")))
+                      "-ffp-contract=off", "-fno-fast-math", "-I/usr/local/cuda/include"], bdir / (unit + ".log")))
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 4)) as ex:
         futs = [ex.submit(_run, cmd, log) for cmd, log in jobs]
         for f in futs:
             f.result()
-    tmp = LIB.with_suffix(".so.tmp")
-    _run([nv, "-shared", "-o", str(tmp)] + [str(o) for o in objs] + ARCH + ["-lpthread"], BUILD / "link.log")
-    os.replace(tmp, LIB)
+    tmp = lib_out.with_suffix(".so.tmp")
+    _run([nv, "-shared", "-o", str(tmp)] + [str(o) for o in objs] + ARCH + ["-lpthread"], bdir / "link.log")
+    os.replace(tmp, lib_out)
     if verbose:
         for unit in UNITS:
-            print((BUILD / (unit + ".log")).read_text())
-    return LIB
+            print((bdir / (unit + ".log")).read_text())
+    return lib_out
 
 
 if __name__ == "__main__":
-    build(force="--force" in sys.argv, verbose="-v" in sys.argv)
-    print(LIB)
+    import argparse
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("-v", action="store_true")
+    ap.add_argument("--out", default=None, help="output library path")
+    ap.add_argument("--build-dir", default=None)
+    ap.add_argument("-D", action="append", default=[], help="extra CUDA define, e.g. -D NX_GEMV_WARPS=16")
+    a = ap.parse_args()
+    print(build(force=a.force, verbose=a.v, out=a.out, build_dir=a.build_dir, extra_cu_flags=[f"-D{d}" for d in a.D]))

@@ -645,6 +645,38 @@ extern "C" int nexus_cuda_qmatvec_device(nexus_cuda_qweight *w, const float *x_d
     return NEXUS_OK;
 }
 
+extern "C" int nexus_cuda_qmatvec_bench(nexus_cuda_qweight *w, const float *x_dev, size_t m, float *y_dev, int iters,
+                                        size_t flush_bytes, float *avg_ms) {
+    if (!w || !x_dev || !y_dev || !avg_ms || iters < 1) return set_err(w ? w->b : nullptr, NEXUS_E_INVALID, "bad argument");
+    nexus_cuda_backend *b = w->b;
+    cudaSetDevice(b->device);
+    cudaStream_t st = b->stream;
+    void *flush = nullptr;
+    if (flush_bytes) NX_CUDA(b, cudaMalloc(&flush, flush_bytes));
+    std::vector<cudaEvent_t> ev(2 * (size_t)iters);
+    for (auto &e : ev) cudaEventCreate(&e);
+    int rc = NEXUS_OK;
+    for (int i = 0; i < iters && rc == NEXUS_OK; i++) {
+        if (flush) cudaMemsetAsync(flush, i & 0xff, flush_bytes, st);
+        cudaEventRecord(ev[2 * i], st);
+        rc = nexus_cuda_qmatvec_device(w, x_dev, m, y_dev);
+        cudaEventRecord(ev[2 * i + 1], st);
+    }
+    cudaError_t e = cudaStreamSynchronize(st);
+    float total = 0.0f;
+    for (int i = 0; rc == NEXUS_OK && e == cudaSuccess && i < iters; i++) {
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, ev[2 * i], ev[2 * i + 1]);
+        total += ms;
+    }
+    for (auto &x : ev) cudaEventDestroy(x);
+    if (flush) cudaFree(flush);
+    if (rc) return rc;
+    if (e != cudaSuccess) return set_err(b, NEXUS_E_CUDA, cudaGetErrorString(e));
+    *avg_ms = total / iters;
+    return NEXUS_OK;
+}
+
 extern "C" int nexus_cuda_qmatvec_host(nexus_cuda_qweight *w, const float *x, size_t m, float *y) {
     if (!w || !x || !y) return set_err(w ? w->b : nullptr, NEXUS_E_INVALID, "NULL argument");
     nexus_cuda_backend *b = w->b;

@@ -69,7 +69,8 @@ struct GemvParams {
     size_t part_floats;     // capacity of part
     unsigned *counters;     // [groups] arrival counters, zero on entry and exit
     int counter_slots;      // capacity of counters
-    int ksplit;             // unused by the stream-K kernel
+    int ksplit;             // warps per row group (set by the launcher)
+    int nst;                // weight ring slots per warp (set by the launcher)
     int *err;               // device flag set when a bounded wait gives up (may be NULL)
 };
 

@@ -66,7 +66,9 @@ __device__ __forceinline__ uint32_t byte_of(uint32_t w, int j) { return (w >> (8
 // layout, in global memory or in a shared-memory copy of it).
 #define NX_CH(i) c[32 * (i)]
 
-// Q4_K super-block (tiles.cuh): chunk 0 = d|dmin, scales; chunks 1..8 = qs
+// Q4_K super-block (tiles.cuh): chunk 0 = d|dmin, scales; chunks 1..8 = qs.
+// Low nibbles are masked in place; high nibbles are used in place as 16*q
+// (one mask, no shift) and their sums carry a factor 16 removed at the end.
 template <int P>
 __device__ __forceinline__ float sb_dot_q4k(const uint4 *c, const XSb &x, int part) {
     const uint4 c0 = NX_CH(0);
@@ -76,7 +78,7 @@ __device__ __forceinline__ float sb_dot_q4k(const uint4 *c, const XSb &x, int pa
     const uint32_t scl = s0 & 0x3f3f3f3fu, mnl = s1 & 0x3f3f3f3fu;
     const uint32_t sch = (s2 & 0x0f0f0f0fu) | ((s0 >> 2) & 0x30303030u);
     const uint32_t mnh = ((s2 >> 4) & 0x0f0f0f0fu) | ((s1 >> 2) & 0x30303030u);
-    int bh = 0, bl = 0, mn = 0;
+    int bh = 0, bl = 0, bh16 = 0, bl16 = 0, mn = 0;
     constexpr int CPP = 8 / P;  // qs chunks per part (whole sub-block pairs)
 #pragma unroll
     for (int k = 0; k < CPP; k++) {
@@ -87,7 +89,7 @@ __device__ __forceinline__ float sb_dot_q4k(const uint4 *c, const XSb &x, int pa
 #define NX_Q4K_STEP(W)                                              \
     {                                                               \
         const uint32_t lo = q.W & 0x0f0f0f0fu;                      \
-        const uint32_t hi = (q.W >> 4) & 0x0f0f0f0fu;               \
+        const uint32_t hi = q.W & 0xf0f0f0f0u;                      \
         ah = dp4a_us(lo, zhl.W, ah);                                \
         al = dp4a_uu(lo, zll.W, al);                                \
         ah2 = dp4a_us(hi, zhh.W, ah2);                              \
@@ -97,15 +99,21 @@ __device__ __forceinline__ float sb_dot_q4k(const uint4 *c, const XSb &x, int pa
 #undef NX_Q4K_STEP
         const int j = cc >> 1;
         const int sl = (int)byte_of(scl, j), sh = (int)byte_of(sch, j);
-        bh += sl * ah + sh * ah2;
-        bl += sl * al + sh * al2;
+        bh += sl * ah;
+        bl += sl * al;
+        bh16 += sh * ah2;
+        bl16 += sh * al2;
         if ((cc & 1) == 0) {
             // min term of sub-blocks j and j + 4 (32 elements each)
             mn += (int)byte_of(mnl, j) * (x.sz[2 * j] + x.sz[2 * j + 1]) +
                   (int)byte_of(mnh, j) * (x.sz[8 + 2 * j] + x.sz[8 + 2 * j + 1]);
         }
     }
-    return x.u * (d * (256.0f * (float)bh + (float)bl) - dmin * (float)mn);
+    // |bh16|, |bl16| < 2^29 (16 * 63 * 8 chunks * 16 products of <= 15*255);
+    // the factor 16 is exact in f32
+    const float hsum = (float)bh + 0.0625f * (float)bh16;
+    const float lsum = (float)bl + 0.0625f * (float)bl16;
+    return x.u * (d * (256.0f * hsum + lsum) - dmin * (float)mn);
 }
 
 // Q8_0 super-block: chunk 0 = eight f16 scales, chunks 1+2b, 2+2b = qs of block b
@@ -223,22 +231,16 @@ __host__ __device__ __forceinline__ size_t tok_smem_bytes(int k) {
 }
 
 // Prepare super-block s of one token: 16-bit quantization of x (times the
-// RMSNorm weight when fused).  One warp; lane handles elements 8*lane ..
-// 8*lane+7.  The quantization is scale-invariant, so RMSNorm's rstd is not
-// needed here: the caller multiplies u[s] by rstd once the sum of squares,
-// accumulated in *ss, is known.  (x*rstd)*w and rstd*(x*w) agree to f32
-// rounding, far below the 16-bit step.
-__device__ __forceinline__ void prep_sb(const float *__restrict__ x, const float *__restrict__ nw, int s,
-                                        int lane, uint32_t *zh, uint32_t *zl, int *sz, float *u, float *ss) {
-    const float4 *xp = reinterpret_cast<const float4 *>(x + 256 * s + 8 * lane);
-    float4 a = xp[0], b = xp[1];
-    float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+// RMSNorm weight when fused) from the lane's 8 values v (elements
+// 8*lane .. 8*lane+7).  The quantization is scale-invariant, so RMSNorm's
+// rstd is not needed here: the caller multiplies u[s] by rstd once the sum of
+// squares, accumulated in *ss, is known.  (x*rstd)*w and rstd*(x*w) agree to
+// f32 rounding, far below the 16-bit step.
+__device__ __forceinline__ void prep_sb_vals(float (&v)[8], const float (&w)[8], bool has_w, int s, int lane,
+                                             uint32_t *zh, uint32_t *zl, int *sz, float *u, float *ss) {
 #pragma unroll
     for (int i = 0; i < 8; i++) *ss += v[i] * v[i];
-    if (nw) {
-        const float4 *wp = reinterpret_cast<const float4 *>(nw + 256 * s + 8 * lane);
-        float4 wa = wp[0], wb = wp[1];
-        float w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+    if (has_w) {
 #pragma unroll
         for (int i = 0; i < 8; i++) v[i] = v[i] * w[i];
     }
@@ -269,6 +271,47 @@ __device__ __forceinline__ void prep_sb(const float *__restrict__ x, const float
     psum += __shfl_xor_sync(0xffffffffu, psum, 1);
     if ((lane & 1) == 0) sz[16 * s + (lane >> 1)] = psum;
     if (lane == 0) u[s] = amax / 32767.0f;
+}
+
+// One warp prepares super-blocks warp, warp + W, ... of one token.  All of a
+// pass's loads are issued before any is used (one memory round trip per
+// kPrepBatch super-blocks instead of one per super-block).
+constexpr int kPrepBatch = 4;
+template <int W>
+__device__ __forceinline__ float prep_token(const float *__restrict__ x, const float *__restrict__ nw, int n_sb,
+                                            int warp, int lane, uint32_t *zh, uint32_t *zl, int *sz, float *u) {
+    float ss = 0.0f;
+    for (int base = warp; base < n_sb; base += W * kPrepBatch) {
+        float4 xa[kPrepBatch], xb[kPrepBatch], wa[kPrepBatch], wb[kPrepBatch];
+#pragma unroll
+        for (int i = 0; i < kPrepBatch; i++) {
+            const int s = base + i * W;
+            if (s < n_sb) {
+                const float4 *xp = reinterpret_cast<const float4 *>(x + 256 * s + 8 * lane);
+                xa[i] = __ldcg(xp);
+                xb[i] = __ldcg(xp + 1);
+                if (nw) {
+                    const float4 *wp = reinterpret_cast<const float4 *>(nw + 256 * s + 8 * lane);
+                    wa[i] = __ldg(wp);
+                    wb[i] = __ldg(wp + 1);
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kPrepBatch; i++) {
+            const int s = base + i * W;
+            if (s < n_sb) {
+                float v[8] = {xa[i].x, xa[i].y, xa[i].z, xa[i].w, xb[i].x, xb[i].y, xb[i].z, xb[i].w};
+                float w[8] = {1, 1, 1, 1, 1, 1, 1, 1};
+                if (nw) {
+                    w[0] = wa[i].x; w[1] = wa[i].y; w[2] = wa[i].z; w[3] = wa[i].w;
+                    w[4] = wb[i].x; w[5] = wb[i].y; w[6] = wb[i].z; w[7] = wb[i].w;
+                }
+                prep_sb_vals(v, w, nw != nullptr, s, lane, zh, zl, sz, u, &ss);
+            }
+        }
+    }
+    return ss;
 }
 
 // Epilogue for one row (lane) of row group g and token t.
@@ -347,15 +390,21 @@ struct Ring {
     static constexpr int C = Fmt<FMT>::C;
     static constexpr int ITEM_BYTES = C * 512;
     static constexpr int AUX_BYTES = Fmt<FMT>::AUX ? 128 : 0;
-    static constexpr int W = 8;        // warps per CTA
-    static constexpr int NST = 2;      // ring slots per warp
+#ifndef NX_GEMV_WARPS
+#define NX_GEMV_WARPS 8
+#endif
+#ifndef NX_GEMV_SLOTS
+#define NX_GEMV_SLOTS 2
+#endif
+    static constexpr int W = NX_GEMV_WARPS;    // warps per CTA
+    static constexpr int NST = NX_GEMV_SLOTS;  // ring slots per warp
     static constexpr int SLOT_BYTES = ITEM_BYTES + AUX_BYTES;
 };
 
 constexpr unsigned kMbarSpinLimit = 1u << 20;
 
 template <int FMT, int M, int EPI>
-__global__ void __launch_bounds__(256, 1) k_gemv(GemvParams p) {
+__global__ void __launch_bounds__(Ring<FMT>::W * 32, 1) k_gemv(GemvParams p) {
     using R = Ring<FMT>;
     constexpr int W = R::W, NST = R::NST;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -421,9 +470,7 @@ __global__ void __launch_bounds__(256, 1) k_gemv(GemvParams p) {
         uint32_t *zl = reinterpret_cast<uint32_t *>(tb + k);
         int *sz = reinterpret_cast<int *>(tb + 2 * k);
         float *u = reinterpret_cast<float *>(tb + 2 * k + 4 * (k / 16));
-        const float *xt = p.x + (size_t)t * p.x_stride;
-        float ss = 0.0f;
-        for (int s = warp; s < n_sb; s += W) prep_sb(xt, p.norm_w, s, lane, zh, zl, sz, u, &ss);
+        float ss = prep_token<W>(p.x + (size_t)t * p.x_stride, p.norm_w, n_sb, warp, lane, zh, zl, sz, u);
         if (p.norm_w) {
             ss = warp_sum(ss);
             if (lane == 0) misc[warp * M + t] = ss;
@@ -483,8 +530,7 @@ __global__ void __launch_bounds__(256, 1) k_gemv(GemvParams p) {
                 xsb.u = reinterpret_cast<const float *>(tb + 2 * k + 4 * (k / 16))[s_sb];
                 acc[t] += sb_dot<FMT, 1>(cbase, auxw, xsb, 0);
             }
-            // every lane is done with the slot: refill it with item j + NST
-            fence_proxy_async_smem();
+            // every lane has consumed the slot's values: refill it with item j + NST
             __syncwarp();
             if (lane == 0 && j + NST < n_total) issue(j + NST);
         }

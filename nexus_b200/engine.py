@@ -226,6 +226,13 @@ class QWeight:
     def matvec_device(self, x_ptr: int, m: int, y_ptr: int) -> None:
         L.check(self.backend._lib.nexus_cuda_qmatvec_device(self.handle, x_ptr, m, y_ptr), self.backend.handle)
 
+    def bench(self, x_ptr: int, m: int, y_ptr: int, iters: int = 20, flush_bytes: int = 256 << 20) -> float:
+        """Mean device time (ms) of one GEMV launch, cold L2 before each."""
+        ms = C.c_float()
+        L.check(self.backend._lib.nexus_cuda_qmatvec_bench(self.handle, x_ptr, m, y_ptr, iters, flush_bytes,
+                                                           C.byref(ms)), self.backend.handle)
+        return ms.value
+
     def dequantize(self) -> np.ndarray:
         out = np.empty(self.rows * self.cols, np.float32)
         L.check(self.backend._lib.nexus_cuda_qweight_dequantize(self.handle, _ptr(out)), self.backend.handle)
