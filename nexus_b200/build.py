@@ -30,6 +30,7 @@ UNITS = {
     "kernels_gemv_q80.cu": [],
     "kernels_gemv_q40.cu": [],
     "kernels_gemv_q2k.cu": [],
+    "kernels_gemm.cu": [],
     "kernels_attn.cu": [],
     "kernels_misc.cu": [],
     "engine.cu": [],

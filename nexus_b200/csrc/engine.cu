@@ -40,6 +40,8 @@ struct nexus_cuda_backend {
     // to go frees it.
     int children = 0;
     bool destroy_pending = false;
+    // set by a kernel whose bounded wait gave up (op-level calls)
+    int *dev_err = nullptr;
 };
 
 static std::mutex g_backend_mu;
@@ -50,6 +52,7 @@ static void backend_free_now(nexus_cuda_backend *b) {
         cudaStreamSynchronize(b->stream);
         cudaStreamDestroy(b->stream);
     }
+    if (b->dev_err) cudaFree(b->dev_err);
     delete b;
 }
 
@@ -128,14 +131,87 @@ static int make_mat(nexus_cuda_backend *b, int fmt, int n, int k, const uint8_t 
 }
 
 // K-split scratch for an N-row GEMV of up to 4 tokens: 8 slices of partials.
-static cudaError_t alloc_split_scratch(size_t n, float **part, size_t *part_floats, unsigned **ctr, int *slots) {
-    const size_t groups = (n + 31) / 32;
-    *part_floats = 8 * 4 * groups * 32;
-    *slots = (int)groups;
-    cudaError_t e = dalloc(part, *part_floats);
-    if (e == cudaSuccess) e = dalloc(ctr, groups);
-    if (e == cudaSuccess) e = cudaMemset(*ctr, 0, groups * sizeof(unsigned));
+// Batches of at least this many tokens run on the tensor-core GEMM.
+static constexpr int kGemmMinM = 8;
+
+// Grow one scratch buffer to `need` elements.  A zeroed buffer is cleared
+// on `st`, so the clear is ordered before the kernels that read it.
+template <typename T>
+static cudaError_t grow(T **p, size_t *cap, size_t need, bool zero, cudaStream_t st) {
+    if (need <= *cap) return cudaSuccess;
+    if (*p) {
+        cudaStreamSynchronize(st);
+        cudaFree(*p);
+    }
+    *p = nullptr;
+    *cap = 0;
+    cudaError_t e = dalloc(p, need);
+    if (e != cudaSuccess) return e;
+    if (zero) e = cudaMemsetAsync(*p, 0, need * sizeof(T), st);
+    if (e == cudaSuccess) *cap = need;
     return e;
+}
+
+// Scratch of the tcgen05 GEMM: prepared activations, token scales, K-split
+// partials and self-resetting tile counters (zero between launches).
+struct LinScratch {
+    uint8_t *bimg = nullptr;
+    size_t bimg_cap = 0;
+    float *scale = nullptr;
+    size_t scale_cap = 0;
+    float *part = nullptr;
+    size_t part_cap = 0;
+    unsigned *count = nullptr;
+    size_t count_cap = 0;
+    cudaError_t ensure(int m, int n, int k, cudaStream_t st) {
+        const GemmScratchSize z = gemm_scratch_size(m, n, k);
+        cudaError_t e = grow(&bimg, &bimg_cap, z.bimg_bytes, false, st);
+        if (e == cudaSuccess) e = grow(&scale, &scale_cap, z.tok_scale_floats, false, st);
+        if (e == cudaSuccess) e = grow(&part, &part_cap, z.part_floats, false, st);
+        if (e == cudaSuccess) e = grow(&count, &count_cap, z.counter_slots, true, st);
+        return e;
+    }
+    void attach(GemvParams &p, GemmScratch &sc) const {
+        p.part = part;
+        p.part_floats = part_cap;
+        p.counters = count;
+        p.counter_slots = (int)count_cap;
+        sc = {bimg, bimg_cap, scale, scale_cap};
+    }
+    void release() {
+        if (bimg) cudaFree(bimg);
+        if (scale) cudaFree(scale);
+        if (part) cudaFree(part);
+        if (count) cudaFree(count);
+        *this = LinScratch();
+    }
+};
+
+// y[m][n] = x[m][k] * W^T on device buffers: the tensor-core GEMM for
+// batches of kGemmMinM+ tokens in a format it covers, else the GEMV.
+static cudaError_t run_qmatvec(const Mat &mat, const float *x, int m, float *y, LinScratch &ls, int *err,
+                               cudaStream_t st) {
+    GemvParams p = {};
+    p.fmt = mat.fmt;
+    p.w_main = mat.main;
+    p.w_aux = mat.aux;
+    p.n = mat.n;
+    p.k = mat.k;
+    p.m = m;
+    p.x = x;
+    p.x_stride = mat.k;
+    p.epi = EPI_STORE;
+    p.y = y;
+    p.y_stride = mat.n;
+    p.err = err;
+    if (m >= kGemmMinM && gemm_supported(mat.fmt)) {
+        cudaError_t e = ls.ensure(m, mat.n, mat.k, st);
+        if (e != cudaSuccess) return e;
+        GemmScratch sc;
+        ls.attach(p, sc);
+        return launch_gemm(p, sc, st);
+    }
+    return launch_gemv(p, st);
 }
 
 // ---------------------------------------------------------------------------
@@ -213,7 +289,10 @@ extern "C" int nexus_cuda_backend_create(const nexus_cuda_config *cfg, nexus_cud
     b->device = c.device;
     cudaError_t e = cudaSetDevice(c.device);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaMalloc((void **)&b->dev_err, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(b->dev_err, 0, sizeof(int));
     if (e != cudaSuccess) {
+        if (b->stream) cudaStreamDestroy(b->stream);
         delete b;
         return set_err(nullptr, NEXUS_E_CUDA, std::string("backend init: ") + cudaGetErrorString(e));
     }
@@ -246,11 +325,22 @@ extern "C" int nexus_cuda_memory_info(nexus_cuda_backend *b, size_t *total, size
     return NEXUS_OK;
 }
 
+// After a synchronize: report (and clear) a bounded wait that gave up.
+static int check_dev_err(nexus_cuda_backend *b) {
+    int v = 0;
+    NX_CUDA(b, cudaMemcpy(&v, b->dev_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (v) {
+        cudaMemset(b->dev_err, 0, sizeof(int));
+        return set_err(b, NEXUS_E_TIMEOUT, "a kernel's bounded wait gave up (asynchronous copy or MMA never completed)");
+    }
+    return NEXUS_OK;
+}
+
 extern "C" int nexus_cuda_synchronize(nexus_cuda_backend *b) {
     if (!b) return set_err(nullptr, NEXUS_E_INVALID, "backend is NULL");
     cudaSetDevice(b->device);
     NX_CUDA(b, cudaStreamSynchronize(b->stream));
-    return NEXUS_OK;
+    return check_dev_err(b);
 }
 
 extern "C" const char *nexus_cuda_last_error(const nexus_cuda_backend *b) {
@@ -381,37 +471,16 @@ extern "C" int nexus_cuda_execute(nexus_cuda_backend *b, const nexus_op *op) {
         out_bytes = m * n * 4;
         NX_CUDA(b, stage_in(op->a, m * k * 4, dev, A, st));
         NX_CUDA(b, stage_out(op->out, out_bytes, dev, O));
-        float *spart = nullptr;
-        size_t spart_floats = 0;
-        unsigned *sctr = nullptr;
-        int sslots = 0;
-        NX_CUDA(b, alloc_split_scratch(n, &spart, &spart_floats, &sctr, &sslots));
-        for (size_t t0 = 0; t0 < m && e == cudaSuccess;) {
-            size_t chunk = m - t0 >= 4 ? 4 : m - t0 >= 2 ? 2 : 1;
-            GemvParams p = {};
-            p.fmt = op->format;
-            p.w_main = mat.main;
-            p.w_aux = mat.aux;
-            p.n = (int)n;
-            p.k = (int)k;
-            p.m = (int)chunk;
-            p.x = (const float *)A.d + t0 * k;
-            p.x_stride = (int)k;
-            p.epi = EPI_STORE;
-            p.y = (float *)O.d + t0 * n;
-            p.y_stride = (int)n;
-            p.part = spart;
-            p.part_floats = spart_floats;
-            p.counters = sctr;
-            p.counter_slots = sslots;
-            e = launch_gemv(p, st);
-            t0 += chunk;
-        }
+        LinScratch ls;
+        e = run_qmatvec(mat, (const float *)A.d, (int)m, (float *)O.d, ls, b->dev_err, st);
         cudaError_t e2 = cudaStreamSynchronize(st);
-        cudaFree(spart);
-        cudaFree(sctr);
+        ls.release();
         mat.release();
         if (e == cudaSuccess) e = e2;
+        if (e == cudaSuccess) {
+            int rc2 = check_dev_err(b);
+            if (rc2) return rc2;
+        }
         break;
     }
     case NEXUS_OP_ROPE: {
@@ -564,11 +633,7 @@ struct nexus_cuda_qweight {
     Mat mat;
     float *xbuf = nullptr, *ybuf = nullptr;
     size_t xcap = 0, ycap = 0;
-    // K-split scratch of the GEMV: partial row sums and per-row-group counters
-    float *part = nullptr;
-    size_t part_floats = 0;
-    unsigned *counters = nullptr;
-    int counter_slots = 0;
+    LinScratch ls;
 };
 
 
@@ -588,14 +653,6 @@ extern "C" int nexus_cuda_qweight_create(nexus_cuda_backend *b, int format, size
         delete w;
         return rc;
     }
-    cudaError_t se = alloc_split_scratch(rows, &w->part, &w->part_floats, &w->counters, &w->counter_slots);
-    if (se != cudaSuccess) {
-        w->mat.release();
-        if (w->part) cudaFree(w->part);
-        if (w->counters) cudaFree(w->counters);
-        delete w;
-        return set_err(b, NEXUS_E_OOM, std::string("qweight scratch: ") + cudaGetErrorString(se));
-    }
     backend_retain(b);
     *out = w;
     return NEXUS_OK;
@@ -604,11 +661,11 @@ extern "C" int nexus_cuda_qweight_create(nexus_cuda_backend *b, int format, size
 extern "C" int nexus_cuda_qweight_destroy(nexus_cuda_qweight *w) {
     if (!w) return NEXUS_OK;
     cudaSetDevice(w->b->device);
+    cudaStreamSynchronize(w->b->stream);
     w->mat.release();
     if (w->xbuf) cudaFree(w->xbuf);
     if (w->ybuf) cudaFree(w->ybuf);
-    if (w->part) cudaFree(w->part);
-    if (w->counters) cudaFree(w->counters);
+    w->ls.release();
     nexus_cuda_backend *b = w->b;
     delete w;
     backend_release(b);
@@ -619,29 +676,10 @@ extern "C" size_t nexus_cuda_qweight_bytes(const nexus_cuda_qweight *w) { return
 
 extern "C" int nexus_cuda_qmatvec_device(nexus_cuda_qweight *w, const float *x_dev, size_t m, float *y_dev) {
     if (!w || !x_dev || !y_dev) return set_err(w ? w->b : nullptr, NEXUS_E_INVALID, "NULL argument");
+    if (m == 0 || m > (1u << 20)) return set_err(w->b, NEXUS_E_INVALID, "qmatvec: bad batch size");
     nexus_cuda_backend *b = w->b;
     cudaSetDevice(b->device);
-    for (size_t t0 = 0; t0 < m;) {
-        size_t chunk = m - t0 >= 4 ? 4 : m - t0 >= 2 ? 2 : 1;
-        GemvParams p = {};
-        p.fmt = w->mat.fmt;
-        p.w_main = w->mat.main;
-        p.w_aux = w->mat.aux;
-        p.n = w->mat.n;
-        p.k = w->mat.k;
-        p.m = (int)chunk;
-        p.x = x_dev + t0 * w->mat.k;
-        p.x_stride = w->mat.k;
-        p.epi = EPI_STORE;
-        p.y = y_dev + t0 * w->mat.n;
-        p.y_stride = w->mat.n;
-        p.part = w->part;
-        p.part_floats = w->part_floats;
-        p.counters = w->counters;
-        p.counter_slots = w->counter_slots;
-        NX_CUDA(b, launch_gemv(p, b->stream));
-        t0 += chunk;
-    }
+    NX_CUDA(b, run_qmatvec(w->mat, x_dev, (int)m, y_dev, w->ls, b->dev_err, b->stream));
     return NEXUS_OK;
 }
 
@@ -673,6 +711,7 @@ extern "C" int nexus_cuda_qmatvec_bench(nexus_cuda_qweight *w, const float *x_de
     if (flush) cudaFree(flush);
     if (rc) return rc;
     if (e != cudaSuccess) return set_err(b, NEXUS_E_CUDA, cudaGetErrorString(e));
+    if ((rc = check_dev_err(b))) return rc;
     *avg_ms = total / iters;
     return NEXUS_OK;
 }
@@ -697,7 +736,7 @@ extern "C" int nexus_cuda_qmatvec_host(nexus_cuda_qweight *w, const float *x, si
     if (rc) return rc;
     NX_CUDA(b, cudaMemcpyAsync(y, w->ybuf, yn * 4, cudaMemcpyDeviceToHost, b->stream));
     NX_CUDA(b, cudaStreamSynchronize(b->stream));
-    return NEXUS_OK;
+    return check_dev_err(b);
 }
 
 extern "C" int nexus_cuda_qweight_dequantize(nexus_cuda_qweight *w, float *out) {
@@ -718,7 +757,7 @@ extern "C" int nexus_cuda_qweight_dequantize(nexus_cuda_qweight *w, float *out) 
 // ---------------------------------------------------------------------------
 // model
 // ---------------------------------------------------------------------------
-static constexpr int kMaxChunk = 4;  // tokens per fused step (GEMV m)
+static constexpr int kMaxChunk = 64;  // tokens per fused step (prefill chunk, decode batch)
 
 struct Layer {
     float *attn_norm = nullptr, *ffn_norm = nullptr;
@@ -742,10 +781,7 @@ struct nexus_cuda_model {
     float *hidden = nullptr, *q = nullptr, *attn = nullptr, *gated = nullptr, *kv_scratch = nullptr;
     float *logits = nullptr, *part = nullptr;
     unsigned *counters = nullptr;
-    float *gemv_part = nullptr;       // GEMV K-split partials
-    size_t gemv_part_floats = 0;
-    unsigned *gemv_ctr = nullptr;     // GEMV row-group arrival counters
-    int gemv_ctr_slots = 0;
+    LinScratch lin;                   // tensor-core GEMM scratch (steps of kGemmMinM+ tokens)
     DevSeq *seqs = nullptr;
     uint32_t *seq_ids = nullptr, *out_tokens = nullptr;
     DevSeq *h_seqs = nullptr;
@@ -783,6 +819,7 @@ static void model_release(nexus_cuda_model *m) {
         L.down.release();
     }
     m->head.release();
+    m->lin.release();
     for (void *p : m->allocs) cudaFree(p);
     if (m->h_seqs) cudaFreeHost(m->h_seqs);
     if (m->h_seq_ids) cudaFreeHost(m->h_seq_ids);
@@ -1038,16 +1075,11 @@ static int model_load(nexus_cuda_backend *b, const char *path, nexus_cuda_model 
     NX_CUDA(b, malloc_tracked(m, &m->counters, (size_t)MC * Hkv));
     NX_CUDA(b, cudaMemset(m->counters, 0, (size_t)MC * Hkv * 4));
     {
-        // stream-K GEMV scratch: partial row sums of row groups shared by up to
-        // 8 CTAs, and one arrival counter per row group, for every GEMV
-        const size_t nmax = std::max<size_t>({(size_t)qdim + 2 * kv_dim, (size_t)2 * F, (size_t)H,
-                                              (size_t)I.vocab_rows});
-        const size_t groups = (nmax + 31) / 32;
-        m->gemv_part_floats = 8 * (size_t)MC * groups * 32;
-        m->gemv_ctr_slots = (int)groups;
-        NX_CUDA(b, malloc_tracked(m, &m->gemv_part, m->gemv_part_floats));
-        NX_CUDA(b, malloc_tracked(m, &m->gemv_ctr, groups));
-        NX_CUDA(b, cudaMemset(m->gemv_ctr, 0, groups * sizeof(unsigned)));
+        // GEMM scratch for every step size that runs on the tensor cores
+        const int shapes[5][2] = {{(int)(qdim + 2 * kv_dim), (int)H}, {(int)H, (int)qdim}, {(int)(2 * F), (int)H},
+                                  {(int)H, (int)F}, {(int)I.vocab_rows, (int)H}};
+        for (int mm = kGemmMinM; mm <= MC; mm++)
+            for (auto &sh : shapes) NX_CUDA(b, m->lin.ensure(mm, sh[0], sh[1], b->stream));
     }
     NX_CUDA(b, malloc_tracked(m, &m->seqs, MC));
     NX_CUDA(b, malloc_tracked(m, &m->seq_ids, MC));
@@ -1123,11 +1155,24 @@ static double gemv_bytes(const Mat &w, int mc, int k, int n_out) {
 }
 
 static void set_split_scratch(const nexus_cuda_model *m, GemvParams &g) {
-    g.part = m->gemv_part;
-    g.part_floats = m->gemv_part_floats;
-    g.counters = m->gemv_ctr;
-    g.counter_slots = m->gemv_ctr_slots;
     g.err = reinterpret_cast<int *>(m->out_tokens + kMaxChunk);
+}
+
+// One fused linear layer of the step: the tensor-core GEMM for steps of
+// kGemmMinM+ tokens in a format it covers, else the GEMV.
+static cudaError_t launch_linear(nexus_cuda_model *m, GemvParams g, cudaStream_t st) {
+    if (g.m >= kGemmMinM && gemm_supported(g.fmt)) {
+        GemmScratch sc;
+        m->lin.attach(g, sc);
+        return launch_gemm(g, sc, st);
+    }
+    return launch_gemv(g, st);
+}
+
+// Tokens of the next fused step out of `remaining`.
+static int step_chunk(size_t remaining) {
+    if (remaining >= (size_t)kGemmMinM) return (int)std::min<size_t>(remaining, kMaxChunk);
+    return remaining >= 4 ? 4 : remaining >= 2 ? 2 : 1;
 }
 
 // Enqueue one fused decode step for `mc` tokens whose DevSeq entries are on the device.
@@ -1181,7 +1226,7 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         g.qkv.seqs = m->seqs;
         g.qkv.seq_ids = m->seq_ids;
         if (prof) prof->begin();
-        if ((e = launch_gemv(g, st)) != cudaSuccess) return e;
+        if ((e = launch_linear(m, g, st)) != cudaSuccess) return e;
         if (prof) prof->end("qkv", gemv_bytes(L.qkv, mc, H, qdim + 2 * kv_dim) + 4.0 * H);
         if (packed) {
             KvPackParams kp = {};
@@ -1266,7 +1311,7 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         o.y = m->hidden;
         o.y_stride = H;
         if (prof) prof->begin();
-        if ((e = launch_gemv(o, st)) != cudaSuccess) return e;
+        if ((e = launch_linear(m, o, st)) != cudaSuccess) return e;
         if (prof) prof->end("o_proj", gemv_bytes(L.o, mc, qdim, H) + 4.0 * mc * H);
         // ffn_norm -> gate/up -> SwiGLU
         GemvParams gu = {};
@@ -1286,7 +1331,7 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         gu.y = m->gated;
         gu.y_stride = F;
         if (prof) prof->begin();
-        if ((e = launch_gemv(gu, st)) != cudaSuccess) return e;
+        if ((e = launch_linear(m, gu, st)) != cudaSuccess) return e;
         if (prof) prof->end("gate_up", gemv_bytes(L.gateup, mc, H, F) + 4.0 * H);
         // down + residual
         GemvParams dn = {};
@@ -1304,7 +1349,7 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         dn.y = m->hidden;
         dn.y_stride = H;
         if (prof) prof->begin();
-        if ((e = launch_gemv(dn, st)) != cudaSuccess) return e;
+        if ((e = launch_linear(m, dn, st)) != cudaSuccess) return e;
         if (prof) prof->end("down", gemv_bytes(L.down, mc, F, H) + 4.0 * mc * H);
     }
     // transformer_logits: output norm + head + greedy argmax
@@ -1327,7 +1372,7 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         hd.y_stride = (int)I.vocab_rows;
         hd.seqs = m->seqs;
         if (prof) prof->begin();
-        if ((e = launch_gemv(hd, st)) != cudaSuccess) return e;
+        if ((e = launch_linear(m, hd, st)) != cudaSuccess) return e;
         if (prof) prof->end("head", gemv_bytes(m->head, mc, H, (int)I.vocab_rows) + 4.0 * H);
     } else {
         if ((e = launch_rms_norm(m->hidden, m->out_norm, m->logits, mc, H, I.rms_norm_eps, st)) != cudaSuccess) return e;
@@ -1488,7 +1533,7 @@ static int prefill_impl(nexus_cuda_model *m, uint32_t seq_id, const uint32_t *to
     size_t p = 0;
     uint32_t last = 0;
     while (p < n) {
-        int mc = n - p >= 4 ? 4 : n - p >= 2 ? 2 : 1;
+        const int mc = step_chunk(n - p);
         StepItem it[kMaxChunk];
         for (int j = 0; j < mc; j++) it[j] = {seq_id, tokens[p + j], (uint32_t)(p + j), (uint32_t)(p + j)};
         const bool final = p + mc == n;
@@ -1597,7 +1642,7 @@ extern "C" int nexus_cuda_decode_batch(nexus_cuda_model *m, const nexus_decode_i
     NX_CUDA(m->b, cudaEventRecord(m->ev0, m->b->stream));
     const size_t V = m->info.vocab_rows;
     for (size_t p = 0; p < n;) {
-        int mc = n - p >= 4 ? 4 : n - p >= 2 ? 2 : 1;
+        const int mc = step_chunk(n - p);
         StepItem it[kMaxChunk];
         for (int j = 0; j < mc; j++) {
             const nexus_decode_item &d = items[p + j];

@@ -76,6 +76,21 @@ struct GemvParams {
 
 cudaError_t launch_gemv(const GemvParams &p, cudaStream_t st);
 
+// ---- kernels_gemm.cu: tcgen05 GEMM for m >= 8 (same weights, epilogues and
+// K-split scratch fields of GemvParams) ----
+struct GemmScratch {
+    uint8_t *bimg;            // prepared activations (f16 hi/lo in the MMA layout)
+    size_t bimg_bytes;
+    float *tok_scale;         // per-token power-of-two scales
+    size_t tok_scale_floats;
+};
+struct GemmScratchSize {
+    size_t bimg_bytes, tok_scale_floats, part_floats, counter_slots;
+};
+bool gemm_supported(int fmt);
+GemmScratchSize gemm_scratch_size(int m, int n, int k);
+cudaError_t launch_gemm(const GemvParams &p, const GemmScratch &sc, cudaStream_t st);
+
 // ---- kernels_attn.cu ----
 struct AttnParams {
     int hq, hkv, head_dim, m;

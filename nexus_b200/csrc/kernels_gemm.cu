@@ -1,0 +1,197 @@
+// kernels_gemm.cu -- activation preparation and launch of the tcgen05 GEMM
+// (kernels_gemm.cuh) for batched decode and prefill.
+#include "kernels_gemm.cuh"
+
+namespace nx {
+namespace qg {
+
+// Position of element e (0..255) of a Q4_K super-block inside its quarter
+// stage: quarter e%128/32; low nibbles (e < 128) first, high nibbles second;
+// inside a 4-byte word the byte order is 0,2,1,3 (see dq_q4k_quarter).
+__device__ __forceinline__ void q4k_kpos(int e, int &quarter, int &pos) {
+    const int b = e & 127, hi = e >> 7;
+    quarter = b >> 5;
+    const int i = (b & 31) >> 2, bw = b & 3;
+    const int pw = ((bw & 1) << 1) | (bw >> 1);
+    pos = hi * 32 + 4 * i + pw;
+}
+
+// One CTA per (token, group of 4 super-blocks): optional RMSNorm
+// ((x*rstd)*w, src/kernel/mod.rs:199-209), a power-of-two scale per token
+// keeping |x| < 2^10 (so the 32-element sub-block sums stay below 2^15, well
+// inside f16 range), the f16 hi/lo split, and the sub-block sums.  Image rows
+// per quarter: tokens' hi halves (rows 0..NT-1), then lo halves (NT..2NT-1).
+template <int NT>
+__global__ void __launch_bounds__(256) k_gemm_prep(const float *__restrict__ x, int x_stride,
+                                                   const float *__restrict__ norm_w, float eps, int m, int k,
+                                                   uint8_t *__restrict__ bimg, float *__restrict__ tok_scale) {
+    const int tok = blockIdx.x, tt = tok / NT, n = tok % NT;
+    const int n_sb = k / 256;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    __shared__ float red_s[8], red_m[8];
+    __shared__ float rstd_s, inv_s;
+    const bool valid = tok < m;
+    const float *xr = x + (size_t)tok * x_stride;
+    if (valid) {
+        float ss = 0.0f, mx = 0.0f;
+        for (int i = tid; i < k; i += 256) {
+            const float v = xr[i];
+            ss += v * v;
+            mx = fmaxf(mx, fabsf(norm_w ? v * norm_w[i] : v));
+        }
+        ss = warp_sum(ss);
+        mx = warp_max(mx);
+        if (lane == 0) {
+            red_s[warp] = ss;
+            red_m[warp] = mx;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            float s = 0.0f, M = 0.0f;
+            for (int w = 0; w < 8; w++) {
+                s += red_s[w];
+                M = fmaxf(M, red_m[w]);
+            }
+            const float rstd = norm_w ? 1.0f / sqrtf(s / (float)k + eps) : 1.0f;
+            const float top = M * rstd;
+            int e2 = 0;
+            if (top > 0.0f && isfinite(top)) frexpf(top, &e2);
+            // |x| < 2^e2 -> scaled by 2^(10-e2) stays below 2^10
+            const float inv = top > 0.0f && isfinite(top) ? ldexpf(1.0f, 10 - e2) : 1.0f;
+            rstd_s = rstd;
+            inv_s = inv;
+            if (blockIdx.y == 0) tok_scale[tok] = 1.0f / inv;
+        }
+        __syncthreads();
+    }
+    const float rstd = valid ? rstd_s : 1.0f, inv = valid ? inv_s : 1.0f;
+    const int sb_end = min(n_sb, (int)(blockIdx.y + 1) * 4);
+    for (int s = blockIdx.y * 4; s < sb_end; s++) {
+        float v = 0.0f;
+        if (valid) {
+            v = xr[s * 256 + tid];
+            if (norm_w) v = (v * rstd) * norm_w[s * 256 + tid];
+            v *= inv;
+        }
+        const __half hi = __float2half_rn(v);
+        const __half lo = __float2half_rn(v - __half2float(hi));
+        uint8_t *base = bimg + ((size_t)tt * n_sb + s) * bimg_sb_bytes(NT);
+        int q, pos;
+        q4k_kpos(tid, q, pos);
+        // K-chunk (pos/8) of 2NT rows x 16 B; hi in row n, lo in row NT + n
+        uint8_t *qb = base + q * NT * 256 + (pos >> 3) * NT * 32 + n * 16 + (pos & 7) * 2;
+        *reinterpret_cast<__half *>(qb) = hi;
+        *reinterpret_cast<__half *>(qb + NT * 16) = lo;
+        // sub-block sums (sub-block j = elements 32j..32j+31 = warp j): K
+        // positions 0..7 of the min operand, positions 8..15 zero
+        const float sj = warp_sum(v);
+        uint8_t *mb = base + 4 * NT * 256;
+        if (lane == 0) {
+            const __half sh = __float2half_rn(sj);
+            const __half sl = __float2half_rn(sj - __half2float(sh));
+            *reinterpret_cast<__half *>(mb + n * 16 + warp * 2) = sh;
+            *reinterpret_cast<__half *>(mb + NT * 16 + n * 16 + warp * 2) = sl;
+        }
+        if (tid < 8) {
+            *reinterpret_cast<__half *>(mb + NT * 32 + n * 16 + tid * 2) = __float2half_rn(0.0f);
+            *reinterpret_cast<__half *>(mb + NT * 32 + NT * 16 + n * 16 + tid * 2) = __float2half_rn(0.0f);
+        }
+    }
+}
+
+static int sm_count_cached() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static int sm_count[16] = {};
+    if (dev < 16 && sm_count[dev] == 0) cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
+    return dev < 16 && sm_count[dev] ? sm_count[dev] : 148;
+}
+
+// Tiles and K split of one GEMM: the split minimises waves x (super-blocks
+// per unit + one for the pipeline fill).
+static GemmShape plan(int m, int n, int k) {
+    const int nt = m <= 16 ? 16 : 32;
+    GemmShape g;
+    g.n_sb = k / 256;
+    g.groups = (n + 31) / 32;
+    g.n_tt = (m + nt - 1) / nt;
+    g.n_rt = (g.groups + 3) / 4;
+    g.mpad = g.n_tt * nt;
+    g.npad = g.n_rt * 128;
+    const int sms = sm_count_cached();
+    const long long units0 = (long long)g.n_tt * g.n_rt;
+    int best = 1;
+    long long best_cost = -1;
+    for (int s = 1; s <= 16 && s <= g.n_sb; s++) {
+        const long long waves = (units0 * s + sms - 1) / sms;
+        const long long cost = waves * ((g.n_sb + s - 1) / s + 1);
+        if (best_cost < 0 || cost < best_cost) {
+            best_cost = cost;
+            best = s;
+        }
+    }
+    g.nsplit = best;
+    return g;
+}
+
+template <int NT, int EPI>
+static cudaError_t launch_nt_epi(const GemvParams &p, const GemmScratch &sc, cudaStream_t st) {
+    constexpr int FMT = 12;
+    using S = Smem<FMT, NT>;
+    GemmShape g = plan(p.m, p.n, p.k);
+    const int sms = sm_count_cached();
+    const long long units0 = (long long)g.n_tt * g.n_rt;
+    if (g.nsplit > 1) {
+        if (!p.part || !p.counters || (size_t)g.nsplit * g.mpad * g.npad > p.part_floats ||
+            units0 > (long long)p.counter_slots)
+            g.nsplit = 1;
+    }
+    const size_t need = (size_t)g.n_tt * g.n_sb * bimg_sb_bytes(NT);
+    if (!sc.bimg || need > sc.bimg_bytes || !sc.tok_scale || (size_t)g.mpad > sc.tok_scale_floats)
+        return cudaErrorInvalidValue;
+    dim3 pg(g.mpad, (g.n_sb + 3) / 4);
+    k_gemm_prep<NT><<<pg, 256, 0, st>>>(p.x, p.x_stride, p.norm_w, p.eps, p.m, p.k, sc.bimg, sc.tok_scale);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    auto fn = k_qgemm<FMT, NT, EPI>;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
+    if (e != cudaSuccess) return e;
+    const long long units = units0 * g.nsplit;
+    const int grid = (int)(units < sms ? units : sms);
+    fn<<<grid, kThreads, S::TOTAL, st>>>(p, g, sc.bimg, sc.tok_scale);
+    return cudaGetLastError();
+}
+
+template <int NT>
+static cudaError_t launch_nt(const GemvParams &p, const GemmScratch &sc, cudaStream_t st) {
+    switch (p.epi) {
+    case EPI_STORE: return launch_nt_epi<NT, EPI_STORE>(p, sc, st);
+    case EPI_ADD: return launch_nt_epi<NT, EPI_ADD>(p, sc, st);
+    case EPI_SWIGLU: return launch_nt_epi<NT, EPI_SWIGLU>(p, sc, st);
+    case EPI_QKV: return launch_nt_epi<NT, EPI_QKV>(p, sc, st);
+    case EPI_ARGMAX: return launch_nt_epi<NT, EPI_ARGMAX>(p, sc, st);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace qg
+
+bool gemm_supported(int fmt) { return fmt == 12; }
+
+GemmScratchSize gemm_scratch_size(int m, int n, int k) {
+    const qg::GemmShape g = qg::plan(m, n, k);
+    const int nt = m <= 16 ? 16 : 32;
+    GemmScratchSize z;
+    z.bimg_bytes = (size_t)g.n_tt * g.n_sb * qg::bimg_sb_bytes(nt);
+    z.tok_scale_floats = (size_t)g.mpad;
+    z.part_floats = g.nsplit > 1 ? (size_t)g.nsplit * g.mpad * g.npad : 0;
+    z.counter_slots = (size_t)g.n_tt * g.n_rt;
+    return z;
+}
+
+cudaError_t launch_gemm(const GemvParams &p, const GemmScratch &sc, cudaStream_t st) {
+    if (!gemm_supported(p.fmt) || p.k % 256 != 0 || p.n <= 0 || p.m <= 0) return cudaErrorInvalidValue;
+    return p.m <= 16 ? qg::launch_nt<16>(p, sc, st) : qg::launch_nt<32>(p, sc, st);
+}
+
+}  // namespace nx

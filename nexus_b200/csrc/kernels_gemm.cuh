@@ -1,0 +1,532 @@
+// kernels_gemm.cuh -- dequant-to-shared-memory tcgen05 GEMM for batched
+// decode and prefill (Y[m][n] = X[m][k] * W[n][k]^T over the row-interleaved
+// weight tiles of tiles.cuh), used where the GEMV's per-token integer work
+// would exceed the HBM budget (m >= 8).
+//
+// Exactness scheme for the super-block formats (Q4_K, Q2_K).  A weight is
+// d*sc_j*q - dmin*m_j (src/gguf/mod.rs:1041-1049, 1076-1081) with integer
+// q, sc_j, m_j.  The tensor cores multiply the exact small integers
+//     A[r][k] = sc_j * q           (f16, <= 945: exact)
+//     Amin[r][j] = m_j             (f16, <= 63: exact)
+// with the activations split into two f16 halves x = hi + lo (22 significant
+// bits), accumulating in f32 in TMEM per super-block:
+//     D = sum_k A*x,  E = sum_j m_j * X_j  (X_j = sum of x over sub-block j)
+// and the epilogue applies the per-row super-block scales in f32:
+//     y += d*D - dmin*E.
+// The activations are scaled per token by a power of two (kept in f16 range)
+// and the scale is undone on output.  Everything beyond f32 rounding is the
+// 2^-22 relative split of x, far inside the 1e-3 per-op bound.
+// A tcgen05.mma of M=128, K=16 costs about the same issue time for any N up
+// to 256, so the hi and lo halves of the tokens are stacked along N (one MMA
+// of N = 2*NT per K step) rather than issued as two MMAs.
+//
+// CTA roles (one CTA per SM, persistent over work units):
+//   warps 0-7  dequantize (warp w: row group w&3 of the 128-row tile, half
+//              w>>2 of each super-block) and run the epilogue (half w>>2 of
+//              the token tile, TMEM lanes 32*(w&3)..)
+//   warp 8     TMA bulk copies of the raw weight tiles (3-slot ring)
+//   warp 9     TMEM allocation + TMA copies of the prepared activations
+//   warp 10    tcgen05.mma issue (one thread)
+// A work unit is (token tile, 128-row tile, K split); a super-block runs as 4
+// quarter stages of 64 K (A: 16 KB in a 6-slot ring, B: NT*256 bytes in a
+// 6- or 8-slot ring), so operands are staged ahead of the MMAs.  K-split partial sums
+// meet in global scratch and the last CTA of a tile adds them in split order
+// (deterministic) before the fused epilogue of kernels_gemv.cuh.
+// Each warp signals a barrier once (after __syncwarp), so the arrival counts
+// are warps, not threads.  Every wait is bounded: a wait that gives up sets the CTA's abort flag and
+// the device error flag, later waits return at once, nothing new is issued,
+// copies and MMAs in flight are waited for, and TMEM is freed before exit.
+#pragma once
+#include <cuda_fp16.h>
+
+#include "kernels_gemv.cuh"
+
+namespace nx {
+namespace qg {
+
+constexpr int kRawSlots = 3;   // raw weight tiles (one super-block of 4 row groups each)
+constexpr int kASlots = 6;     // dequantized quarter stages
+constexpr int kQuarters = 4;
+constexpr int kDqWarps = 8;
+constexpr int kThreads = (kDqWarps + 3) * 32;
+constexpr unsigned kSpin = 1u << 22;
+
+template <int FMT>
+struct Raw {
+    static constexpr int ITEM = Fmt<FMT>::C * 512;  // one row group x one super-block
+    static constexpr int AUXB = Fmt<FMT>::AUX ? 128 : 0;
+    static constexpr int SLOT = 4 * (ITEM + AUXB);  // four row groups
+};
+
+// Bytes of the prepared activations of one (token tile, super-block):
+// 4 quarters x 8 K-chunks x 2NT rows (hi, lo) x 16 B, then the sub-block
+// sums: 2 K-chunks x 2NT rows x 16 B.
+__host__ __device__ constexpr int bimg_sb_bytes(int nt) { return nt * 1088; }
+
+// Shared memory: independent rings for the raw weights, the dequantized
+// quarter stages (A), the prepared activations (B, one quarter per slot) and
+// the per-super-block min operands, so every load runs ahead of the MMAs.
+template <int FMT, int NT>
+struct Smem {
+    static constexpr int BSLOTS = NT == 16 ? 8 : 6;
+    static constexpr int A_BYTES = 8 * 128 * 16;
+    static constexpr int B_BYTES = NT * 256;
+    static constexpr int AMIN_BYTES = 2 * 128 * 16;
+    static constexpr int BMIN_BYTES = NT * 64;
+    static constexpr int RAW = 0;
+    static constexpr int A = RAW + kRawSlots * Raw<FMT>::SLOT;
+    static constexpr int B = A + kASlots * A_BYTES;
+    static constexpr int AMIN = B + BSLOTS * B_BYTES;
+    static constexpr int BMIN = AMIN + 2 * AMIN_BYTES;
+    static constexpr int TOTAL = BMIN + 2 * BMIN_BYTES + 1024;  // + alignment slack
+};
+
+struct GemmShape {
+    int n_tt, n_rt, nsplit, n_sb, groups, mpad, npad;
+};
+
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    // K-major, no swizzle: ((8 rows, n), 2 K-chunks) : ((16 B, SBO), LBO); version 1
+    return (uint64_t)((saddr >> 4) & 0x3fffu) | ((uint64_t)((lbo >> 4) & 0x3fffu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3fffu) << 32) | (1ull << 46);
+}
+template <int N>
+__device__ __forceinline__ constexpr uint32_t umma_idesc() {
+    // D f32, A/B f16, both K-major, N, M = 128
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+__device__ __forceinline__ void umma_f16(uint32_t dt, uint64_t ad, uint64_t bd, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n}\n" ::"r"(dt),
+        "l"(ad), "l"(bd), "r"(idesc), "r"(acc), "r"(0u)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(unsigned long long *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive(unsigned long long *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, float (&v)[N]);
+template <>
+__device__ __forceinline__ void tmem_ld<8>(uint32_t taddr, float (&v)[8]) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = __uint_as_float(r[i]);
+}
+template <>
+__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Bounded mbarrier wait; false once this CTA has given up (abort set).
+__device__ __forceinline__ bool bwait(unsigned long long *bar, unsigned parity, volatile int *abort_flag, int *err) {
+    unsigned n = 0;
+    while (!mbar_try_wait(bar, parity)) {
+        if ((++n & 255u) == 0) {
+            if (*abort_flag) return false;
+            if (n > kSpin) {
+                *abort_flag = 1;
+                if (err) atomicExch(err, 2);
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ uint32_t lop_or(uint32_t w, uint32_t mask) {
+    // (w & mask) | 0x64006400: two f16 values 1024 + field
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(r) : "r"(w), "r"(mask), "r"(0x64006400u));
+    return r;
+}
+__device__ __forceinline__ uint32_t hfma2u(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+__device__ __forceinline__ uint32_t f16x2_splat(float v) {
+    const uint32_t h = __half_as_ushort(__float2half_rn(v));
+    return h | (h << 16);
+}
+
+// Work unit u -> (token tile, row tile, split) and the split's super-blocks.
+__device__ __forceinline__ void unit_coords(const GemmShape &g, int u, int &tt, int &rt, int &ks, int &s0, int &s1) {
+    ks = u % g.nsplit;
+    const int tile = u / g.nsplit;
+    rt = tile % g.n_rt;
+    tt = tile / g.n_rt;
+    const int per = g.n_sb / g.nsplit, rem = g.n_sb % g.nsplit;
+    s0 = ks * per + min(ks, rem);
+    s1 = s0 + per + (ks < rem ? 1 : 0);
+}
+
+// Q4_K dequantization of one quarter (qs bytes 32q..32q+31 of the row) into
+// the stage's A chunks.  K order inside a quarter: positions 0..31 are the
+// low nibbles (sub-block q), 32..63 the high nibbles (sub-block q+4); within
+// each 4-byte word the order is bytes 0,2,1,3 (the prepared activations use
+// the same order, so the product is unchanged).
+__device__ __forceinline__ void dq_q4k_quarter(const uint32_t (&w)[8], uint32_t sc_lo, uint32_t sc_hi,
+                                               uint8_t *a_row) {
+    // exact f16 products: (1024+q)*sc - 1024*sc and (1024+16q)*(sc/16) - 64*sc
+    const uint32_t ml = f16x2_splat((float)sc_lo), bl = f16x2_splat(-1024.0f * (float)sc_lo);
+    const uint32_t mh = f16x2_splat((float)sc_hi * 0.0625f), bh = f16x2_splat(-64.0f * (float)sc_hi);
+#pragma unroll
+    for (int kc = 0; kc < 4; kc++) {
+        const uint32_t w0 = w[2 * kc], w1 = w[2 * kc + 1];
+        const uint32_t w0s = w0 >> 8, w1s = w1 >> 8;
+        uint4 lo, hi;
+        lo.x = hfma2u(lop_or(w0, 0x000f000fu), ml, bl);
+        lo.y = hfma2u(lop_or(w0s, 0x000f000fu), ml, bl);
+        lo.z = hfma2u(lop_or(w1, 0x000f000fu), ml, bl);
+        lo.w = hfma2u(lop_or(w1s, 0x000f000fu), ml, bl);
+        hi.x = hfma2u(lop_or(w0, 0x00f000f0u), mh, bh);
+        hi.y = hfma2u(lop_or(w0s, 0x00f000f0u), mh, bh);
+        hi.z = hfma2u(lop_or(w1, 0x00f000f0u), mh, bh);
+        hi.w = hfma2u(lop_or(w1s, 0x00f000f0u), mh, bh);
+        *reinterpret_cast<uint4 *>(a_row + kc * 2048) = lo;
+        *reinterpret_cast<uint4 *>(a_row + (4 + kc) * 2048) = hi;
+    }
+}
+
+template <int FMT, int NT, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_qgemm(GemvParams p, GemmShape g, const uint8_t *__restrict__ bimg, const float *__restrict__ tok_scale) {
+    static_assert(FMT == 12, "tcgen05 GEMM: Q4_K");
+    static_assert(NT == 16 || NT == 32, "token tile");
+    using S = Smem<FMT, NT>;
+    using R = Raw<FMT>;
+    constexpr int H = NT / 2;  // tokens per epilogue warp
+    constexpr int NB = S::BSLOTS;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ unsigned long long raw_full[kRawSlots], raw_empty[kRawSlots];
+    __shared__ unsigned long long a_full[kASlots], a_empty[kASlots];
+    __shared__ unsigned long long b_full[NB], b_empty[NB];
+    __shared__ unsigned long long amin_full[2], bmin_full[2], min_empty[2];
+    __shared__ unsigned long long acc_full[2], acc_empty[2], mma_done;
+    __shared__ uint32_t tmem_base_s;
+    __shared__ volatile int abort_s;
+    __shared__ int last_s;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_units = g.n_tt * g.n_rt * g.nsplit;
+    // per accumulator buffer: D (2NT columns: hi tokens, lo tokens), E (2NT)
+    constexpr uint32_t kTmemCols = 8 * NT;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kRawSlots; i++) {
+            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_empty[i], kDqWarps);
+        }
+        for (int i = 0; i < kASlots; i++) {
+            mbar_init(&a_full[i], 4);
+            mbar_init(&a_empty[i], 1);
+        }
+        for (int i = 0; i < NB; i++) {
+            mbar_init(&b_full[i], 1);
+            mbar_init(&b_empty[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&amin_full[i], 4);
+            mbar_init(&bmin_full[i], 1);
+            mbar_init(&min_empty[i], 1);
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], kDqWarps);
+        }
+        mbar_init(&mma_done, 1);
+        abort_s = 0;
+        mbar_init_fence();
+    }
+    if (warp == 9) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_s;
+
+    if (warp == 8) {
+        // ---- raw weight tiles: 4 row groups of one super-block per slot ----
+        if (lane == 0) {
+            unsigned n = 0;
+            for (int u = blockIdx.x; u < n_units && !abort_s; u += gridDim.x) {
+                int tt, rt, ks, s0, s1;
+                unit_coords(g, u, tt, rt, ks, s0, s1);
+                for (int s = s0; s < s1; s++, n++) {
+                    const int slot = n % kRawSlots;
+                    if (!bwait(&raw_empty[slot], ((n / kRawSlots) & 1) ^ 1, &abort_s, p.err)) break;
+                    const int ng = min(4, g.groups - 4 * rt);
+                    mbar_expect_tx(&raw_full[slot], (unsigned)(ng * (R::ITEM + R::AUXB)));
+                    uint8_t *dst = smem + S::RAW + slot * R::SLOT;
+                    for (int gi = 0; gi < ng; gi++) {
+                        const size_t item = (size_t)(4 * rt + gi) * g.n_sb + s;
+                        tma_load_1d(dst + gi * R::ITEM, reinterpret_cast<const uint8_t *>(p.w_main) + item * R::ITEM,
+                                    R::ITEM, &raw_full[slot]);
+                    }
+                }
+            }
+            // copies still in flight land before the CTA exits
+            for (int sl = 0; sl < kRawSlots; sl++) {
+                if ((unsigned)sl < n) {
+                    const unsigned fills = (n - 1 - sl) / kRawSlots + 1;
+                    unsigned k = 0;
+                    while (!mbar_try_wait(&raw_full[sl], (fills - 1) & 1) && ++k < kSpin) {
+                    }
+                }
+            }
+        }
+    } else if (warp == 9) {
+        // ---- prepared activations: one quarter per slot, sub-block sums per super-block ----
+        if (lane == 0) {
+            unsigned n = 0, c = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+                int tt, rt, ks, s0, s1;
+                unit_coords(g, u, tt, rt, ks, s0, s1);
+                for (int s = s0; s < s1 && ok; s++, n++) {
+                    const uint8_t *src = bimg + ((size_t)tt * g.n_sb + s) * bimg_sb_bytes(NT);
+                    for (int q = 0; q < kQuarters; q++, c++) {
+                        const int slot = c % NB;
+                        if (!(ok = bwait(&b_empty[slot], ((c / NB) & 1) ^ 1, &abort_s, p.err))) break;
+                        mbar_expect_tx(&b_full[slot], S::B_BYTES);
+                        tma_load_1d(smem + S::B + slot * S::B_BYTES, src + q * S::B_BYTES, S::B_BYTES, &b_full[slot]);
+                        if (q == 0) {
+                            const int ms = n & 1;
+                            if (!(ok = bwait(&min_empty[ms], ((n >> 1) & 1) ^ 1, &abort_s, p.err))) break;
+                            mbar_expect_tx(&bmin_full[ms], S::BMIN_BYTES);
+                            tma_load_1d(smem + S::BMIN + ms * S::BMIN_BYTES, src + kQuarters * S::B_BYTES,
+                                        S::BMIN_BYTES, &bmin_full[ms]);
+                        }
+                    }
+                }
+            }
+            // copies still in flight land before the CTA exits
+            for (int sl = 0; sl < NB; sl++) {
+                if ((unsigned)sl < c) {
+                    const unsigned fills = (c - 1 - sl) / NB + 1;
+                    unsigned k = 0;
+                    while (!mbar_try_wait(&b_full[sl], (fills - 1) & 1) && ++k < kSpin) {
+                    }
+                }
+            }
+            for (int ms = 0; ms < 2; ms++) {
+                if ((unsigned)ms < n) {
+                    const unsigned fills = (n - 1 - ms) / 2 + 1;
+                    unsigned k = 0;
+                    while (!mbar_try_wait(&bmin_full[ms], (fills - 1) & 1) && ++k < kSpin) {
+                    }
+                }
+            }
+        }
+    } else if (warp == 10) {
+        // ---- MMA issue ----
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc<2 * NT>();
+            const uint32_t a0 = smem_u32(smem + S::A), b0 = smem_u32(smem + S::B);
+            const uint32_t amin0 = smem_u32(smem + S::AMIN), bmin0 = smem_u32(smem + S::BMIN);
+            unsigned n = 0, c = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+                int tt, rt, ks, s0, s1;
+                unit_coords(g, u, tt, rt, ks, s0, s1);
+                for (int s = s0; s < s1 && ok; s++, n++) {
+                    const int ab = n & 1;
+                    const uint32_t dcol = tmem + ab * 4 * NT, ecol = dcol + 2 * NT;
+                    if (!(ok = bwait(&acc_empty[ab], ((n >> 1) & 1) ^ 1, &abort_s, p.err))) break;
+                    tc_fence_after();
+                    for (int q = 0; q < kQuarters; q++, c++) {
+                        const int as = c % kASlots, bs = c % NB;
+                        if (!(ok = bwait(&a_full[as], (c / kASlots) & 1, &abort_s, p.err))) break;
+                        if (!(ok = bwait(&b_full[bs], (c / NB) & 1, &abort_s, p.err))) break;
+                        tc_fence_after();
+#pragma unroll
+                        for (int kk = 0; kk < 4; kk++) {
+                            const uint64_t ad = umma_desc(a0 + as * S::A_BYTES + kk * 2 * 2048, 2048, 128);
+                            const uint32_t bq = b0 + bs * S::B_BYTES + kk * 2 * NT * 32;
+                            umma_f16(dcol, ad, umma_desc(bq, NT * 32, 128), idesc, (q | kk) != 0);
+                        }
+                        umma_commit(&a_empty[as]);
+                        umma_commit(&b_empty[bs]);
+                        if (q == 0) {
+                            const int ms = n & 1;
+                            if (!(ok = bwait(&amin_full[ms], (n >> 1) & 1, &abort_s, p.err))) break;
+                            if (!(ok = bwait(&bmin_full[ms], (n >> 1) & 1, &abort_s, p.err))) break;
+                            tc_fence_after();
+                            const uint64_t ad = umma_desc(amin0 + ms * S::AMIN_BYTES, 2048, 128);
+                            const uint32_t bm = bmin0 + ms * S::BMIN_BYTES;
+                            umma_f16(ecol, ad, umma_desc(bm, NT * 32, 128), idesc, 0);
+                            umma_commit(&min_empty[ms]);
+                        }
+                    }
+                    if (ok) umma_commit(&acc_full[ab]);
+                }
+            }
+            // all MMAs issued so far have completed before TMEM is released
+            umma_commit(&mma_done);
+            unsigned k = 0;
+            while (!mbar_try_wait(&mma_done, 0) && ++k < kSpin) {
+            }
+        }
+    } else {
+        // ---- dequantization + epilogue (warps 0-7) ----
+        const int rg = warp & 3, half = warp >> 2;
+        const int r = 32 * rg + lane;  // row inside the 128-row tile
+        const uint32_t t_lane = (uint32_t)(32 * rg) << 16;
+        unsigned n = 0;
+        float pd = 0.0f, pdm = 0.0f;  // scales of the previous super-block
+        auto epilogue_sb = [&](unsigned nn, float d, float dm, float (&acc)[H]) {
+            const int ab = nn & 1;
+            bwait(&acc_full[ab], (nn >> 1) & 1, &abort_s, p.err);
+            __syncwarp();
+            tc_fence_after();
+            float dh[H], dl[H], eh[H], el[H];
+            const uint32_t col = tmem + t_lane + ab * 4 * NT + half * H;
+            tmem_ld<H>(col, dh);
+            tmem_ld<H>(col + NT, dl);
+            tmem_ld<H>(col + 2 * NT, eh);
+            tmem_ld<H>(col + 3 * NT, el);
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[ab]);
+#pragma unroll
+            for (int t = 0; t < H; t++) acc[t] = fmaf(d, dh[t] + dl[t], fmaf(-dm, eh[t] + el[t], acc[t]));
+        };
+        for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+            int tt, rt, ks, s0, s1;
+            unit_coords(g, u, tt, rt, ks, s0, s1);
+            float acc[H];
+#pragma unroll
+            for (int t = 0; t < H; t++) acc[t] = 0.0f;
+            for (int s = s0; s < s1; s++, n++) {
+                const int slot = n % kRawSlots;
+                bwait(&raw_full[slot], (n / kRawSlots) & 1, &abort_s, p.err);
+                const uint8_t *rawp = smem + S::RAW + slot * R::SLOT + rg * R::ITEM + lane * 16;
+                const uint4 c0 = *reinterpret_cast<const uint4 *>(rawp);
+                uint32_t wq[16];
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    const uint4 v = *reinterpret_cast<const uint4 *>(rawp + (1 + 4 * half + c) * 512);
+                    wq[4 * c] = v.x;
+                    wq[4 * c + 1] = v.y;
+                    wq[4 * c + 2] = v.z;
+                    wq[4 * c + 3] = v.w;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&raw_empty[slot]);
+                const float d = h2f_bits(c0.x), dm = h2f_bits(c0.x >> 16);
+                // unpack_q4_k_scales (src/gguf/mod.rs:1547-1554)
+                const uint32_t scl = c0.y & 0x3f3f3f3fu, mnl = c0.z & 0x3f3f3f3fu;
+                const uint32_t sch = (c0.w & 0x0f0f0f0fu) | ((c0.y >> 2) & 0x30303030u);
+                const uint32_t mnh = ((c0.w >> 4) & 0x0f0f0f0fu) | ((c0.z >> 2) & 0x30303030u);
+#pragma unroll
+                for (int qq = 0; qq < 2; qq++) {
+                    const int q = 2 * half + qq;
+                    const unsigned c = 4 * n + q;
+                    const int as = c % kASlots;
+                    bwait(&a_empty[as], ((c / kASlots) & 1) ^ 1, &abort_s, p.err);
+                    uint32_t w8[8];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) w8[i] = wq[8 * qq + i];
+                    dq_q4k_quarter(w8, byte_of(scl, q), byte_of(sch, q), smem + S::A + as * S::A_BYTES + r * 16);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&a_full[as]);
+                    if (q == 0) {
+                        // Amin row: m_0..m_7, then eight zeros
+                        const int ms = n & 1;
+                        bwait(&min_empty[ms], ((n >> 1) & 1) ^ 1, &abort_s, p.err);
+                        uint4 m0;
+                        m0.x = __half_as_ushort(__float2half_rn((float)byte_of(mnl, 0))) |
+                               ((uint32_t)__half_as_ushort(__float2half_rn((float)byte_of(mnl, 1))) << 16);
+                        m0.y = __half_as_ushort(__float2half_rn((float)byte_of(mnl, 2))) |
+                               ((uint32_t)__half_as_ushort(__float2half_rn((float)byte_of(mnl, 3))) << 16);
+                        m0.z = __half_as_ushort(__float2half_rn((float)byte_of(mnh, 0))) |
+                               ((uint32_t)__half_as_ushort(__float2half_rn((float)byte_of(mnh, 1))) << 16);
+                        m0.w = __half_as_ushort(__float2half_rn((float)byte_of(mnh, 2))) |
+                               ((uint32_t)__half_as_ushort(__float2half_rn((float)byte_of(mnh, 3))) << 16);
+                        uint8_t *am = smem + S::AMIN + ms * S::AMIN_BYTES + r * 16;
+                        *reinterpret_cast<uint4 *>(am) = m0;
+                        *reinterpret_cast<uint4 *>(am + 2048) = make_uint4(0, 0, 0, 0);
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&amin_full[ms]);
+                    }
+                }
+                if (s > s0) epilogue_sb(n - 1, pd, pdm, acc);
+                pd = d;
+                pdm = dm;
+            }
+            epilogue_sb(n - 1, pd, pdm, acc);
+
+            // ---- unit output ----
+            const int grp = 4 * rt + rg;
+            const int tok0 = tt * NT + half * H;
+            if (g.nsplit == 1) {
+                if (grp < g.groups) {
+#pragma unroll
+                    for (int t = 0; t < H; t++)
+                        if (tok0 + t < p.m) gemv_epilogue<EPI>(p, grp, tok0 + t, lane, acc[t] * tok_scale[tok0 + t]);
+                }
+            } else {
+                float *part = p.part + ((size_t)ks * g.mpad + tok0) * g.npad + 128 * rt + r;
+#pragma unroll
+                for (int t = 0; t < H; t++) __stcg(part + (size_t)t * g.npad, acc[t]);
+                __threadfence();
+                asm volatile("bar.sync 1, %0;" ::"r"(kDqWarps * 32) : "memory");
+                if (threadIdx.x == 0) {
+                    const unsigned tile = (unsigned)(tt * g.n_rt + rt);
+                    last_s = atomicAdd(&p.counters[tile], 1u) == (unsigned)(g.nsplit - 1);
+                    if (last_s) p.counters[tile] = 0;
+                }
+                asm volatile("bar.sync 1, %0;" ::"r"(kDqWarps * 32) : "memory");
+                if (last_s) {
+                    __threadfence();
+                    if (grp < g.groups) {
+                        const float *pp = p.part + (size_t)tok0 * g.npad + 128 * rt + r;
+#pragma unroll
+                        for (int t = 0; t < H; t++) {
+                            float tot = 0.0f;
+                            for (int k2 = 0; k2 < g.nsplit; k2++)
+                                tot += __ldcg(pp + ((size_t)k2 * g.mpad + t) * g.npad);
+                            if (tok0 + t < p.m) gemv_epilogue<EPI>(p, grp, tok0 + t, lane, tot * tok_scale[tok0 + t]);
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 9) {
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    }
+}
+
+}  // namespace qg
+}  // namespace nx

@@ -647,7 +647,17 @@ cudaError_t launch_gemv_fmt(const GemvParams &p, cudaStream_t st) {
     case 1: return launch_epi<FMT, 1>(p, st);
     case 2: return launch_epi<FMT, 2>(p, st);
     case 4: return launch_epi<FMT, 4>(p, st);
-    default: return cudaErrorInvalidValue;
+    default: {
+        // other batch sizes: slices of 4, then 2, then 1 tokens
+        if (p.m <= 0) return cudaErrorInvalidValue;
+        for (int t0 = 0; t0 < p.m;) {
+            const int r = p.m - t0, c = r >= 4 ? 4 : r >= 2 ? 2 : 1;
+            cudaError_t e = launch_gemv_fmt<FMT>(token_slice(p, t0, c), st);
+            if (e != cudaSuccess) return e;
+            t0 += c;
+        }
+        return cudaSuccess;
+    }
     }
 }
 

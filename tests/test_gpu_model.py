@@ -85,6 +85,28 @@ def test_tiny_decode_batch_matches_single(tiny_engine, oracle, tiny_path):
         assert tiny_engine.seq_len(s) == len(seqs[s]) + 1
 
 
+def test_tiny_decode_batch_tensor_core_path(nb, oracle, tiny_path):
+    """12 sequences in one decode batch run on the tcgen05 GEMM (batches of 8+);
+    every sequence's logits and greedy token match the oracle's single-stream decode."""
+    b = nb.CudaBackend(device=0, max_batch=16)
+    e = nb.InferenceEngine(b)
+    e.load_model(tiny_path)
+    seqs = [prompt(200 + s, 3 + s, 4096) for s in range(12)]
+    refs = []
+    for s, p in enumerate(seqs):
+        m = oracle.Model(tiny_path)
+        t = oracle.greedy(m.prefill(p))
+        refs.append((t, m.decode(t, len(p))))
+        e.prefill(p, seq_id=s)
+    items = [(s, refs[s][0], len(seqs[s])) for s in range(12)]
+    toks, logits = e.decode_batch(items, want_logits=True)
+    for s in range(12):
+        assert np.max(np.abs(logits[s] - refs[s][1])) < LOGIT_TOL, s
+        assert toks[s] == oracle.greedy(refs[s][1])
+    e.close()
+    b.close()
+
+
 @pytest.mark.parametrize("bits", [(4, 4), (3, 2)])
 def test_tiny_packed_kv(nb, oracle, tiny_path, bits):
     """Packed low-bit KV.  Packing itself is bit-exact (test_kv_quantize_bit_exact);
