@@ -193,9 +193,9 @@ def run_reference(args):
 
 
 def run_ncu_case(args):
-    """Small, fixed launch sequence for `ncu` captures: prefill 8 tokens as two
-    4-token steps (163 kernels each on the 8B shape), then ncu_steps
-    single-token decode steps from the captured graph."""
+    """Small, fixed launch sequence for `ncu` captures: prefill 8 tokens as one
+    8-token step on the tensor-core GEMM path, then ncu_steps single-token
+    decode steps from the captured graph (5 kernels per layer + 3 per step)."""
     import nexus_b200 as nb
     path = nb.model_path(args.config, threads=cpu_threads())
     backend = nb.CudaBackend(device=0, max_seq_len=64)
@@ -210,6 +210,55 @@ def run_ncu_case(args):
     return 0
 
 
+def run_batched(nb, L, path, batch: int, prompt_len: int, steps: int, warmup: int, device: int) -> dict:
+    """Config E at batch `batch`: every sequence gets its own random prompt of
+    `prompt_len` tokens (seed 1 + index), then `steps` decode steps each
+    advance all sequences by one token through nexus_cuda_decode_batch.  The
+    device time is the CUDA-event time of each batched step; the end-to-end
+    time is the host wall clock around the calls (token ids in, argmax ids out)."""
+    import torch
+    be = nb.CudaBackend(device=device, max_batch=batch, max_seq_len=prompt_len + steps + warmup + 8)
+    eng = nb.InferenceEngine(be)
+    eng.load_model(path)
+    V = eng.info.vocab_rows
+    toks, pos = [], []
+    t0 = time.perf_counter()
+    for s in range(batch):
+        p = np.random.default_rng(SEED_PROMPT + s).integers(0, V, prompt_len).tolist()
+        _, t = eng.prefill(p, seq_id=s, want_logits=False)
+        toks.append(t)
+        pos.append(prompt_len)
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+    prefill_ms_last = eng.last_step_ms()
+
+    def step():
+        nonlocal toks
+        items = [(s, toks[s], pos[s]) for s in range(batch)]
+        out, _ = eng.decode_batch(items, want_logits=False)
+        toks = [int(v) for v in out]
+        for s in range(batch):
+            pos[s] += 1
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    dev_ms = 0.0
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+        dev_ms += eng.last_step_ms()
+    wall = time.perf_counter() - t0
+    eng.close()
+    be.close()
+    return {"value": batch * steps / (dev_ms / 1000.0), "unit": "tok/s", "batch": batch, "steps": steps,
+            "ms_per_step": dev_ms / steps,
+            "e2e": {"value": batch * steps / wall, "unit": "tok/s", "h2d_bytes_per_step": 28 * batch,
+                    "d2h_bytes_per_step": 4 * batch},
+            "prefill": {"tokens": batch * prompt_len, "seconds": prefill_s,
+                        "tok_s": batch * prompt_len / prefill_s, "last_prompt_ms": prefill_ms_last}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -220,6 +269,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-budget", type=float, default=60.0)
     ap.add_argument("--profile-steps", type=int, default=4)
+    ap.add_argument("--batch", type=int, default=32, help="batched-decode measurement (config E at b=32); 1 = off")
     ap.add_argument("--ncu-steps", type=int, default=0,
                     help="profiling run for ncu: 8-token prefill (2 fused 4-token steps), then this many "
                          "device-chained decode steps; prints a short JSON line")
@@ -331,13 +381,19 @@ def main():
     launches_per_step = sum(r["launches"] for r in prof) / args.profile_steps
     line["gpu_launches"] = int(round(launches_per_step * args.steps))
 
+    eng.close()
+    backend.close()
+    # ---- b=32: one decode step advances 32 sequences (tensor-core GEMM path) ----
+    if args.batch > 1:
+        line["b32"] = run_batched(nb, L, path, args.batch, prompt_len=PROMPT_LEN, steps=min(args.steps, 32),
+                                  warmup=args.warmup, device=local)
+        line["metric"] = f"decode tok/s, Llama-3-8B-shape Q4_K, b=1 (b={args.batch} in b32)"
+
     if rank == 0 and not args.no_cpu_baseline:
         r = time_oracle(path, 64, 1, budget_s=20.0, threads=cpu_threads())
         line["cpu_baseline"] = {"value": r["tok_s"], "unit": "tok/s", "cores": r["threads"], "kind": "port",
                                 "sample": f"{r['steps']} decode steps of the same model after a 4-token prompt "
                                           "(oracle restatement of the reference CPU path)"}
-    eng.close()
-    backend.close()
     if dist is not None:
         barrier(dist, device)
         dist.destroy_process_group()

@@ -93,6 +93,25 @@ __device__ __forceinline__ void tma_load_1d(void *dst, const void *src, unsigned
         : "memory");
 }
 
+// Issue forms for a converged warp: one lane, chosen by elect.sync inside the
+// same asm block, arms the barrier or starts the copy (a lone divergent
+// thread issues these several times slower).
+__device__ __forceinline__ void expect_tx_w(unsigned long long *bar, unsigned bytes) {
+    asm volatile(
+        "{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n"
+        " @p mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n}\n" ::"r"(smem_u32(bar)),
+        "r"(bytes)
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_1d_w(void *dst, const void *src, unsigned bytes, unsigned long long *bar) {
+    asm volatile(
+        "{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n"
+        " @p cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n}\n" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

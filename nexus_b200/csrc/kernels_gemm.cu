@@ -21,7 +21,7 @@ __device__ __forceinline__ void q4k_kpos(int e, int &quarter, int &pos) {
 // keeping |x| < 2^10 (so the 32-element sub-block sums stay below 2^15, well
 // inside f16 range), the f16 hi/lo split, and the sub-block sums.  Image rows
 // per quarter: tokens' hi halves (rows 0..NT-1), then lo halves (NT..2NT-1).
-template <int NT>
+template <int FMT, int NT>
 __global__ void __launch_bounds__(256) k_gemm_prep(const float *__restrict__ x, int x_stride,
                                                    const float *__restrict__ norm_w, float eps, int m, int k,
                                                    uint8_t *__restrict__ bimg, float *__restrict__ tok_scale) {
@@ -77,11 +77,17 @@ __global__ void __launch_bounds__(256) k_gemm_prep(const float *__restrict__ x, 
         const __half lo = __float2half_rn(v - __half2float(hi));
         uint8_t *base = bimg + ((size_t)tt * n_sb + s) * bimg_sb_bytes(NT);
         int q, pos;
-        q4k_kpos(tid, q, pos);
+        if constexpr (FMT == 12) {
+            q4k_kpos(tid, q, pos);
+        } else {
+            q = tid >> 6;  // natural K order
+            pos = tid & 63;
+        }
         // K-chunk (pos/8) of 2NT rows x 16 B; hi in row n, lo in row NT + n
         uint8_t *qb = base + q * NT * 256 + (pos >> 3) * NT * 32 + n * 16 + (pos & 7) * 2;
         *reinterpret_cast<__half *>(qb) = hi;
         *reinterpret_cast<__half *>(qb + NT * 16) = lo;
+        if constexpr (!GemmFmt<FMT>::MIN) continue;
         // sub-block sums (sub-block j = elements 32j..32j+31 = warp j): K
         // positions 0..7 of the min operand, positions 8..15 zero
         const float sj = warp_sum(v);
@@ -134,9 +140,8 @@ static GemmShape plan(int m, int n, int k) {
     return g;
 }
 
-template <int NT, int EPI>
+template <int FMT, int NT, int EPI>
 static cudaError_t launch_nt_epi(const GemvParams &p, const GemmScratch &sc, cudaStream_t st) {
-    constexpr int FMT = 12;
     using S = Smem<FMT, NT>;
     GemmShape g = plan(p.m, p.n, p.k);
     const int sms = sm_count_cached();
@@ -150,7 +155,7 @@ static cudaError_t launch_nt_epi(const GemvParams &p, const GemmScratch &sc, cud
     if (!sc.bimg || need > sc.bimg_bytes || !sc.tok_scale || (size_t)g.mpad > sc.tok_scale_floats)
         return cudaErrorInvalidValue;
     dim3 pg(g.mpad, (g.n_sb + 3) / 4);
-    k_gemm_prep<NT><<<pg, 256, 0, st>>>(p.x, p.x_stride, p.norm_w, p.eps, p.m, p.k, sc.bimg, sc.tok_scale);
+    k_gemm_prep<FMT, NT><<<pg, 256, 0, st>>>(p.x, p.x_stride, p.norm_w, p.eps, p.m, p.k, sc.bimg, sc.tok_scale);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     auto fn = k_qgemm<FMT, NT, EPI>;
@@ -162,21 +167,26 @@ static cudaError_t launch_nt_epi(const GemvParams &p, const GemmScratch &sc, cud
     return cudaGetLastError();
 }
 
-template <int NT>
+template <int FMT, int NT>
 static cudaError_t launch_nt(const GemvParams &p, const GemmScratch &sc, cudaStream_t st) {
     switch (p.epi) {
-    case EPI_STORE: return launch_nt_epi<NT, EPI_STORE>(p, sc, st);
-    case EPI_ADD: return launch_nt_epi<NT, EPI_ADD>(p, sc, st);
-    case EPI_SWIGLU: return launch_nt_epi<NT, EPI_SWIGLU>(p, sc, st);
-    case EPI_QKV: return launch_nt_epi<NT, EPI_QKV>(p, sc, st);
-    case EPI_ARGMAX: return launch_nt_epi<NT, EPI_ARGMAX>(p, sc, st);
+    case EPI_STORE: return launch_nt_epi<FMT, NT, EPI_STORE>(p, sc, st);
+    case EPI_ADD: return launch_nt_epi<FMT, NT, EPI_ADD>(p, sc, st);
+    case EPI_SWIGLU: return launch_nt_epi<FMT, NT, EPI_SWIGLU>(p, sc, st);
+    case EPI_QKV: return launch_nt_epi<FMT, NT, EPI_QKV>(p, sc, st);
+    case EPI_ARGMAX: return launch_nt_epi<FMT, NT, EPI_ARGMAX>(p, sc, st);
     default: return cudaErrorInvalidValue;
     }
 }
 
+template <int FMT>
+static cudaError_t launch_fmt(const GemvParams &p, const GemmScratch &sc, cudaStream_t st) {
+    return p.m <= 16 ? launch_nt<FMT, 16>(p, sc, st) : launch_nt<FMT, 32>(p, sc, st);
+}
+
 }  // namespace qg
 
-bool gemm_supported(int fmt) { return fmt == 12; }
+bool gemm_supported(int fmt) { return fmt == 12 || fmt == 8; }
 
 GemmScratchSize gemm_scratch_size(int m, int n, int k) {
     const qg::GemmShape g = qg::plan(m, n, k);
@@ -191,7 +201,7 @@ GemmScratchSize gemm_scratch_size(int m, int n, int k) {
 
 cudaError_t launch_gemm(const GemvParams &p, const GemmScratch &sc, cudaStream_t st) {
     if (!gemm_supported(p.fmt) || p.k % 256 != 0 || p.n <= 0 || p.m <= 0) return cudaErrorInvalidValue;
-    return p.m <= 16 ? qg::launch_nt<16>(p, sc, st) : qg::launch_nt<32>(p, sc, st);
+    return p.fmt == 12 ? qg::launch_fmt<12>(p, sc, st) : qg::launch_fmt<8>(p, sc, st);
 }
 
 }  // namespace nx

@@ -44,12 +44,29 @@
 namespace nx {
 namespace qg {
 
-constexpr int kRawSlots = 3;   // raw weight tiles (one super-block of 4 row groups each)
-constexpr int kASlots = 6;     // dequantized quarter stages
 constexpr int kQuarters = 4;
 constexpr int kDqWarps = 8;
 constexpr int kThreads = (kDqWarps + 3) * 32;
 constexpr unsigned kSpin = 1u << 22;
+
+// Per-format scheme.  Super-block formats (Q4_K) multiply exact integers
+// sc_j*q with a min operand and scale per super-block in the epilogue; the
+// block formats (Q8_0) put the whole weight d*q into A as an exact f16 pair
+// hi + lo (two MMAs per K step, no min term, no per-super-block scale).
+template <int FMT>
+struct GemmFmt;
+template <>
+struct GemmFmt<12> {  // Q4_K
+    static constexpr bool MIN = true;
+    static constexpr int A_MATS = 1;
+    static constexpr int RAW_SLOTS = 3, STAGES = 6;
+};
+template <>
+struct GemmFmt<8> {  // Q8_0
+    static constexpr bool MIN = false;
+    static constexpr int A_MATS = 2;
+    static constexpr int RAW_SLOTS = 2, STAGES = 3;
+};
 
 template <int FMT>
 struct Raw {
@@ -60,22 +77,27 @@ struct Raw {
 
 // Bytes of the prepared activations of one (token tile, super-block):
 // 4 quarters x 8 K-chunks x 2NT rows (hi, lo) x 16 B, then the sub-block
-// sums: 2 K-chunks x 2NT rows x 16 B.
+// sums: 2 K-chunks x 2NT rows x 16 B (used by formats with a min term).
 __host__ __device__ constexpr int bimg_sb_bytes(int nt) { return nt * 1088; }
 
-// Shared memory: independent rings for the raw weights, the dequantized
-// quarter stages (A), the prepared activations (B, one quarter per slot) and
-// the per-super-block min operands, so every load runs ahead of the MMAs.
+// Shared memory: a ring of raw weight tiles (one super-block of 4 row
+// groups per slot), a ring of quarter stages (the dequantized A matrix of 64 K
+// and the prepared activations B of the same K; one full and one empty
+// barrier per stage, signalled by the dequant warps and the B copy together),
+// and two slots of the per-super-block min operands.
 template <int FMT, int NT>
 struct Smem {
-    static constexpr int BSLOTS = NT == 16 ? 8 : 6;
-    static constexpr int A_BYTES = 8 * 128 * 16;
+    using GF = GemmFmt<FMT>;
+    static constexpr int RSLOTS = GF::RAW_SLOTS, ASLOTS = GF::STAGES;
+    static constexpr int BSLOTS = GF::STAGES;
+    static constexpr int A_MAT = 8 * 128 * 16;          // one 128 x 64 f16 matrix
+    static constexpr int A_BYTES = GF::A_MATS * A_MAT;  // one quarter stage
     static constexpr int B_BYTES = NT * 256;
-    static constexpr int AMIN_BYTES = 2 * 128 * 16;
-    static constexpr int BMIN_BYTES = NT * 64;
+    static constexpr int AMIN_BYTES = GF::MIN ? 2 * 128 * 16 : 0;
+    static constexpr int BMIN_BYTES = GF::MIN ? NT * 64 : 0;
     static constexpr int RAW = 0;
-    static constexpr int A = RAW + kRawSlots * Raw<FMT>::SLOT;
-    static constexpr int B = A + kASlots * A_BYTES;
+    static constexpr int A = RAW + RSLOTS * Raw<FMT>::SLOT;
+    static constexpr int B = A + ASLOTS * A_BYTES;
     static constexpr int AMIN = B + BSLOTS * B_BYTES;
     static constexpr int BMIN = AMIN + 2 * AMIN_BYTES;
     static constexpr int TOTAL = BMIN + 2 * BMIN_BYTES + 1024;  // + alignment slack
@@ -105,6 +127,22 @@ __device__ __forceinline__ void umma_f16(uint32_t dt, uint64_t ad, uint64_t bd, 
 __device__ __forceinline__ void umma_commit(unsigned long long *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
+}
+// Issue forms for a converged warp: one lane, chosen by elect.sync inside the
+// same asm block, issues the instruction.  Issuing from a converged warp keeps
+// the operands warp-uniform; a lone divergent thread issues several times slower.
+__device__ __forceinline__ void umma_f16_w(uint32_t dt, uint64_t ad, uint64_t bd, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p, q;\n elect.sync _|p, 0xffffffff;\n setp.ne.b32 q, %4, 0;\n"
+        " @p tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, q;\n}\n" ::"r"(dt),
+        "l"(ad), "l"(bd), "r"(idesc), "r"(acc), "r"(0u)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit_w(unsigned long long *bar) {
+    asm volatile(
+        "{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n"
+        " @p tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}\n" ::"r"(smem_u32(bar))
+        : "memory");
 }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -207,10 +245,46 @@ __device__ __forceinline__ void dq_q4k_quarter(const uint32_t (&w)[8], uint32_t 
     }
 }
 
+// Q8_0 dequantization of one quarter (blocks 2q and 2q+1 of the row, K in
+// natural order) into the stage's hi and lo matrices: w = d*q exactly as
+// hi + lo, hi = f16(d*q), lo = f16(d*q - hi) (one fma).
+__device__ __forceinline__ void dq_q80_quarter(const uint32_t (&w)[16], uint32_t d01, uint8_t *a_row) {
+    const uint32_t bias = 0x64806480u;  // f16x2 (1152, 1152): (1024 + (q ^ 0x80)) - 1152 = q
+#pragma unroll
+    for (int b = 0; b < 2; b++) {
+        const uint32_t dh = (d01 >> (16 * b)) & 0xffffu;
+        const uint32_t d2 = dh | (dh << 16);
+#pragma unroll
+        for (int kc = 0; kc < 4; kc++) {
+            uint32_t hv[4], lv[4];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const uint32_t u = w[8 * b + 2 * kc + h] ^ 0x80808080u;
+                uint32_t p01, p23;
+                asm("prmt.b32 %0, %1, 0x64646464, 0x4140;" : "=r"(p01) : "r"(u));
+                asm("prmt.b32 %0, %1, 0x64646464, 0x4342;" : "=r"(p23) : "r"(u));
+                uint32_t q01, q23;
+                asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(q01) : "r"(p01), "r"(bias));
+                asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(q23) : "r"(p23), "r"(bias));
+                uint32_t h01, h23;
+                asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(h01) : "r"(q01), "r"(d2));
+                asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(h23) : "r"(q23), "r"(d2));
+                hv[2 * h] = h01;
+                hv[2 * h + 1] = h23;
+                lv[2 * h] = hfma2u(q01, d2, h01 ^ 0x80008000u);
+                lv[2 * h + 1] = hfma2u(q23, d2, h23 ^ 0x80008000u);
+            }
+            const int chunk = 4 * b + kc;
+            *reinterpret_cast<uint4 *>(a_row + chunk * 2048) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+            *reinterpret_cast<uint4 *>(a_row + 16384 + chunk * 2048) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+        }
+    }
+}
+
 template <int FMT, int NT, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     k_qgemm(GemvParams p, GemmShape g, const uint8_t *__restrict__ bimg, const float *__restrict__ tok_scale) {
-    static_assert(FMT == 12, "tcgen05 GEMM: Q4_K");
+    using GF = GemmFmt<FMT>;
     static_assert(NT == 16 || NT == 32, "token tile");
     using S = Smem<FMT, NT>;
     using R = Raw<FMT>;
@@ -218,10 +292,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int NB = S::BSLOTS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    constexpr int kRawSlots = S::RSLOTS, kASlots = S::ASLOTS;
     __shared__ unsigned long long raw_full[kRawSlots], raw_empty[kRawSlots];
-    __shared__ unsigned long long a_full[kASlots], a_empty[kASlots];
-    __shared__ unsigned long long b_full[NB], b_empty[NB];
-    __shared__ unsigned long long amin_full[2], bmin_full[2], min_empty[2];
+    __shared__ unsigned long long st_full[kASlots], st_empty[kASlots];
+    __shared__ unsigned long long mn_full[2], mn_empty[2];
     __shared__ unsigned long long acc_full[2], acc_empty[2], mma_done;
     __shared__ uint32_t tmem_base_s;
     __shared__ volatile int abort_s;
@@ -238,17 +312,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&raw_empty[i], kDqWarps);
         }
         for (int i = 0; i < kASlots; i++) {
-            mbar_init(&a_full[i], 4);
-            mbar_init(&a_empty[i], 1);
-        }
-        for (int i = 0; i < NB; i++) {
-            mbar_init(&b_full[i], 1);
-            mbar_init(&b_empty[i], 1);
+            mbar_init(&st_full[i], 4 + 1);  // 4 dequant warps + the activation copy
+            mbar_init(&st_empty[i], 1);
         }
         for (int i = 0; i < 2; i++) {
-            mbar_init(&amin_full[i], 4);
-            mbar_init(&bmin_full[i], 1);
-            mbar_init(&min_empty[i], 1);
+            mbar_init(&mn_full[i], 4 + 1);
+            mbar_init(&mn_empty[i], 1);
             mbar_init(&acc_full[i], 1);
             mbar_init(&acc_empty[i], kDqWarps);
         }
@@ -268,26 +337,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = tmem_base_s;
 
     if (warp == 8) {
-        // ---- raw weight tiles: 4 row groups of one super-block per slot ----
-        if (lane == 0) {
-            unsigned n = 0;
-            for (int u = blockIdx.x; u < n_units && !abort_s; u += gridDim.x) {
-                int tt, rt, ks, s0, s1;
-                unit_coords(g, u, tt, rt, ks, s0, s1);
-                for (int s = s0; s < s1; s++, n++) {
-                    const int slot = n % kRawSlots;
-                    if (!bwait(&raw_empty[slot], ((n / kRawSlots) & 1) ^ 1, &abort_s, p.err)) break;
-                    const int ng = min(4, g.groups - 4 * rt);
-                    mbar_expect_tx(&raw_full[slot], (unsigned)(ng * (R::ITEM + R::AUXB)));
-                    uint8_t *dst = smem + S::RAW + slot * R::SLOT;
-                    for (int gi = 0; gi < ng; gi++) {
-                        const size_t item = (size_t)(4 * rt + gi) * g.n_sb + s;
-                        tma_load_1d(dst + gi * R::ITEM, reinterpret_cast<const uint8_t *>(p.w_main) + item * R::ITEM,
-                                    R::ITEM, &raw_full[slot]);
-                    }
+        // ---- raw weight tiles: 4 row groups of one super-block per slot (whole warp, elected issue) ----
+        unsigned n = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+            int tt, rt, ks, s0, s1;
+            unit_coords(g, u, tt, rt, ks, s0, s1);
+            for (int s = s0; s < s1; s++, n++) {
+                const int slot = n % kRawSlots;
+                ok = __all_sync(0xffffffffu, bwait(&raw_empty[slot], ((n / kRawSlots) & 1) ^ 1, &abort_s, p.err));
+                if (!ok) break;
+                const int ng = min(4, g.groups - 4 * rt);
+                expect_tx_w(&raw_full[slot], (unsigned)(ng * (R::ITEM + R::AUXB)));
+                uint8_t *dst = smem + S::RAW + slot * R::SLOT;
+                for (int gi = 0; gi < ng; gi++) {
+                    const size_t item = (size_t)(4 * rt + gi) * g.n_sb + s;
+                    tma_load_1d_w(dst + gi * R::ITEM, reinterpret_cast<const uint8_t *>(p.w_main) + item * R::ITEM,
+                                  R::ITEM, &raw_full[slot]);
                 }
             }
-            // copies still in flight land before the CTA exits
+        }
+        // copies still in flight land before the CTA exits
+        if (lane == 0) {
             for (int sl = 0; sl < kRawSlots; sl++) {
                 if ((unsigned)sl < n) {
                     const unsigned fills = (n - 1 - sl) / kRawSlots + 1;
@@ -299,96 +370,104 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 9) {
         // ---- prepared activations: one quarter per slot, sub-block sums per super-block ----
-        if (lane == 0) {
-            unsigned n = 0, c = 0;
-            bool ok = true;
-            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-                int tt, rt, ks, s0, s1;
-                unit_coords(g, u, tt, rt, ks, s0, s1);
-                for (int s = s0; s < s1 && ok; s++, n++) {
-                    const uint8_t *src = bimg + ((size_t)tt * g.n_sb + s) * bimg_sb_bytes(NT);
-                    for (int q = 0; q < kQuarters; q++, c++) {
-                        const int slot = c % NB;
-                        if (!(ok = bwait(&b_empty[slot], ((c / NB) & 1) ^ 1, &abort_s, p.err))) break;
-                        mbar_expect_tx(&b_full[slot], S::B_BYTES);
-                        tma_load_1d(smem + S::B + slot * S::B_BYTES, src + q * S::B_BYTES, S::B_BYTES, &b_full[slot]);
-                        if (q == 0) {
-                            const int ms = n & 1;
-                            if (!(ok = bwait(&min_empty[ms], ((n >> 1) & 1) ^ 1, &abort_s, p.err))) break;
-                            mbar_expect_tx(&bmin_full[ms], S::BMIN_BYTES);
-                            tma_load_1d(smem + S::BMIN + ms * S::BMIN_BYTES, src + kQuarters * S::B_BYTES,
-                                        S::BMIN_BYTES, &bmin_full[ms]);
-                        }
+        unsigned n = 0, c = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+            int tt, rt, ks, s0, s1;
+            unit_coords(g, u, tt, rt, ks, s0, s1);
+            for (int s = s0; s < s1 && ok; s++, n++) {
+                const uint8_t *src = bimg + ((size_t)tt * g.n_sb + s) * bimg_sb_bytes(NT);
+                for (int q = 0; q < kQuarters; q++, c++) {
+                    const int slot = c % NB;
+                    ok = __all_sync(0xffffffffu, bwait(&st_empty[slot], ((c / NB) & 1) ^ 1, &abort_s, p.err));
+                    if (!ok) break;
+                    expect_tx_w(&st_full[slot], S::B_BYTES);
+                    tma_load_1d_w(smem + S::B + slot * S::B_BYTES, src + q * S::B_BYTES, S::B_BYTES, &st_full[slot]);
+                    if (GF::MIN && q == 0) {
+                        const int ms = n & 1;
+                        ok = __all_sync(0xffffffffu, bwait(&mn_empty[ms], ((n >> 1) & 1) ^ 1, &abort_s, p.err));
+                        if (!ok) break;
+                        expect_tx_w(&mn_full[ms], S::BMIN_BYTES);
+                        tma_load_1d_w(smem + S::BMIN + ms * S::BMIN_BYTES, src + kQuarters * S::B_BYTES,
+                                      S::BMIN_BYTES, &mn_full[ms]);
                     }
                 }
             }
-            // copies still in flight land before the CTA exits
+        }
+        // copies still in flight land before the CTA exits
+        if (lane == 0) {
             for (int sl = 0; sl < NB; sl++) {
                 if ((unsigned)sl < c) {
                     const unsigned fills = (c - 1 - sl) / NB + 1;
                     unsigned k = 0;
-                    while (!mbar_try_wait(&b_full[sl], (fills - 1) & 1) && ++k < kSpin) {
+                    while (!mbar_try_wait(&st_full[sl], (fills - 1) & 1) && ++k < kSpin) {
                     }
                 }
             }
-            for (int ms = 0; ms < 2; ms++) {
+            for (int ms = 0; ms < 2 && GF::MIN; ms++) {
                 if ((unsigned)ms < n) {
                     const unsigned fills = (n - 1 - ms) / 2 + 1;
                     unsigned k = 0;
-                    while (!mbar_try_wait(&bmin_full[ms], (fills - 1) & 1) && ++k < kSpin) {
+                    while (!mbar_try_wait(&mn_full[ms], (fills - 1) & 1) && ++k < kSpin) {
                     }
                 }
             }
         }
     } else if (warp == 10) {
-        // ---- MMA issue ----
-        if (lane == 0) {
-            constexpr uint32_t idesc = umma_idesc<2 * NT>();
-            const uint32_t a0 = smem_u32(smem + S::A), b0 = smem_u32(smem + S::B);
-            const uint32_t amin0 = smem_u32(smem + S::AMIN), bmin0 = smem_u32(smem + S::BMIN);
-            unsigned n = 0, c = 0;
-            bool ok = true;
-            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-                int tt, rt, ks, s0, s1;
-                unit_coords(g, u, tt, rt, ks, s0, s1);
-                for (int s = s0; s < s1 && ok; s++, n++) {
-                    const int ab = n & 1;
-                    const uint32_t dcol = tmem + ab * 4 * NT, ecol = dcol + 2 * NT;
-                    if (!(ok = bwait(&acc_empty[ab], ((n >> 1) & 1) ^ 1, &abort_s, p.err))) break;
+        // ---- MMA issue (whole warp, elected lane) ----
+        constexpr uint32_t idesc = umma_idesc<2 * NT>();
+        const uint32_t a0 = smem_u32(smem + S::A), b0 = smem_u32(smem + S::B);
+        const uint32_t amin0 = smem_u32(smem + S::AMIN), bmin0 = smem_u32(smem + S::BMIN);
+        unsigned n = 0, c = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+            int tt, rt, ks, s0, s1;
+            unit_coords(g, u, tt, rt, ks, s0, s1);
+            for (int s = s0; s < s1 && ok; s++, n++) {
+                const int ab = n & 1;
+                const uint32_t dcol = tmem + ab * 4 * NT, ecol = dcol + 2 * NT;
+                ok = __all_sync(0xffffffffu, bwait(&acc_empty[ab], ((n >> 1) & 1) ^ 1, &abort_s, p.err));
+                if (!ok) break;
+                tc_fence_after();
+                for (int q = 0; q < kQuarters; q++, c++) {
+                    const int as = c % kASlots, bs = as;
+                    ok = __all_sync(0xffffffffu, bwait(&st_full[as], (c / kASlots) & 1, &abort_s, p.err));
+                    if (!ok) break;
                     tc_fence_after();
-                    for (int q = 0; q < kQuarters; q++, c++) {
-                        const int as = c % kASlots, bs = c % NB;
-                        if (!(ok = bwait(&a_full[as], (c / kASlots) & 1, &abort_s, p.err))) break;
-                        if (!(ok = bwait(&b_full[bs], (c / NB) & 1, &abort_s, p.err))) break;
-                        tc_fence_after();
 #pragma unroll
-                        for (int kk = 0; kk < 4; kk++) {
-                            const uint64_t ad = umma_desc(a0 + as * S::A_BYTES + kk * 2 * 2048, 2048, 128);
-                            const uint32_t bq = b0 + bs * S::B_BYTES + kk * 2 * NT * 32;
-                            umma_f16(dcol, ad, umma_desc(bq, NT * 32, 128), idesc, (q | kk) != 0);
-                        }
-                        umma_commit(&a_empty[as]);
-                        umma_commit(&b_empty[bs]);
-                        if (q == 0) {
-                            const int ms = n & 1;
-                            if (!(ok = bwait(&amin_full[ms], (n >> 1) & 1, &abort_s, p.err))) break;
-                            if (!(ok = bwait(&bmin_full[ms], (n >> 1) & 1, &abort_s, p.err))) break;
-                            tc_fence_after();
-                            const uint64_t ad = umma_desc(amin0 + ms * S::AMIN_BYTES, 2048, 128);
-                            const uint32_t bm = bmin0 + ms * S::BMIN_BYTES;
-                            umma_f16(ecol, ad, umma_desc(bm, NT * 32, 128), idesc, 0);
-                            umma_commit(&min_empty[ms]);
+                    for (int kk = 0; kk < 4; kk++) {
+                        const uint32_t bq = b0 + bs * S::B_BYTES + kk * 2 * NT * 32;
+                        const uint64_t bd = umma_desc(bq, NT * 32, 128);
+#pragma unroll
+                        for (int am = 0; am < GF::A_MATS; am++) {
+                            const uint64_t ad =
+                                umma_desc(a0 + as * S::A_BYTES + am * S::A_MAT + kk * 2 * 2048, 2048, 128);
+                            umma_f16_w(dcol, ad, bd, idesc, (q | kk | am) != 0);
                         }
                     }
-                    if (ok) umma_commit(&acc_full[ab]);
+                    umma_commit_w(&st_empty[as]);
+                    if (GF::MIN && q == 0) {
+                        const int ms = n & 1;
+                        ok = __all_sync(0xffffffffu, bwait(&mn_full[ms], (n >> 1) & 1, &abort_s, p.err));
+                        if (!ok) break;
+                        tc_fence_after();
+                        const uint64_t ad = umma_desc(amin0 + ms * S::AMIN_BYTES, 2048, 128);
+                        const uint32_t bm = bmin0 + ms * S::BMIN_BYTES;
+                        umma_f16_w(ecol, ad, umma_desc(bm, NT * 32, 128), idesc, 0);
+                        umma_commit_w(&mn_empty[ms]);
+                    }
                 }
+                if (ok) umma_commit_w(&acc_full[ab]);
             }
-            // all MMAs issued so far have completed before TMEM is released
-            umma_commit(&mma_done);
+        }
+        // all MMAs issued so far have completed before TMEM is released
+        umma_commit_w(&mma_done);
+        if (lane == 0) {
             unsigned k = 0;
             while (!mbar_try_wait(&mma_done, 0) && ++k < kSpin) {
             }
         }
+        __syncwarp();
     } else {
         // ---- dequantization + epilogue (warps 0-7) ----
         const int rg = warp & 3, half = warp >> 2;
@@ -405,14 +484,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t col = tmem + t_lane + ab * 4 * NT + half * H;
             tmem_ld<H>(col, dh);
             tmem_ld<H>(col + NT, dl);
-            tmem_ld<H>(col + 2 * NT, eh);
-            tmem_ld<H>(col + 3 * NT, el);
+            if constexpr (GF::MIN) {
+                tmem_ld<H>(col + 2 * NT, eh);
+                tmem_ld<H>(col + 3 * NT, el);
+            }
             tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[ab]);
+            if constexpr (GF::MIN) {
 #pragma unroll
-            for (int t = 0; t < H; t++) acc[t] = fmaf(d, dh[t] + dl[t], fmaf(-dm, eh[t] + el[t], acc[t]));
+                for (int t = 0; t < H; t++) acc[t] = fmaf(d, dh[t] + dl[t], fmaf(-dm, eh[t] + el[t], acc[t]));
+            } else {
+#pragma unroll
+                for (int t = 0; t < H; t++) acc[t] += dh[t] + dl[t];
+            }
         };
         for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
             int tt, rt, ks, s0, s1;
@@ -424,55 +510,88 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int slot = n % kRawSlots;
                 bwait(&raw_full[slot], (n / kRawSlots) & 1, &abort_s, p.err);
                 const uint8_t *rawp = smem + S::RAW + slot * R::SLOT + rg * R::ITEM + lane * 16;
-                const uint4 c0 = *reinterpret_cast<const uint4 *>(rawp);
-                uint32_t wq[16];
+                float d = 1.0f, dm = 0.0f;
+                if constexpr (FMT == 12) {
+                    const uint4 c0 = *reinterpret_cast<const uint4 *>(rawp);
+                    uint32_t wq[16];
 #pragma unroll
-                for (int c = 0; c < 4; c++) {
-                    const uint4 v = *reinterpret_cast<const uint4 *>(rawp + (1 + 4 * half + c) * 512);
-                    wq[4 * c] = v.x;
-                    wq[4 * c + 1] = v.y;
-                    wq[4 * c + 2] = v.z;
-                    wq[4 * c + 3] = v.w;
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&raw_empty[slot]);
-                const float d = h2f_bits(c0.x), dm = h2f_bits(c0.x >> 16);
-                // unpack_q4_k_scales (src/gguf/mod.rs:1547-1554)
-                const uint32_t scl = c0.y & 0x3f3f3f3fu, mnl = c0.z & 0x3f3f3f3fu;
-                const uint32_t sch = (c0.w & 0x0f0f0f0fu) | ((c0.y >> 2) & 0x30303030u);
-                const uint32_t mnh = ((c0.w >> 4) & 0x0f0f0f0fu) | ((c0.z >> 2) & 0x30303030u);
-#pragma unroll
-                for (int qq = 0; qq < 2; qq++) {
-                    const int q = 2 * half + qq;
-                    const unsigned c = 4 * n + q;
-                    const int as = c % kASlots;
-                    bwait(&a_empty[as], ((c / kASlots) & 1) ^ 1, &abort_s, p.err);
-                    uint32_t w8[8];
-#pragma unroll
-                    for (int i = 0; i < 8; i++) w8[i] = wq[8 * qq + i];
-                    dq_q4k_quarter(w8, byte_of(scl, q), byte_of(sch, q), smem + S::A + as * S::A_BYTES + r * 16);
-                    fence_proxy_async_smem();
+                    for (int c = 0; c < 4; c++) {
+                        const uint4 v = *reinterpret_cast<const uint4 *>(rawp + (1 + 4 * half + c) * 512);
+                        wq[4 * c] = v.x;
+                        wq[4 * c + 1] = v.y;
+                        wq[4 * c + 2] = v.z;
+                        wq[4 * c + 3] = v.w;
+                    }
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&a_full[as]);
-                    if (q == 0) {
-                        // Amin row: m_0..m_7, then eight zeros
-                        const int ms = n & 1;
-                        bwait(&min_empty[ms], ((n >> 1) & 1) ^ 1, &abort_s, p.err);
-                        uint4 m0;
-                        m0.x = __half_as_ushort(__float2half_rn((float)byte_of(mnl, 0))) |
-                               ((uint32_t)__half_as_ushort(__float2half_rn((float)byte_of(mnl, 1))) << 16);
-                        m0.y = __half_as_ushort(__float2half_rn((float)byte_of(mnl, 2))) |
-                               ((uint32_t)__half_as_ushort(__float2half_rn((float)byte_of(mnl, 3))) << 16);
-                        m0.z = __half_as_ushort(__float2half_rn((float)byte_of(mnh, 0))) |
-                               ((uint32_t)__half_as_ushort(__float2half_rn((float)byte_of(mnh, 1))) << 16);
-                        m0.w = __half_as_ushort(__float2half_rn((float)byte_of(mnh, 2))) |
-                               ((uint32_t)__half_as_ushort(__float2half_rn((float)byte_of(mnh, 3))) << 16);
-                        uint8_t *am = smem + S::AMIN + ms * S::AMIN_BYTES + r * 16;
-                        *reinterpret_cast<uint4 *>(am) = m0;
-                        *reinterpret_cast<uint4 *>(am + 2048) = make_uint4(0, 0, 0, 0);
+                    if (lane == 0) mbar_arrive(&raw_empty[slot]);
+                    d = h2f_bits(c0.x);
+                    dm = h2f_bits(c0.x >> 16);
+                    // unpack_q4_k_scales (src/gguf/mod.rs:1547-1554)
+                    const uint32_t scl = c0.y & 0x3f3f3f3fu, mnl = c0.z & 0x3f3f3f3fu;
+                    const uint32_t sch = (c0.w & 0x0f0f0f0fu) | ((c0.y >> 2) & 0x30303030u);
+                    const uint32_t mnh = ((c0.w >> 4) & 0x0f0f0f0fu) | ((c0.z >> 2) & 0x30303030u);
+#pragma unroll
+                    for (int qq = 0; qq < 2; qq++) {
+                        const int q = 2 * half + qq;
+                        const unsigned c = 4 * n + q;
+                        const int as = c % kASlots;
+                        bwait(&st_empty[as], ((c / kASlots) & 1) ^ 1, &abort_s, p.err);
+                        uint32_t w8[8];
+#pragma unroll
+                        for (int i = 0; i < 8; i++) w8[i] = wq[8 * qq + i];
+                        dq_q4k_quarter(w8, byte_of(scl, q), byte_of(sch, q), smem + S::A + as * S::A_BYTES + r * 16);
                         fence_proxy_async_smem();
                         __syncwarp();
-                        if (lane == 0) mbar_arrive(&amin_full[ms]);
+                        if (lane == 0) mbar_arrive(&st_full[as]);
+                        if (q == 0) {
+                            // Amin row: m_0..m_7, then eight zeros
+                            const int ms = n & 1;
+                            bwait(&mn_empty[ms], ((n >> 1) & 1) ^ 1, &abort_s, p.err);
+                            uint4 m0;
+                            m0.x = __half_as_ushort(__float2half_rn((float)byte_of(mnl, 0))) |
+                                   ((uint32_t)__half_as_ushort(__float2half_rn((float)byte_of(mnl, 1))) << 16);
+                            m0.y = __half_as_ushort(__float2half_rn((float)byte_of(mnl, 2))) |
+                                   ((uint32_t)__half_as_ushort(__float2half_rn((float)byte_of(mnl, 3))) << 16);
+                            m0.z = __half_as_ushort(__float2half_rn((float)byte_of(mnh, 0))) |
+                                   ((uint32_t)__half_as_ushort(__float2half_rn((float)byte_of(mnh, 1))) << 16);
+                            m0.w = __half_as_ushort(__float2half_rn((float)byte_of(mnh, 2))) |
+                                   ((uint32_t)__half_as_ushort(__float2half_rn((float)byte_of(mnh, 3))) << 16);
+                            uint8_t *am = smem + S::AMIN + ms * S::AMIN_BYTES + r * 16;
+                            *reinterpret_cast<uint4 *>(am) = m0;
+                            *reinterpret_cast<uint4 *>(am + 2048) = make_uint4(0, 0, 0, 0);
+                            fence_proxy_async_smem();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&mn_full[ms]);
+                        }
+                    }
+                } else {
+                    // Q8_0: chunk 0 = the eight block scales, chunks 1+2b, 2+2b = qs of block b
+                    const uint4 c0 = *reinterpret_cast<const uint4 *>(rawp);
+                    uint32_t wq[32];
+#pragma unroll
+                    for (int c = 0; c < 8; c++) {
+                        const uint4 v = *reinterpret_cast<const uint4 *>(rawp + (1 + 8 * half + c) * 512);
+                        wq[4 * c] = v.x;
+                        wq[4 * c + 1] = v.y;
+                        wq[4 * c + 2] = v.z;
+                        wq[4 * c + 3] = v.w;
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&raw_empty[slot]);
+                    const uint32_t dsc[4] = {c0.x, c0.y, c0.z, c0.w};
+#pragma unroll
+                    for (int qq = 0; qq < 2; qq++) {
+                        const int q = 2 * half + qq;
+                        const unsigned c = 4 * n + q;
+                        const int as = c % kASlots;
+                        bwait(&st_empty[as], ((c / kASlots) & 1) ^ 1, &abort_s, p.err);
+                        uint32_t w16[16];
+#pragma unroll
+                        for (int i = 0; i < 16; i++) w16[i] = wq[16 * qq + i];
+                        dq_q80_quarter(w16, half ? dsc[2 + qq] : dsc[qq], smem + S::A + as * S::A_BYTES + r * 16);
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&st_full[as]);
                     }
                 }
                 if (s > s0) epilogue_sb(n - 1, pd, pdm, acc);

@@ -102,38 +102,41 @@ def test_qmatvec_input_edge_cases(backend, oracle, nb):
         assert rel_err(y[t], oracle.qmatvec(oracle.Q4_K, q, n, k, x[t])) < REL_TOL
 
 
+@pytest.mark.parametrize("fmt", ["Q4_K", "Q8_0"])
 @pytest.mark.parametrize("m", [8, 16, 17, 64])
 @pytest.mark.parametrize("shape", [(4096, 4096), (1024, 4096), (4096, 14336)], ids=lambda s: f"{s[0]}x{s[1]}")
-def test_qgemm_batched_q4k(backend, oracle, nb, shape, m):
-    """Batches of 8+ tokens run on the tcgen05 GEMM; every token's row is
-    checked against the oracle's sequential f32 matvec (rows sampled at 64)."""
+def test_qgemm_batched(backend, oracle, nb, shape, m, fmt):
+    """Batches of 8+ tokens run on the tcgen05 GEMM; tokens 0, m/2 and m-1
+    are checked against the oracle's sequential f32 matvec."""
     n, k = shape
     rng = np.random.default_rng(60 + m + n + k)
-    q = oracle.quantize(oracle.Q4_K, weights(rng, n * k))
-    w = nb.QWeight(backend, nb.Q4_K, n, k, q)
+    q = oracle.quantize(getattr(oracle, fmt), weights(rng, n * k))
+    w = nb.QWeight(backend, getattr(nb, fmt), n, k, q)
     x = rng.standard_normal((m, k)).astype(np.float32)
     y = w.matvec(x)
     for t in sorted({0, m // 2, m - 1}):
-        ref = oracle.qmatvec(oracle.Q4_K, q, n, k, x[t], threads=16)
+        ref = oracle.qmatvec(getattr(oracle, fmt), q, n, k, x[t], threads=16)
         assert rel_err(y[t], ref) < REL_TOL, (t, rel_err(y[t], ref))
     w.close()
 
 
-def test_qgemm_edge_cases(backend, oracle, nb):
+@pytest.mark.parametrize("fmt", ["Q4_K", "Q8_0"])
+def test_qgemm_edge_cases(backend, oracle, nb, fmt):
     """Zero, huge, tiny and mixed-scale tokens; a partial 128-row tile."""
     rng = np.random.default_rng(61)
     n, k = 72, 768
-    q = oracle.quantize(oracle.Q4_K, weights(rng, n * k))
+    F = getattr(oracle, fmt)
+    q = oracle.quantize(F, weights(rng, n * k))
     x = rng.standard_normal((9, k)).astype(np.float32)
     x[0] = 0.0
     x[1] *= 3e4
     x[2] *= 1e-6
     x[3, :256] *= 1e4
     x[4, 256:] = 0.0
-    y = backend.qmatvec(nb.Q4_K, q, n, k, x)
+    y = backend.qmatvec(getattr(nb, fmt), q, n, k, x)
     assert np.all(y[0] == 0.0)
     for t in range(1, 9):
-        assert rel_err(y[t], oracle.qmatvec(oracle.Q4_K, q, n, k, x[t])) < REL_TOL, t
+        assert rel_err(y[t], oracle.qmatvec(F, q, n, k, x[t])) < REL_TOL, t
 
 
 def test_qgemm_matches_gemv_path(backend, nb, oracle):
