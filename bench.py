@@ -210,7 +210,18 @@ def run_ncu_case(args):
     return 0
 
 
-def run_batched(nb, L, path, batch: int, prompt_len: int, steps: int, warmup: int, device: int) -> dict:
+def tp_join(dist, nb, backend, rank: int, world: int) -> None:
+    """Tensor parallelism over the torchrun ranks: rank 0's NCCL group id is
+    broadcast and every rank joins before loading its slice of the model."""
+    if world <= 1:
+        return
+    uid = [nb.tp_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    backend.tp_init(rank, world, uid[0])
+
+
+def run_batched(nb, L, path, batch: int, prompt_len: int, steps: int, warmup: int, device: int, dist=None,
+                rank: int = 0, world: int = 1) -> dict:
     """Config E at batch `batch`: every sequence gets its own random prompt of
     `prompt_len` tokens (seed 1 + index), then `steps` decode steps each
     advance all sequences by one token through nexus_cuda_decode_batch.  The
@@ -218,6 +229,7 @@ def run_batched(nb, L, path, batch: int, prompt_len: int, steps: int, warmup: in
     time is the host wall clock around the calls (token ids in, argmax ids out)."""
     import torch
     be = nb.CudaBackend(device=device, max_batch=batch, max_seq_len=prompt_len + steps + warmup + 8)
+    tp_join(dist, nb, be, rank, world)
     eng = nb.InferenceEngine(be)
     eng.load_model(path)
     V = eng.info.vocab_rows
@@ -251,12 +263,72 @@ def run_batched(nb, L, path, batch: int, prompt_len: int, steps: int, warmup: in
     wall = time.perf_counter() - t0
     eng.close()
     be.close()
+    dev_ms = reduce_max(dist, dev_ms, torch.device("cuda", device))
+    wall = reduce_max(dist, wall, torch.device("cuda", device))
     return {"value": batch * steps / (dev_ms / 1000.0), "unit": "tok/s", "batch": batch, "steps": steps,
             "ms_per_step": dev_ms / steps,
             "e2e": {"value": batch * steps / wall, "unit": "tok/s", "h2d_bytes_per_step": 28 * batch,
                     "d2h_bytes_per_step": 4 * batch},
             "prefill": {"tokens": batch * prompt_len, "seconds": prefill_s,
                         "tok_s": batch * prompt_len / prefill_s, "last_prompt_ms": prefill_ms_last}}
+
+
+SWEEP_SHAPES = [(4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]
+SWEEP_FORMATS = ["Q8_0", "Q4_0", "Q4_K", "Q2_K"]
+SWEEP_M = [1, 4, 16, 64, 512]
+
+
+def sweep_weight(nb, fmt: int, n: int, k: int, seed: int = 0):
+    """A seeded N(0, 0.02^2) weight quantized on the host: 256 distinct rows
+    repeated down the matrix (the timing does not depend on the values)."""
+    rng = np.random.default_rng(seed)
+    base = (rng.standard_normal((256, k), dtype=np.float32) * 0.02).reshape(-1)
+    blk = nb.quantize_host(fmt, base)
+    return np.tile(blk.reshape(256, -1), (n // 256, 1))
+
+
+def run_matvec(args):
+    """Config S (quantized matvec/matmul sweep): device time per launch with a
+    cold L2 (256 MB written between launches), HBM GB/s of the algorithmic
+    bytes (weights + x + y) and, for 64+ tokens, useful TFLOP/s (2*M*N*K).
+    --matvec FMT N K M runs one case three times (the ncu target)."""
+    import torch
+    import nexus_b200 as nb
+    be = nb.CudaBackend(device=0)
+    peaks = measured_peaks()
+    cases = []
+    if args.matvec:
+        f, n, k, m = args.matvec
+        cases = [(f, int(n), int(k), [int(m)])]
+    else:
+        cases = [(f, n, k, SWEEP_M) for (n, k) in SWEEP_SHAPES for f in SWEEP_FORMATS]
+    rows = []
+    for fname, n, k, ms in cases:
+        fmt = getattr(nb, fname)
+        qw = nb.QWeight(be, fmt, n, k, sweep_weight(nb, fmt, n, k))
+        for m in ms:
+            x = torch.randn(m, k, device="cuda", generator=torch.Generator("cuda").manual_seed(3))
+            y = torch.empty(m, n, device="cuda")
+            torch.cuda.synchronize()
+            if args.matvec:
+                for _ in range(3):
+                    qw.matvec_device(x.data_ptr(), m, y.data_ptr())
+                be.synchronize()
+                ms_ = qw.bench(x.data_ptr(), m, y.data_ptr(), iters=3)
+            else:
+                qw.bench(x.data_ptr(), m, y.data_ptr(), iters=2)
+                ms_ = qw.bench(x.data_ptr(), m, y.data_ptr(), iters=10 if m < 512 else 4)
+            byts = qw.nbytes() + 4.0 * m * k + 4.0 * m * n
+            row = {"format": fname, "n": n, "k": k, "m": m, "us": ms_ * 1e3, "gbs": byts / (ms_ * 1e-3) / 1e9,
+                   "hbm_frac": byts / (ms_ * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                   "path": "tcgen05 GEMM" if (m >= 8 and fname in ("Q4_K", "Q8_0")) else "dp4a GEMV"}
+            if m >= 64:
+                row["tflops"] = 2.0 * m * n * k / (ms_ * 1e-3) / 1e12
+            rows.append(row)
+            print(json.dumps(row), flush=True)
+        qw.close()
+    be.close()
+    return 0
 
 
 def main():
@@ -273,7 +345,11 @@ def main():
     ap.add_argument("--ncu-steps", type=int, default=0,
                     help="profiling run for ncu: 8-token prefill (2 fused 4-token steps), then this many "
                          "device-chained decode steps; prints a short JSON line")
+    ap.add_argument("--sweep", action="store_true", help="config S: quantized matvec/matmul sweep, one JSON line per case")
+    ap.add_argument("--matvec", nargs=4, metavar=("FMT", "N", "K", "M"), help="one config-S case, three launches")
     args = ap.parse_args()
+    if args.sweep or args.matvec:
+        return run_matvec(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.steps + args.warmup > GEN_TOKENS:
@@ -299,6 +375,7 @@ def main():
         path = nb.model_path(args.config)
 
     backend = nb.CudaBackend(device=local, max_seq_len=PROMPT_LEN + GEN_TOKENS + 8)
+    tp_join(dist, nb, backend, rank, world)
     eng = nb.InferenceEngine(backend)
     eng.load_model(path)
     info = eng.info
@@ -321,7 +398,8 @@ def main():
         torch.cuda.synchronize()
     gen_ms = eng.last_step_ms()  # CUDA events around the K chained steps (excludes the prefill)
     ms_max = reduce_max(dist, gen_ms, device)
-    value = world * args.steps / (ms_max / 1000.0)
+    # one decode stream served by all ranks (tensor parallel): tokens per second of the job
+    value = args.steps / (ms_max / 1000.0)
 
     # ---- e2e: nexus_cuda_decode with host token in / argmax out per step ----
     _, tok = eng.prefill(prompt, want_logits=False)
@@ -340,7 +418,7 @@ def main():
         pos += 1
     torch.cuda.synchronize()
     e2e_s = reduce_max(dist, time.perf_counter() - t0, device)
-    e2e_value = world * args.steps / e2e_s
+    e2e_value = args.steps / e2e_s
 
     # ---- live per-kernel profile (CUDA events per launch, no graph) ----
     eng.prefill(prompt, want_logits=False)
@@ -356,12 +434,13 @@ def main():
     line = {
         "metric": "decode tok/s, Llama-3-8B-shape Q4_K, b=1",
         "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "int8x4 dp4a + f32 (Q4_K/Q8_0 weights)", "data": "synthetic (seeded random-init weights, random prompt)",
         "config": {"workload": f"{args.config}: prompt {PROMPT_LEN} (seed {SEED_PROMPT}), greedy decode b=1, "
                                f"context {PROMPT_LEN}-{PROMPT_LEN + args.warmup + args.steps}",
-                   "model": args.config, "global_batch": world, "seq_len": PROMPT_LEN + GEN_TOKENS,
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "model": args.config, "global_batch": 1, "seq_len": PROMPT_LEN + GEN_TOKENS,
+                   "parallelism": f"tp{world} (heads, FFN and vocab rows per rank; NCCL all-reduce per sublayer)"
+                   if world > 1 else "single GPU",
                    "l2": "inputs larger than L2: every step streams all weights "
                          f"({info.weight_bytes / 1e9:.3f} GB) from HBM",
                    "weight_bytes_per_token": info.weight_bytes},
@@ -386,7 +465,7 @@ def main():
     # ---- b=32: one decode step advances 32 sequences (tensor-core GEMM path) ----
     if args.batch > 1:
         line["b32"] = run_batched(nb, L, path, args.batch, prompt_len=PROMPT_LEN, steps=min(args.steps, 32),
-                                  warmup=args.warmup, device=local)
+                                  warmup=args.warmup, device=local, dist=dist, rank=rank, world=world)
         line["metric"] = f"decode tok/s, Llama-3-8B-shape Q4_K, b=1 (b={args.batch} in b32)"
 
     if rank == 0 and not args.no_cpu_baseline:

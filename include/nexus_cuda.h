@@ -110,6 +110,31 @@ int nexus_cuda_synchronize(nexus_cuda_backend *b);
 /* Last error message for this backend (thread-local when b is NULL). */
 const char *nexus_cuda_last_error(const nexus_cuda_backend *b);
 
+/* ---- Tensor parallelism (one process per GPU) ----
+ * No counterpart in the reference, which has no multi-GPU path; these give
+ * BackendFactory::create(Some(Cuda)) (src/backend/mod.rs:206-213) a
+ * multi-GPU form.  Rank 0 creates an id, the launcher shares it with every
+ * rank (e.g. over torch.distributed), and each rank calls tp_init on its
+ * backend before nexus_cuda_model_load.  Layers are then sharded: query/KV
+ * heads, FFN rows and LM-head rows per rank; o_proj and down are column
+ * slices whose partial sums meet in one all-reduce per sublayer (NCCL, loaded
+ * at tp_init).  Every rank must make the same model calls in the same order. */
+#define NEXUS_TP_ID_BYTES 128
+int nexus_cuda_tp_unique_id(void *id, size_t id_bytes);
+int nexus_cuda_tp_init(nexus_cuda_backend *b, int rank, int world, const void *id, size_t id_bytes);
+
+/* The slice of a model one rank holds (host-only arithmetic, no device). */
+typedef struct nexus_tp_slice {
+    uint32_t q_head_begin, q_heads;    /* query heads */
+    uint32_t kv_head_begin, kv_heads;  /* KV heads (each rank's query heads use only its own) */
+    uint32_t ffn_begin, ffn_rows;      /* gate/up rows = down columns */
+    uint32_t vocab_begin, vocab_rows;  /* LM-head rows */
+} nexus_tp_slice;
+/* NEXUS_E_INVALID when the shapes do not split (heads divisible by world,
+ * column slices whole 256-element super-blocks, vocab rows whole 32-row groups). */
+int nexus_tp_plan(uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim, uint32_t ff_dim,
+                  uint32_t vocab_rows, int rank, int world, nexus_tp_slice *out);
+
 /* ---- KernelOp (src/backend/mod.rs:118-183) executed by Backend::execute ---- */
 enum {
     NEXUS_OP_MATMUL = 0,      /* C[m,n] = A[m,k] @ B  (B is [n,k] when transpose_b, else [k,n]) */

@@ -6,9 +6,10 @@ package is its Python binding and the reference-shaped engine surface.
 from . import _lib
 from ._lib import (BF16, F16, F32, FORMAT_IDS, FORMAT_NAMES, Q2_K, Q4_0, Q4_K, Q8_0, NexusError)
 from .engine import (BackendCapabilities, CudaBackend, InferenceEngine, MemoryInfo, QWeight,
-                     cuda_capabilities, quantize_host, write_synthetic_model)
+                     cuda_capabilities, quantize_host, tp_plan, tp_unique_id, write_synthetic_model)
 from .configs import CONFIGS, model_path
 
 __all__ = ["_lib", "F32", "F16", "BF16", "Q4_0", "Q8_0", "Q2_K", "Q4_K", "FORMAT_IDS", "FORMAT_NAMES",
            "NexusError", "BackendCapabilities", "CudaBackend", "InferenceEngine", "MemoryInfo", "QWeight",
-           "cuda_capabilities", "quantize_host", "write_synthetic_model", "CONFIGS", "model_path"]
+           "cuda_capabilities", "quantize_host", "tp_plan", "tp_unique_id", "write_synthetic_model", "CONFIGS",
+           "model_path"]

@@ -89,6 +89,14 @@ class SynthConfig(C.Structure):
 
 P = C.c_void_p
 # (name, restype, argtypes) of every symbol declared in include/nexus_cuda.h
+class TpSlice(C.Structure):
+    _fields_ = [("q_head_begin", C.c_uint32), ("q_heads", C.c_uint32), ("kv_head_begin", C.c_uint32),
+                ("kv_heads", C.c_uint32), ("ffn_begin", C.c_uint32), ("ffn_rows", C.c_uint32),
+                ("vocab_begin", C.c_uint32), ("vocab_rows", C.c_uint32)]
+
+
+TP_ID_BYTES = 128
+
 SIGNATURES = [
     ("nexus_cuda_is_available", C.c_int, []),
     ("nexus_cuda_capabilities", C.c_int, [C.POINTER(Caps)]),
@@ -99,6 +107,10 @@ SIGNATURES = [
     ("nexus_cuda_memory_info", C.c_int, [P, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
     ("nexus_cuda_synchronize", C.c_int, [P]),
     ("nexus_cuda_last_error", C.c_char_p, [P]),
+    ("nexus_cuda_tp_unique_id", C.c_int, [P, C.c_size_t]),
+    ("nexus_cuda_tp_init", C.c_int, [P, C.c_int, C.c_int, P, C.c_size_t]),
+    ("nexus_tp_plan", C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_int, C.c_int,
+                                C.POINTER(TpSlice)]),
     ("nexus_cuda_execute", C.c_int, [P, C.POINTER(Op)]),
     ("nexus_cuda_qweight_create", C.c_int, [P, C.c_int, C.c_size_t, C.c_size_t, P, C.c_size_t, C.POINTER(P)]),
     ("nexus_cuda_qweight_destroy", C.c_int, [P]),

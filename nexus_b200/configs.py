@@ -21,6 +21,12 @@ CONFIGS = {
     "tiny": dict(num_layers=4, hidden_size=256, num_heads=8, num_kv_heads=4, ff_dim=768, vocab_size=4096,
                  context_length=512, rope_theta=10000.0, attn_format=Q4_K, ffn_format=Q4_K, embd_format=Q4_K,
                  head_format=Q4_K, norm_format=Q4_K),
+    # small model whose heads, FFN rows and vocab split over 2/4/8 tensor-parallel
+    # ranks (per-rank column slices of whole super-blocks): 2 layers, hidden 2048,
+    # 16/8 heads, head_dim 128, FFN 4096, vocab 8192, all Q4_K
+    "tp_small": dict(num_layers=2, hidden_size=2048, num_heads=16, num_kv_heads=8, ff_dim=4096, vocab_size=8192,
+                     context_length=512, rope_theta=10000.0, attn_format=Q4_K, ffn_format=Q4_K, embd_format=Q4_K,
+                     head_format=Q4_K, norm_format=Q4_K),
     # Llama-3-8B shape, Q4_K body, Q8_0 embedding and LM head
     "llama8b_q4k": dict(num_layers=32, hidden_size=4096, num_heads=32, num_kv_heads=8, ff_dim=14336,
                         vocab_size=128256, context_length=8448, rope_theta=500000.0, attn_format=Q4_K,

@@ -6,7 +6,9 @@
 // generation chained on the device, batched decode, and the generic KernelOp
 // surface of Backend::execute (src/backend/mod.rs:92).
 #include <cuda_runtime.h>
+#include <dlfcn.h>
 #include <math.h>
+#include <nccl.h>
 #include <string.h>
 
 #include <algorithm>
@@ -42,7 +44,47 @@ struct nexus_cuda_backend {
     bool destroy_pending = false;
     // set by a kernel whose bounded wait gave up (op-level calls)
     int *dev_err = nullptr;
+    // tensor parallelism (nexus_cuda_tp_init)
+    int tp_rank = 0, tp_world = 1;
+    ncclComm_t comm = nullptr;
 };
+
+// NCCL is opened at nexus_cuda_tp_init (no link-time dependency).
+struct NcclApi {
+    ncclResult_t (*get_unique_id)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                               cudaStream_t) = nullptr;
+    ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    const char *(*error_string)(ncclResult_t) = nullptr;
+    bool ok = false;
+};
+
+static NcclApi *nccl_api(std::string *why) {
+    static NcclApi api;
+    static std::once_flag once;
+    static std::string load_error;
+    std::call_once(once, [] {
+        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) {
+            load_error = std::string("cannot load NCCL: ") + dlerror();
+            return;
+        }
+        api.get_unique_id = (decltype(api.get_unique_id))dlsym(h, "ncclGetUniqueId");
+        api.comm_init_rank = (decltype(api.comm_init_rank))dlsym(h, "ncclCommInitRank");
+        api.all_reduce = (decltype(api.all_reduce))dlsym(h, "ncclAllReduce");
+        api.all_gather = (decltype(api.all_gather))dlsym(h, "ncclAllGather");
+        api.comm_destroy = (decltype(api.comm_destroy))dlsym(h, "ncclCommDestroy");
+        api.error_string = (decltype(api.error_string))dlsym(h, "ncclGetErrorString");
+        api.ok = api.get_unique_id && api.comm_init_rank && api.all_reduce && api.all_gather && api.comm_destroy &&
+                 api.error_string;
+        if (!api.ok) load_error = "NCCL library lacks a required symbol";
+    });
+    if (!api.ok && why) *why = load_error;
+    return api.ok ? &api : nullptr;
+}
 
 static std::mutex g_backend_mu;
 
@@ -53,6 +95,9 @@ static void backend_free_now(nexus_cuda_backend *b) {
         cudaStreamDestroy(b->stream);
     }
     if (b->dev_err) cudaFree(b->dev_err);
+    if (b->comm) {
+        if (NcclApi *api = nccl_api(nullptr)) api->comm_destroy(b->comm);
+    }
     delete b;
 }
 
@@ -277,7 +322,9 @@ extern "C" int nexus_cuda_backend_create(const nexus_cuda_config *cfg, nexus_cud
     if (c.tp < 1) c.tp = 1;
     if (c.max_batch < 1) c.max_batch = 1;
     if (c.page_tokens == 0) c.page_tokens = 16;
-    if (c.tp != 1) return set_err(nullptr, NEXUS_E_INVALID, "tensor parallelism is driven by one process per GPU; tp must be 1 per backend");
+    if (c.tp != 1)
+        return set_err(nullptr, NEXUS_E_INVALID,
+                       "tensor parallelism runs one process per GPU: create each backend with tp 1, then nexus_cuda_tp_init");
     if ((c.kv_bits_k == 0) != (c.kv_bits_v == 0)) return set_err(nullptr, NEXUS_E_INVALID, "kv_bits_k and kv_bits_v must both be 0 or both set");
     if (c.kv_bits_k > 8 || c.kv_bits_v > 8) return set_err(nullptr, NEXUS_E_INVALID, "packed KV supports 1..8 bits");
     if (!nexus_cuda_is_available()) return set_err(nullptr, NEXUS_E_UNAVAILABLE, "no sm_100 CUDA device");
@@ -341,6 +388,62 @@ extern "C" int nexus_cuda_synchronize(nexus_cuda_backend *b) {
     cudaSetDevice(b->device);
     NX_CUDA(b, cudaStreamSynchronize(b->stream));
     return check_dev_err(b);
+}
+
+extern "C" int nexus_tp_plan(uint32_t Hq, uint32_t Hkv, uint32_t D, uint32_t F, uint32_t V, int rank, int world,
+                             nexus_tp_slice *out) {
+    if (!out || world < 1 || rank < 0 || rank >= world || !Hq || !Hkv || !D || !F || !V)
+        return set_err(nullptr, NEXUS_E_INVALID, "tp plan: bad argument");
+    const uint32_t w = (uint32_t)world;
+    if (Hq % w || Hkv % w || F % w || V % w)
+        return set_err(nullptr, NEXUS_E_INVALID, "tp plan: heads, FFN rows and vocab rows must divide by the world size");
+    const uint32_t hq = Hq / w, hkv = Hkv / w, f = F / w, v = V / w;
+    if (w > 1 && ((hq * D) % 256 || f % 256 || v % 32))
+        return set_err(nullptr, NEXUS_E_INVALID,
+                       "tp plan: per-rank attention and FFN column slices must be whole 256-element super-blocks "
+                       "and vocab slices whole 32-row groups");
+    out->q_head_begin = (uint32_t)rank * hq;
+    out->q_heads = hq;
+    out->kv_head_begin = (uint32_t)rank * hkv;
+    out->kv_heads = hkv;
+    out->ffn_begin = (uint32_t)rank * f;
+    out->ffn_rows = f;
+    out->vocab_begin = (uint32_t)rank * v;
+    out->vocab_rows = v;
+    return NEXUS_OK;
+}
+
+extern "C" int nexus_cuda_tp_unique_id(void *id, size_t id_bytes) {
+    if (!id || id_bytes < sizeof(ncclUniqueId)) return set_err(nullptr, NEXUS_E_INVALID, "tp id buffer too small");
+    std::string why;
+    NcclApi *api = nccl_api(&why);
+    if (!api) return set_err(nullptr, NEXUS_E_COMM, why);
+    ncclUniqueId u;
+    ncclResult_t r = api->get_unique_id(&u);
+    if (r != ncclSuccess) return set_err(nullptr, NEXUS_E_COMM, std::string("ncclGetUniqueId: ") + api->error_string(r));
+    memcpy(id, &u, sizeof(u));
+    return NEXUS_OK;
+}
+
+extern "C" int nexus_cuda_tp_init(nexus_cuda_backend *b, int rank, int world, const void *id, size_t id_bytes) {
+    if (!b || !id || id_bytes < sizeof(ncclUniqueId) || world < 1 || rank < 0 || rank >= world)
+        return set_err(b, NEXUS_E_INVALID, "tp init: bad argument");
+    if (b->comm) return set_err(b, NEXUS_E_INVALID, "tp init: already initialised");
+    if (world == 1) return NEXUS_OK;
+    std::string why;
+    NcclApi *api = nccl_api(&why);
+    if (!api) return set_err(b, NEXUS_E_COMM, why);
+    cudaSetDevice(b->device);
+    ncclUniqueId u;
+    memcpy(&u, id, sizeof(u));
+    ncclResult_t r = api->comm_init_rank(&b->comm, world, u, rank);
+    if (r != ncclSuccess) {
+        b->comm = nullptr;
+        return set_err(b, NEXUS_E_COMM, std::string("ncclCommInitRank: ") + api->error_string(r));
+    }
+    b->tp_rank = rank;
+    b->tp_world = world;
+    return NEXUS_OK;
 }
 
 extern "C" const char *nexus_cuda_last_error(const nexus_cuda_backend *b) {
@@ -782,6 +885,10 @@ struct nexus_cuda_model {
     float *logits = nullptr, *part = nullptr;
     unsigned *counters = nullptr;
     LinScratch lin;                   // tensor-core GEMM scratch (steps of kGemmMinM+ tokens)
+    // this rank's slice (the whole model without tensor parallelism) and local sizes
+    nexus_tp_slice sl = {};
+    uint32_t hq_l = 0, hkv_l = 0, qdim_l = 0, kvd_l = 0, f_l = 0, v_l = 0;
+    float *logits_gather = nullptr;   // [world][kMaxChunk][v_l] all-gather target
     DevSeq *seqs = nullptr;
     uint32_t *seq_ids = nullptr, *out_tokens = nullptr;
     DevSeq *h_seqs = nullptr;
@@ -881,6 +988,17 @@ static int check_matrix(nexus_cuda_backend *b, const GgufTensor *t, size_t rows,
     return NEXUS_OK;
 }
 
+// Columns [c0, c0 + n) of a rows x k block-format matrix (c0 and n whole
+// blocks): the full matrix when they cover it, else a copy in `buf`.
+static const uint8_t *column_slice(int fmt, const uint8_t *src, uint32_t rows, uint32_t k, uint32_t c0, uint32_t n,
+                                   std::vector<uint8_t> &buf) {
+    if (c0 == 0 && n == k) return src;
+    const size_t rb = row_bytes(fmt, k), off = row_bytes(fmt, c0), nb = row_bytes(fmt, n);
+    buf.resize((size_t)rows * nb);
+    for (uint32_t r = 0; r < rows; r++) memcpy(buf.data() + (size_t)r * nb, src + (size_t)r * rb + off, nb);
+    return buf.data();
+}
+
 static int model_load(nexus_cuda_backend *b, const char *path, nexus_cuda_model **out) {
     GgufFile f;
     std::string err;
@@ -935,6 +1053,17 @@ static int model_load(nexus_cuda_backend *b, const char *path, nexus_cuda_model 
     if (rc) return rc;
     const GgufTensor *th = find_any(f, {"output.weight", "lm_head.weight", "model.embed_tokens.weight", "token_embd.weight"});
     uint64_t weight_bytes = 0;
+    const int tp = b->tp_world, rk = b->tp_rank;
+    if (tp > 1 && !th) return set_err(b, NEXUS_E_INVALID, "tensor parallelism needs an LM head tensor");
+    if (tp > 1 && m->bits_k) return set_err(b, NEXUS_E_UNSUPPORTED_FORMAT, "tensor parallelism runs with the float KV cache");
+    I.vocab_rows = th ? (uint32_t)(th->elems() / H) : H;  // no head: logits are the normed hidden state (:1040-1043)
+    if ((rc = nexus_tp_plan(Hq, Hkv, D, F, I.vocab_rows, rk, tp, &m->sl))) return set_err(b, rc, g_tls_error);
+    m->hq_l = m->sl.q_heads;
+    m->hkv_l = m->sl.kv_heads;
+    m->qdim_l = m->hq_l * D;
+    m->kvd_l = m->hkv_l * D;
+    m->f_l = m->sl.ffn_rows;
+    m->v_l = m->sl.vocab_rows;
     if (th) {
         size_t rows = th->elems() / H;
         rc = check_matrix(b, th, rows, H, "output.weight");
@@ -942,13 +1071,12 @@ static int model_load(nexus_cuda_backend *b, const char *path, nexus_cuda_model 
         size_t nb = 0;
         const uint8_t *src = f.data(*th, &nb);
         if (!src) return set_err(b, NEXUS_E_TRUNCATED, "output payload truncated");
-        rc = make_mat(b, th->type, (int)rows, (int)H, src, m->head);
+        // this rank's vocab rows
+        src += (size_t)m->sl.vocab_begin * row_bytes(th->type, H);
+        rc = make_mat(b, th->type, (int)m->v_l, (int)H, src, m->head);
         if (rc) return rc;
         m->has_head = true;
-        I.vocab_rows = (uint32_t)rows;
         weight_bytes += m->head.bytes;
-    } else {
-        I.vocab_rows = H;  // transformer_logits returns the normed hidden state (:1040-1043)
     }
 
     m->layers.resize(I.num_layers);
@@ -986,45 +1114,54 @@ static int model_load(nexus_cuda_backend *b, const char *path, nexus_cuda_model 
         {
             const int fmt = tq->type;
             const size_t rb = row_bytes(fmt, H);
-            const uint32_t nrows = qdim + 2 * kv_dim;
+            const uint32_t qd = m->qdim_l, kd = m->kvd_l;  // this rank's heads
+            const uint32_t nrows = qd + 2 * kd;
             buf.resize((size_t)nrows * rb);
             const uint32_t gph = D / 32;
             for (uint32_t r = 0; r < nrows; r++) {
                 const uint8_t *src;
-                if (r < qdim + kv_dim) {
-                    const bool isq = r < qdim;
-                    const uint32_t rr = isq ? r : r - qdim;
+                if (r < qd + kd) {
+                    const bool isq = r < qd;
+                    const uint32_t rr = isq ? r : r - qd;
                     const uint32_t g = rr / 32, lane = rr % 32, head = g / gph, i = g % gph;
                     const uint32_t d = lane < 16 ? 16 * i + lane : 16 * i + (lane - 16) + D / 2;
-                    src = (isq ? pq : pk) + (size_t)(head * D + d) * rb;
+                    const uint32_t ghead = head + (isq ? m->sl.q_head_begin : m->sl.kv_head_begin);
+                    src = (isq ? pq : pk) + (size_t)(ghead * D + d) * rb;
                 } else {
-                    src = pv + (size_t)(r - qdim - kv_dim) * rb;
+                    src = pv + (size_t)(m->sl.kv_head_begin * D + (r - qd - kd)) * rb;
                 }
                 memcpy(buf.data() + (size_t)r * rb, src, rb);
             }
             if ((rc = make_mat(b, fmt, (int)nrows, (int)H, buf.data(), L.qkv))) return rc;
         }
-        if ((rc = make_mat(b, to->type, (int)H, (int)qdim, po, L.o))) return rc;
+        // o_proj: this rank's columns (its heads' outputs), whole super-blocks
+        if ((rc = make_mat(b, to->type, (int)H, (int)m->qdim_l,
+                           column_slice(to->type, po, H, qdim, m->sl.q_head_begin * D, m->qdim_l, buf), L.o)))
+            return rc;
         // gate/up interleaved: lanes 0..15 gate rows, lanes 16..31 the same up rows
         {
             const int fmt = tg->type;
             const size_t rb = row_bytes(fmt, H);
-            buf.resize((size_t)2 * F * rb);
-            for (uint32_t r = 0; r < 2 * F; r++) {
+            const uint32_t fl = m->f_l, f0 = m->sl.ffn_begin;
+            buf.resize((size_t)2 * fl * rb);
+            for (uint32_t r = 0; r < 2 * fl; r++) {
                 const uint32_t g = r / 32, lane = r % 32;
-                const uint8_t *src = lane < 16 ? pg + (size_t)(16 * g + lane) * rb : pu + (size_t)(16 * g + lane - 16) * rb;
+                const uint8_t *src = lane < 16 ? pg + (size_t)(f0 + 16 * g + lane) * rb
+                                               : pu + (size_t)(f0 + 16 * g + lane - 16) * rb;
                 memcpy(buf.data() + (size_t)r * rb, src, rb);
             }
-            if ((rc = make_mat(b, fmt, (int)(2 * F), (int)H, buf.data(), L.gateup))) return rc;
+            if ((rc = make_mat(b, fmt, (int)(2 * fl), (int)H, buf.data(), L.gateup))) return rc;
         }
-        if ((rc = make_mat(b, td->type, (int)H, (int)F, pd, L.down))) return rc;
+        if ((rc = make_mat(b, td->type, (int)H, (int)m->f_l,
+                           column_slice(td->type, pd, H, F, m->sl.ffn_begin, m->f_l, buf), L.down)))
+            return rc;
         weight_bytes += L.qkv.bytes + L.o.bytes + L.gateup.bytes + L.down.bytes;
         if (l == 0) I.body_format = tq->type;
         // KV cache (KvCache::new(num_kv_heads*head_dim, max_seq_len, kv_quant), :593-597)
         const size_t toks = (size_t)m->max_batch * m->max_seq;
         if (m->bits_k == 0) {
-            NX_CUDA(b, malloc_tracked(m, &L.k_cache, toks * kv_dim));
-            NX_CUDA(b, malloc_tracked(m, &L.v_cache, toks * kv_dim));
+            NX_CUDA(b, malloc_tracked(m, &L.k_cache, toks * m->kvd_l));
+            NX_CUDA(b, malloc_tracked(m, &L.v_cache, toks * m->kvd_l));
         } else {
             m->bpt_k = ((size_t)kv_dim * m->bits_k + 7) / 8;
             m->bpt_v = ((size_t)kv_dim * m->bits_v + 7) / 8;
@@ -1059,25 +1196,28 @@ static int model_load(nexus_cuda_backend *b, const char *path, nexus_cuda_model 
     }
 
     // activations for up to kMaxChunk tokens per step
+    // (this rank's heads, FFN rows and vocab rows under tensor parallelism)
     const int MC = kMaxChunk;
+    const uint32_t qd = m->qdim_l, kd = m->kvd_l, fl = m->f_l, hkv_l = m->hkv_l;
     NX_CUDA(b, malloc_tracked(m, &m->hidden, (size_t)MC * H));
-    NX_CUDA(b, malloc_tracked(m, &m->q, (size_t)MC * qdim));
-    NX_CUDA(b, malloc_tracked(m, &m->attn, (size_t)MC * qdim));
-    NX_CUDA(b, malloc_tracked(m, &m->gated, (size_t)MC * F));
-    NX_CUDA(b, malloc_tracked(m, &m->kv_scratch, (size_t)MC * 2 * kv_dim));
-    NX_CUDA(b, malloc_tracked(m, &m->logits, (size_t)MC * I.vocab_rows));
+    NX_CUDA(b, malloc_tracked(m, &m->q, (size_t)MC * qd));
+    NX_CUDA(b, malloc_tracked(m, &m->attn, (size_t)MC * qd));
+    NX_CUDA(b, malloc_tracked(m, &m->gated, (size_t)MC * fl));
+    NX_CUDA(b, malloc_tracked(m, &m->kv_scratch, (size_t)MC * 2 * kd));
+    NX_CUDA(b, malloc_tracked(m, &m->logits, (size_t)MC * (m->has_head ? m->v_l : I.vocab_rows)));
+    if (tp > 1) NX_CUDA(b, malloc_tracked(m, &m->logits_gather, (size_t)tp * MC * m->v_l));
     const int G = (int)(Hq / Hkv);
     // context slices of >= 64 tokens, at most 64 per (sequence, KV head); the
     // kernel uses only as many as the current context needs
     int max_split = std::max(1, std::min(64, (int)((m->max_seq + 63) / 64)));
     for (int mm = 1; mm <= MC; mm++) m->nsplit[mm] = max_split;
-    NX_CUDA(b, malloc_tracked(m, &m->part, (size_t)MC * Hkv * max_split * G * (D + 2)));
-    NX_CUDA(b, malloc_tracked(m, &m->counters, (size_t)MC * Hkv));
-    NX_CUDA(b, cudaMemset(m->counters, 0, (size_t)MC * Hkv * 4));
+    NX_CUDA(b, malloc_tracked(m, &m->part, (size_t)MC * hkv_l * max_split * G * (D + 2)));
+    NX_CUDA(b, malloc_tracked(m, &m->counters, (size_t)MC * hkv_l));
+    NX_CUDA(b, cudaMemset(m->counters, 0, (size_t)MC * hkv_l * 4));
     {
         // GEMM scratch for every step size that runs on the tensor cores
-        const int shapes[5][2] = {{(int)(qdim + 2 * kv_dim), (int)H}, {(int)H, (int)qdim}, {(int)(2 * F), (int)H},
-                                  {(int)H, (int)F}, {(int)I.vocab_rows, (int)H}};
+        const int shapes[5][2] = {{(int)(qd + 2 * kd), (int)H}, {(int)H, (int)qd}, {(int)(2 * fl), (int)H},
+                                  {(int)H, (int)fl}, {(int)m->v_l, (int)H}};
         for (int mm = kGemmMinM; mm <= MC; mm++)
             for (auto &sh : shapes) NX_CUDA(b, m->lin.ensure(mm, sh[0], sh[1], b->stream));
     }
@@ -1179,8 +1319,19 @@ static int step_chunk(size_t remaining) {
 static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof = nullptr) {
     const nexus_cuda_model_info &I = m->info;
     cudaStream_t st = m->b->stream;
-    const int H = (int)I.hidden_size, D = (int)I.head_dim, F = (int)I.ff_dim;
-    const int Hq = (int)I.num_heads, Hkv = (int)I.num_kv_heads, kv_dim = Hkv * D, qdim = Hq * D;
+    // this rank's share of heads and FFN rows (all of them without tensor parallelism)
+    const int H = (int)I.hidden_size, D = (int)I.head_dim, F = (int)m->f_l;
+    const int Hq = (int)m->hq_l, Hkv = (int)m->hkv_l, kv_dim = Hkv * D, qdim = Hq * D;
+    const bool tp = m->b->tp_world > 1, lead = m->b->tp_rank == 0;
+    NcclApi *nccl = tp ? nccl_api(nullptr) : nullptr;
+    if (tp && !nccl) return cudaErrorInvalidValue;
+    // partial sums of the column-sliced o_proj/down meet here: rank 0 adds the
+    // residual, the others store their part, and the all-reduce sums them
+    auto reduce_hidden = [&]() -> cudaError_t {
+        if (!tp) return cudaSuccess;
+        ncclResult_t r = nccl->all_reduce(m->hidden, m->hidden, (size_t)mc * H, ncclFloat32, ncclSum, m->b->comm, st);
+        return r == ncclSuccess ? cudaSuccess : cudaErrorUnknown;
+    };
     const int pdl = m->use_pdl ? 1 : 0;
     cudaError_t e;
     EmbedParams ep = {};
@@ -1307,11 +1458,12 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         o.k = qdim;
         o.x = m->attn;
         o.x_stride = qdim;
-        o.epi = EPI_ADD;
+        o.epi = lead ? EPI_ADD : EPI_STORE;
         o.y = m->hidden;
         o.y_stride = H;
         if (prof) prof->begin();
         if ((e = launch_linear(m, o, st)) != cudaSuccess) return e;
+        if ((e = reduce_hidden()) != cudaSuccess) return e;
         if (prof) prof->end("o_proj", gemv_bytes(L.o, mc, qdim, H) + 4.0 * mc * H);
         // ffn_norm -> gate/up -> SwiGLU
         GemvParams gu = {};
@@ -1345,11 +1497,12 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         dn.k = F;
         dn.x = m->gated;
         dn.x_stride = F;
-        dn.epi = EPI_ADD;
+        dn.epi = lead ? EPI_ADD : EPI_STORE;
         dn.y = m->hidden;
         dn.y_stride = H;
         if (prof) prof->begin();
         if ((e = launch_linear(m, dn, st)) != cudaSuccess) return e;
+        if ((e = reduce_hidden()) != cudaSuccess) return e;
         if (prof) prof->end("down", gemv_bytes(L.down, mc, F, H) + 4.0 * mc * H);
     }
     // transformer_logits: output norm + head + greedy argmax
@@ -1369,10 +1522,18 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         hd.norm_w = m->out_norm;
         hd.epi = EPI_ARGMAX;
         hd.y = m->logits;
-        hd.y_stride = (int)I.vocab_rows;
+        hd.y_stride = (int)m->v_l;
+        hd.row_offset = (int)m->sl.vocab_begin;
         hd.seqs = m->seqs;
         if (prof) prof->begin();
         if ((e = launch_linear(m, hd, st)) != cudaSuccess) return e;
+        if (tp) {
+            // greedy over all ranks' vocab slices: the packed (value, index)
+            // keys reduce with max; the rest of DevSeq is equal on every rank
+            static_assert(sizeof(DevSeq) == 24, "DevSeq is three 64-bit words");
+            ncclResult_t r = nccl->all_reduce(m->seqs, m->seqs, (size_t)mc * 3, ncclUint64, ncclMax, m->b->comm, st);
+            if (r != ncclSuccess) return cudaErrorUnknown;
+        }
         if (prof) prof->end("head", gemv_bytes(m->head, mc, H, (int)I.vocab_rows) + 4.0 * H);
     } else {
         if ((e = launch_rms_norm(m->hidden, m->out_norm, m->logits, mc, H, I.rms_norm_eps, st)) != cudaSuccess) return e;
@@ -1445,7 +1606,16 @@ static int host_step(nexus_cuda_model *m, const StepItem *items, int mc, float *
     int rc = run_step(m, mc);
     if (rc) return rc;
     const size_t V = m->info.vocab_rows;
-    if (logits_out) {
+    std::vector<float> gathered;
+    if (logits_out && b->tp_world > 1) {
+        // every rank holds its vocab slice: gather [world][mc][v_l], reorder on the host
+        NcclApi *nccl = nccl_api(nullptr);
+        const size_t per = (size_t)mc * m->v_l;
+        ncclResult_t r = nccl->all_gather(m->logits, m->logits_gather, per, ncclFloat32, b->comm, st);
+        if (r != ncclSuccess) return set_err(b, NEXUS_E_COMM, std::string("logits all-gather: ") + nccl->error_string(r));
+        gathered.resize(per * b->tp_world);
+        NX_CUDA(b, cudaMemcpyAsync(gathered.data(), m->logits_gather, gathered.size() * 4, cudaMemcpyDeviceToHost, st));
+    } else if (logits_out) {
         if (logits_last_only)
             NX_CUDA(b, cudaMemcpyAsync(logits_out, m->logits + (size_t)(mc - 1) * V, V * 4, cudaMemcpyDeviceToHost, st));
         else
@@ -1454,6 +1624,14 @@ static int host_step(nexus_cuda_model *m, const StepItem *items, int mc, float *
     NX_CUDA(b, cudaMemcpyAsync(m->h_out_tokens, m->out_tokens, (kMaxChunk + 1) * 4, cudaMemcpyDeviceToHost, st));
     NX_CUDA(b, cudaStreamSynchronize(st));
     if (m->h_out_tokens[kMaxChunk]) return device_timeout(m);
+    if (!gathered.empty()) {
+        const size_t vl = m->v_l;
+        for (int t = logits_last_only ? mc - 1 : 0; t < mc; t++) {
+            float *dst = logits_out + (logits_last_only ? 0 : (size_t)t * V);
+            for (int r = 0; r < b->tp_world; r++)
+                memcpy(dst + (size_t)r * vl, gathered.data() + ((size_t)r * mc + t) * vl, vl * 4);
+        }
+    }
     if (tokens_out) memcpy(tokens_out, m->h_out_tokens, mc * 4);
     return NEXUS_OK;
 }

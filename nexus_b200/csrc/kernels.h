@@ -72,6 +72,7 @@ struct GemvParams {
     int ksplit;             // warps per row group (set by the launcher)
     int nst;                // weight ring slots per warp (set by the launcher)
     int *err;               // device flag set when a bounded wait gives up (may be NULL)
+    int row_offset;         // EPI_ARGMAX: global index of local row 0 (vocab slice of a rank)
 };
 
 cudaError_t launch_gemv(const GemvParams &p, cudaStream_t st);

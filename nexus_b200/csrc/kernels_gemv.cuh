@@ -373,7 +373,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, int g, int t,
         // greedy_token: finite values only, larger value wins, ties -> larger index
         unsigned long long key = 0ull;
         if (row < p.n && isfinite(tot))
-            key = ((unsigned long long)((unsigned)total_key(tot) ^ 0x80000000u) << 32) | (unsigned)row;
+            key = ((unsigned long long)((unsigned)total_key(tot) ^ 0x80000000u) << 32) | (unsigned)(row + p.row_offset);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);

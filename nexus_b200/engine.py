@@ -73,6 +73,12 @@ class CudaBackend:
         self._lib = lib
         self.handle = h
 
+    # -- tensor parallelism (one process per GPU) --
+    def tp_init(self, rank: int, world: int, uid: bytes) -> None:
+        """Join the tensor-parallel group `uid` (from tp_unique_id on rank 0)."""
+        buf = C.create_string_buffer(bytes(uid), L.TP_ID_BYTES)
+        L.check(self._lib.nexus_cuda_tp_init(self.handle, rank, world, buf, L.TP_ID_BYTES), self.handle)
+
     # -- trait methods --
     def name(self) -> str:
         return self._lib.nexus_cuda_backend_name(self.handle).decode()
@@ -343,6 +349,23 @@ class InferenceEngine:
             self.close()
         except Exception:
             pass
+
+
+def tp_unique_id() -> bytes:
+    """A fresh tensor-parallel group id (rank 0 creates it, every rank passes it to tp_init)."""
+    lib = L.load()
+    buf = C.create_string_buffer(L.TP_ID_BYTES)
+    L.check(lib.nexus_cuda_tp_unique_id(buf, L.TP_ID_BYTES))
+    return buf.raw
+
+
+def tp_plan(num_heads: int, num_kv_heads: int, head_dim: int, ff_dim: int, vocab_rows: int, rank: int,
+            world: int) -> dict:
+    """The slice of the model one rank holds (nexus_tp_plan)."""
+    lib = L.load()
+    out = L.TpSlice()
+    L.check(lib.nexus_tp_plan(num_heads, num_kv_heads, head_dim, ff_dim, vocab_rows, rank, world, C.byref(out)))
+    return {k: getattr(out, k) for k, _ in L.TpSlice._fields_}
 
 
 def write_synthetic_model(path: str, *, num_layers: int, hidden_size: int, num_heads: int, num_kv_heads: int,
