@@ -45,6 +45,16 @@ GEN_TOKENS = 128
 SEED_PROMPT = 1
 
 
+def profiled_traffic(name: str):
+    """DRAM bytes per launch (read + write) recorded from an ncu capture in profiles/."""
+    import re
+    f = Path(__file__).resolve().parent / "profiles" / name
+    if not f.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*(\d+)", f.read_text())
+    return int(m.group(1)) if m else None
+
+
 def measured_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -447,7 +457,10 @@ def main():
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 28, "d2h_bytes_per_step": 4},
         "gpu_launches": None,
         "roofline": {"bound": "hbm", "kernel": dom["name"], "achieved": achieved, "peak": peaks["hbm_gbs"],
-                     "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                     "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                     "traffic": profiled_traffic("k_gemv_q4k_gateup_28672x4096_m1.md"),
+                     "traffic_source": "ncu dram__bytes_read+write of the same GEMV shape "
+                                       "(profiles/k_gemv_q4k_gateup_28672x4096_m1.md)",
                      "peak_source": peaks["source"],
                      "step_achieved_gbs": info.weight_bytes / (ms_max / args.steps / 1000.0) / 1e9},
         "kernels": {r["name"]: {"launches_per_step": r["launches"] / args.profile_steps,

@@ -93,6 +93,7 @@ typedef struct {
 
 #define NEXUS_CFG_NO_GRAPH 0x1u  /* launch kernels directly instead of a CUDA graph */
 #define NEXUS_CFG_NO_PDL 0x2u    /* no programmatic dependent launch between kernels */
+#define NEXUS_CFG_NO_PREFETCH 0x4u /* no L2 prefetch of the next matrix during each decode GEMV */
 
 typedef struct nexus_cuda_backend nexus_cuda_backend;
 
