@@ -331,13 +331,138 @@ def run_matvec(args):
             byts = qw.nbytes() + 4.0 * m * k + 4.0 * m * n
             row = {"format": fname, "n": n, "k": k, "m": m, "us": ms_ * 1e3, "gbs": byts / (ms_ * 1e-3) / 1e9,
                    "hbm_frac": byts / (ms_ * 1e-3) / 1e9 / peaks["hbm_gbs"],
-                   "path": "tcgen05 GEMM" if (m >= 8 and fname in ("Q4_K", "Q8_0")) else "dp4a GEMV"}
+                   "path": "tcgen05 GEMM" if m >= 8 else "dp4a GEMV"}
             if m >= 64:
                 row["tflops"] = 2.0 * m * n * k / (ms_ * 1e-3) / 1e12
             rows.append(row)
             print(json.dumps(row), flush=True)
         qw.close()
     be.close()
+    return 0
+
+
+def run_workload_p(args):
+    """Config P: the 8B shape with Q8_0 weights and the 4-bit packed KV cache;
+    64 requests with context lengths uniform in [1024, 8192] (seed 2) of random
+    token ids (seed 1 + request), then `steps` continuous decode steps that
+    advance all 64 requests by one token each through nexus_cuda_decode_batch,
+    with scheduler-style 16-token page lists (src/scheduler.rs:333-361)."""
+    import torch
+    import nexus_b200 as nb
+    n_req, gen = 64, args.steps
+    path = nb.model_path("llama8b_q8", threads=cpu_threads())
+    ctx = np.random.default_rng(2).integers(1024, 8193, n_req)
+    be = nb.CudaBackend(device=0, kv_bits=(4, 4), max_batch=n_req, max_seq_len=int(ctx.max()) + gen + args.warmup + 8)
+    eng = nb.InferenceEngine(be)
+    eng.load_model(path)
+    V = eng.info.vocab_rows
+    toks, pos, pages, next_page = [], [], [], 0
+    t0 = time.perf_counter()
+    for r in range(n_req):
+        prompt = np.random.default_rng(SEED_PROMPT + r).integers(0, V, int(ctx[r])).tolist()
+        _, t = eng.prefill(prompt, seq_id=r, want_logits=False)
+        toks.append(t)
+        pos.append(int(ctx[r]))
+        npg = (int(ctx[r]) + gen + args.warmup + 15) // 16
+        pages.append(list(range(next_page, next_page + npg)))
+        next_page += npg
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+
+    def step():
+        nonlocal toks
+        out, _ = eng.decode_batch([(r, toks[r], pos[r]) for r in range(n_req)], want_logits=False,
+                                  page_ids=pages)
+        toks = [int(v) for v in out]
+        for r in range(n_req):
+            pos[r] += 1
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dev_ms = 0.0
+    t0 = time.perf_counter()
+    with ClockSampler(0) as clk:
+        for _ in range(gen):
+            step()
+            dev_ms += eng.last_step_ms()
+    wall = time.perf_counter() - t0
+    mean_ctx = float(ctx.mean()) + args.warmup + gen / 2
+    kv_bytes = 2 * eng.info.num_layers * mean_ctx * (eng.info.num_kv_heads * eng.info.head_dim * 4 // 8 + 8) * n_req
+    step_bytes = eng.info.weight_bytes + kv_bytes
+    line = {"metric": "continuous decode tok/s, 8B-shape Q8_0, 4-bit packed KV, 64 requests (config P)",
+            "value": n_req * gen / (dev_ms / 1000.0), "unit": "tok/s", "n_gpus": 1, "steps": gen,
+            "warmup": args.warmup, "ms_per_step": dev_ms / gen, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16 tensor-core (exact Q8_0 hi/lo) + f32", "data": "synthetic",
+            "config": {"workload": "llama8b_q8, 64 requests, ctx U[1024,8192] seed 2, KV 4/4-bit packed, "
+                                   "16-token pages", "model": "llama8b_q8", "global_batch": n_req,
+                       "mean_ctx": mean_ctx, "l2": "inputs larger than L2 (weights + KV per step)"},
+            "e2e": {"value": n_req * gen / wall, "unit": "tok/s", "h2d_bytes_per_step": 28 * n_req,
+                    "d2h_bytes_per_step": 4 * n_req},
+            "roofline": {"bound": "hbm", "kernel": "whole step", "achieved": step_bytes / (dev_ms / gen / 1000) / 1e9,
+                         "peak": measured_peaks()["hbm_gbs"], "unit": "GB/s",
+                         "frac": step_bytes / (dev_ms / gen / 1000) / 1e9 / measured_peaks()["hbm_gbs"],
+                         "traffic": None, "bytes_per_step": step_bytes},
+            "prefill": {"tokens": int(ctx.sum()), "seconds": prefill_s, "tok_s": float(ctx.sum()) / prefill_s},
+            "clocks": clk.summary()}
+    eng.close()
+    be.close()
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_workload_x(args, dist, rank: int, world: int, local: int):
+    """Config X: the 70B shape (Q4_K attention, Q2_K FFN, Q8_0 embedding and
+    head), tensor parallel over the ranks: a 4096-token random prompt, then
+    `steps` greedy decode steps at batch 1 (device-chained), and the same at
+    batch 16 through nexus_cuda_decode_batch."""
+    import torch
+    import nexus_b200 as nb
+    device = torch.device("cuda", local)
+    prompt_len = 4096
+    if rank == 0:
+        path = nb.model_path("llama70b", threads=cpu_threads())
+    barrier(dist, device)
+    if rank != 0:
+        path = nb.model_path("llama70b")
+    be = nb.CudaBackend(device=local, max_seq_len=prompt_len + args.steps + args.warmup + 8)
+    tp_join(dist, nb, be, rank, world)
+    eng = nb.InferenceEngine(be)
+    eng.load_model(path)
+    info = eng.info
+    prompt = np.random.default_rng(SEED_PROMPT).integers(0, info.vocab_rows, prompt_len).tolist()
+    t0 = time.perf_counter()
+    eng.prefill(prompt, want_logits=False)
+    torch.cuda.synchronize()
+    prefill_s = reduce_max(dist, time.perf_counter() - t0, device)
+    eng.generate(prompt, args.warmup)
+    barrier(dist, device)
+    with ClockSampler(local) as clk:
+        eng.generate(prompt, args.steps)
+        torch.cuda.synchronize()
+    ms = reduce_max(dist, eng.last_step_ms(), device)
+    eng.close()
+    be.close()
+    b16 = run_batched(nb, None, path, 16, prompt_len=prompt_len, steps=min(args.steps, 16), warmup=args.warmup,
+                      device=local, dist=dist, rank=rank, world=world)
+    line = {"metric": "decode tok/s, Llama-3-70B-shape (Q4_K attn, Q2_K FFN), b=1 (b=16 in b16)",
+            "value": args.steps / (ms / 1000.0), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8x4 dp4a + f32 (b=1); f16 tensor-core (b=16)", "data": "synthetic",
+            "config": {"workload": f"llama70b: prompt {prompt_len} (seed {SEED_PROMPT}), greedy decode",
+                       "model": "llama70b", "global_batch": 1,
+                       "parallelism": f"tp{world}" if world > 1 else "single GPU",
+                       "weight_bytes_per_token_per_rank": info.weight_bytes,
+                       "l2": "inputs larger than L2"},
+            "roofline": {"bound": "hbm", "kernel": "whole step",
+                         "achieved": info.weight_bytes / (ms / args.steps / 1000) / 1e9,
+                         "peak": measured_peaks()["hbm_gbs"], "unit": "GB/s",
+                         "frac": info.weight_bytes / (ms / args.steps / 1000) / 1e9 / measured_peaks()["hbm_gbs"],
+                         "traffic": None},
+            "prefill": {"tokens": prompt_len, "seconds": prefill_s, "tok_s": prompt_len / prefill_s},
+            "b16": b16, "clocks": clk.summary()}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     return 0
 
 
@@ -355,6 +480,8 @@ def main():
     ap.add_argument("--ncu-steps", type=int, default=0,
                     help="profiling run for ncu: 8-token prefill (2 fused 4-token steps), then this many "
                          "device-chained decode steps; prints a short JSON line")
+    ap.add_argument("--workload", default="E", choices=["E", "P", "X"],
+                    help="E: 8B Q4_K b=1 (+b=32) [default]; P: 8B Q8_0, packed KV, 64 requests; X: 70B shape, TP")
     ap.add_argument("--sweep", action="store_true", help="config S: quantized matvec/matmul sweep, one JSON line per case")
     ap.add_argument("--matvec", nargs=4, metavar=("FMT", "N", "K", "M"), help="one config-S case, three launches")
     args = ap.parse_args()
@@ -369,11 +496,19 @@ def main():
     if args.ncu_steps:
         return run_ncu_case(args)
 
+    if args.workload == "P":
+        return run_workload_p(args)
     world, rank, local = dist_env()
     import torch
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     dist = init_dist(world, "nccl")
+    if args.workload == "X":
+        rc = run_workload_x(args, dist, rank, world, local)
+        if dist is not None:
+            barrier(dist, device)
+            dist.destroy_process_group()
+        return rc
 
     import nexus_b200 as nb
     from nexus_b200 import _lib as L

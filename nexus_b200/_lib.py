@@ -40,7 +40,6 @@ OP_QUANTIZE, OP_DEQUANTIZE, OP_QMATVEC, OP_ROPE, OP_ARGMAX, OP_KV_QUANTIZE = 7, 
 
 CFG_NO_GRAPH = 0x1
 CFG_NO_PDL = 0x2
-CFG_NO_PREFETCH = 0x4
 
 
 class Caps(C.Structure):

@@ -93,11 +93,6 @@ __device__ __forceinline__ void tma_load_1d(void *dst, const void *src, unsigned
         : "memory");
 }
 
-// Bulk prefetch of global memory into L2 (bytes a multiple of 16).
-__device__ __forceinline__ void prefetch_l2(const void *src, unsigned bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-
 // Issue forms for a converged warp: one lane, chosen by elect.sync inside the
 // same asm block, arms the barrier or starts the copy (a lone divergent
 // thread issues these several times slower).

@@ -153,9 +153,6 @@ struct Mat {
     }
 };
 
-// The next matrix of the step, prefetched into L2 by the GEMV before it.
-static void set_prefetch(const nexus_cuda_model *m, GemvParams &g, const Mat *next);
-
 // Upload rows x k raw block bytes (already row-permuted) and repack to tiles.
 static int make_mat(nexus_cuda_backend *b, int fmt, int n, int k, const uint8_t *raw_host, Mat &m) {
     if (!tile_supported(fmt)) return set_err(b, NEXUS_E_UNSUPPORTED_FORMAT, "matrix format not supported by the GEMV");
@@ -863,7 +860,7 @@ extern "C" int nexus_cuda_qweight_dequantize(nexus_cuda_qweight *w, float *out) 
 // ---------------------------------------------------------------------------
 // model
 // ---------------------------------------------------------------------------
-static constexpr int kMaxChunk = 64;  // tokens per fused step (prefill chunk, decode batch)
+static constexpr int kMaxChunk = 256;  // tokens per fused step (prefill chunk, decode batch)
 
 struct Layer {
     float *attn_norm = nullptr, *ffn_norm = nullptr;
@@ -901,7 +898,7 @@ struct nexus_cuda_model {
     size_t bpt_k = 0, bpt_v = 0;
     int nsplit[kMaxChunk + 1] = {};
     cudaGraphExec_t graph[kMaxChunk + 1] = {};
-    bool use_graph = true, use_pdl = true, prefetch = true;
+    bool use_graph = true, use_pdl = true;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     float last_ms = 0.0f;
     std::vector<void *> allocs;
@@ -1037,7 +1034,6 @@ static int model_load(nexus_cuda_backend *b, const char *path, nexus_cuda_model 
     m->bits_v = b->cfg.kv_bits_v;
     m->use_graph = !(b->cfg.flags & NEXUS_CFG_NO_GRAPH);
     m->use_pdl = !(b->cfg.flags & NEXUS_CFG_NO_PDL);
-    m->prefetch = !(b->cfg.flags & NEXUS_CFG_NO_PREFETCH);
     cudaSetDevice(b->device);
 
     // embedding (raw blocks; rows decoded per token on the device)
@@ -1302,12 +1298,6 @@ static void set_split_scratch(const nexus_cuda_model *m, GemvParams &g) {
     g.err = reinterpret_cast<int *>(m->out_tokens + kMaxChunk);
 }
 
-static void set_prefetch(const nexus_cuda_model *m, GemvParams &g, const Mat *next) {
-    if (!next || !next->main || !m->prefetch) return;
-    g.pf = next->main;
-    g.pf_bytes = next->bytes - tile_aux_bytes(next->fmt, (size_t)next->n, (size_t)next->k);
-}
-
 // One fused linear layer of the step: the tensor-core GEMM for steps of
 // kGemmMinM+ tokens in a format it covers, else the GEMV.
 static cudaError_t launch_linear(nexus_cuda_model *m, GemvParams g, cudaStream_t st) {
@@ -1386,7 +1376,6 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         g.qkv.kv_scratch = packed ? m->kv_scratch : nullptr;
         g.qkv.seqs = m->seqs;
         g.qkv.seq_ids = m->seq_ids;
-        set_prefetch(m, g, &L.o);
         if (prof) prof->begin();
         if ((e = launch_linear(m, g, st)) != cudaSuccess) return e;
         if (prof) prof->end("qkv", gemv_bytes(L.qkv, mc, H, qdim + 2 * kv_dim) + 4.0 * H);
@@ -1471,7 +1460,6 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         o.x_stride = qdim;
         o.epi = lead ? EPI_ADD : EPI_STORE;
         o.y = m->hidden;
-        set_prefetch(m, o, &L.gateup);
         o.y_stride = H;
         if (prof) prof->begin();
         if ((e = launch_linear(m, o, st)) != cudaSuccess) return e;
@@ -1492,7 +1480,6 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         gu.x_stride = H;
         gu.norm_w = L.ffn_norm;
         gu.epi = EPI_SWIGLU;
-        set_prefetch(m, gu, &L.down);
         gu.y = m->gated;
         gu.y_stride = F;
         if (prof) prof->begin();
@@ -1512,7 +1499,6 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         dn.x_stride = F;
         dn.epi = lead ? EPI_ADD : EPI_STORE;
         dn.y = m->hidden;
-        set_prefetch(m, dn, l + 1 < I.num_layers ? &m->layers[l + 1].qkv : (m->has_head ? &m->head : nullptr));
         dn.y_stride = H;
         if (prof) prof->begin();
         if ((e = launch_linear(m, dn, st)) != cudaSuccess) return e;

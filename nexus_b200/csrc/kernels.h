@@ -73,9 +73,6 @@ struct GemvParams {
     int nst;                // weight ring slots per warp (set by the launcher)
     int *err;               // device flag set when a bounded wait gives up (may be NULL)
     int row_offset;         // EPI_ARGMAX: global index of local row 0 (vocab slice of a rank)
-    // L2 prefetch of the matrix the next kernel of the step streams (may be NULL)
-    const void *pf;
-    size_t pf_bytes;
 };
 
 cudaError_t launch_gemv(const GemvParams &p, cudaStream_t st);

@@ -79,6 +79,16 @@ __global__ void __launch_bounds__(256) k_gemm_prep(const float *__restrict__ x, 
         int q, pos;
         if constexpr (FMT == 12) {
             q4k_kpos(tid, q, pos);
+        } else if constexpr (FMT == 10) {
+            // Q2_K: sub-block j = tid/16 in quarter j/4; bit-plane k, bytes 0,2,1,3
+            const int j = tid >> 4, i = tid & 15, k4 = i >> 2, b = i & 3;
+            q = j >> 2;
+            pos = 16 * (j & 3) + 4 * k4 + (((b & 1) << 1) | (b >> 1));
+        } else if constexpr (FMT == 2) {
+            // Q4_0: block tid/32 in quarter tid/64; low nibbles then high, bytes 0,2,1,3
+            const int blk = tid >> 5, i = tid & 31, nib = i >> 4, wi = (i & 15) >> 2, b = i & 3;
+            q = blk >> 1;
+            pos = 32 * (blk & 1) + 16 * nib + 4 * wi + (((b & 1) << 1) | (b >> 1));
         } else {
             q = tid >> 6;  // natural K order
             pos = tid & 63;
@@ -88,10 +98,25 @@ __global__ void __launch_bounds__(256) k_gemm_prep(const float *__restrict__ x, 
         *reinterpret_cast<__half *>(qb) = hi;
         *reinterpret_cast<__half *>(qb + NT * 16) = lo;
         if constexpr (!GemmFmt<FMT>::MIN) continue;
+        uint8_t *mb = base + 4 * NT * 256;
+        if constexpr (FMT == 10) {
+            // Q2_K: sixteen 16-element sub-blocks, sums at K positions 0..15
+            float sj = v;
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) sj += __shfl_xor_sync(0xffffffffu, sj, o);
+            if ((lane & 15) == 0) {
+                const int j = tid >> 4;
+                const __half sh = __float2half_rn(sj);
+                const __half sl = __float2half_rn(sj - __half2float(sh));
+                uint8_t *cb = mb + (j >> 3) * NT * 32 + n * 16 + (j & 7) * 2;
+                *reinterpret_cast<__half *>(cb) = sh;
+                *reinterpret_cast<__half *>(cb + NT * 16) = sl;
+            }
+            continue;
+        }
         // sub-block sums (sub-block j = elements 32j..32j+31 = warp j): K
         // positions 0..7 of the min operand, positions 8..15 zero
         const float sj = warp_sum(v);
-        uint8_t *mb = base + 4 * NT * 256;
         if (lane == 0) {
             const __half sh = __float2half_rn(sj);
             const __half sl = __float2half_rn(sj - __half2float(sh));
@@ -186,7 +211,7 @@ static cudaError_t launch_fmt(const GemvParams &p, const GemmScratch &sc, cudaSt
 
 }  // namespace qg
 
-bool gemm_supported(int fmt) { return fmt == 12 || fmt == 8; }
+bool gemm_supported(int fmt) { return fmt == 12 || fmt == 8 || fmt == 10 || fmt == 2; }
 
 GemmScratchSize gemm_scratch_size(int m, int n, int k) {
     const qg::GemmShape g = qg::plan(m, n, k);
@@ -201,7 +226,12 @@ GemmScratchSize gemm_scratch_size(int m, int n, int k) {
 
 cudaError_t launch_gemm(const GemvParams &p, const GemmScratch &sc, cudaStream_t st) {
     if (!gemm_supported(p.fmt) || p.k % 256 != 0 || p.n <= 0 || p.m <= 0) return cudaErrorInvalidValue;
-    return p.fmt == 12 ? qg::launch_fmt<12>(p, sc, st) : qg::launch_fmt<8>(p, sc, st);
+    switch (p.fmt) {
+    case 12: return qg::launch_fmt<12>(p, sc, st);
+    case 8: return qg::launch_fmt<8>(p, sc, st);
+    case 10: return qg::launch_fmt<10>(p, sc, st);
+    default: return qg::launch_fmt<2>(p, sc, st);
+    }
 }
 
 }  // namespace nx

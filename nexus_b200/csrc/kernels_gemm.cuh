@@ -67,6 +67,18 @@ struct GemmFmt<8> {  // Q8_0
     static constexpr int A_MATS = 2;
     static constexpr int RAW_SLOTS = 2, STAGES = 3;
 };
+template <>
+struct GemmFmt<10> {  // Q2_K: exact sc_j*q (<= 45) and sixteen 4-bit mins
+    static constexpr bool MIN = true;
+    static constexpr int A_MATS = 1;
+    static constexpr int RAW_SLOTS = 4, STAGES = 6;
+};
+template <>
+struct GemmFmt<2> {  // Q4_0: d*(q-8) as an exact f16 pair
+    static constexpr bool MIN = false;
+    static constexpr int A_MATS = 2;
+    static constexpr int RAW_SLOTS = 3, STAGES = 3;
+};
 
 template <int FMT>
 struct Raw {
@@ -281,6 +293,62 @@ __device__ __forceinline__ void dq_q80_quarter(const uint32_t (&w)[16], uint32_t
     }
 }
 
+// Q2_K dequantization of one quarter (sub-blocks 4q..4q+3, one tile word
+// each; bits 2k..2k+1 of byte b are element 16j+4k+b) into exact f16
+// sc_j*q.  K order inside a sub-block: bit-plane k, bytes 0,2,1,3.
+__device__ __forceinline__ void dq_q2k_quarter(const uint32_t (&w)[4], uint32_t sc4, uint8_t *a_row) {
+#pragma unroll
+    for (int jj = 0; jj < 4; jj++) {
+        const float sc = (float)((sc4 >> (8 * jj)) & 0xfu);
+        const uint32_t ms = f16x2_splat(sc), bs = f16x2_splat(-1024.0f * sc);
+        uint32_t v[8];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            v[2 * k] = hfma2u(lop_or(w[jj] >> (2 * k), 0x00030003u), ms, bs);
+            v[2 * k + 1] = hfma2u(lop_or(w[jj] >> (2 * k + 8), 0x00030003u), ms, bs);
+        }
+        *reinterpret_cast<uint4 *>(a_row + (2 * jj) * 2048) = make_uint4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<uint4 *>(a_row + (2 * jj + 1) * 2048) = make_uint4(v[4], v[5], v[6], v[7]);
+    }
+}
+
+// Q4_0 dequantization of one quarter (blocks 2q, 2q+1; element i of a block
+// is the low nibble of byte i%16 for i < 16, else the high nibble) into the
+// stage's hi and lo matrices: w = d*(q-8) exactly as hi + lo.  K order per
+// block: low nibbles then high nibbles, bytes 0,2,1,3 inside each word.
+__device__ __forceinline__ void dq_q40_quarter(const uint32_t (&w)[8], uint32_t d01, uint8_t *a_row) {
+    const uint32_t bias = 0x64086408u;  // f16x2 (1032, 1032): (1024 + q) - 1032 = q - 8
+#pragma unroll
+    for (int b = 0; b < 2; b++) {
+        const uint32_t dh = (d01 >> (16 * b)) & 0xffffu;
+        const uint32_t d2 = dh | (dh << 16);
+#pragma unroll
+        for (int nib = 0; nib < 2; nib++) {
+#pragma unroll
+            for (int kc = 0; kc < 2; kc++) {
+                uint32_t hv[4], lv[4];
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const uint32_t x = w[4 * b + 2 * kc + h] >> (4 * nib);
+                    uint32_t q02 = lop_or(x, 0x000f000fu), q13 = lop_or(x >> 8, 0x000f000fu);
+                    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(q02) : "r"(q02), "r"(bias));
+                    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(q13) : "r"(q13), "r"(bias));
+                    uint32_t h02, h13;
+                    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(h02) : "r"(q02), "r"(d2));
+                    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(h13) : "r"(q13), "r"(d2));
+                    hv[2 * h] = h02;
+                    hv[2 * h + 1] = h13;
+                    lv[2 * h] = hfma2u(q02, d2, h02 ^ 0x80008000u);
+                    lv[2 * h + 1] = hfma2u(q13, d2, h13 ^ 0x80008000u);
+                }
+                const int chunk = 4 * b + 2 * nib + kc;
+                *reinterpret_cast<uint4 *>(a_row + chunk * 2048) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+                *reinterpret_cast<uint4 *>(a_row + 16384 + chunk * 2048) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+            }
+        }
+    }
+}
+
 template <int FMT, int NT, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     k_qgemm(GemvParams p, GemmShape g, const uint8_t *__restrict__ bimg, const float *__restrict__ tok_scale) {
@@ -354,6 +422,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const size_t item = (size_t)(4 * rt + gi) * g.n_sb + s;
                     tma_load_1d_w(dst + gi * R::ITEM, reinterpret_cast<const uint8_t *>(p.w_main) + item * R::ITEM,
                                   R::ITEM, &raw_full[slot]);
+                    if constexpr (R::AUXB > 0)
+                        tma_load_1d_w(dst + 4 * R::ITEM + gi * R::AUXB,
+                                      reinterpret_cast<const uint8_t *>(p.w_aux) + item * R::AUXB, R::AUXB,
+                                      &raw_full[slot]);
                 }
             }
         }
@@ -563,6 +635,80 @@ __global__ void __launch_bounds__(kThreads, 1)
                             __syncwarp();
                             if (lane == 0) mbar_arrive(&mn_full[ms]);
                         }
+                    }
+                } else if constexpr (FMT == 10) {
+                    // Q2_K: chunk 0 = sixteen scale bytes (sc | m << 4), chunk 1+q = the
+                    // four sub-block words of quarter q, side word = d | dmin << 16
+                    const uint4 c0 = *reinterpret_cast<const uint4 *>(rawp);
+                    const uint4 qa = *reinterpret_cast<const uint4 *>(rawp + (1 + 2 * half) * 512);
+                    const uint4 qb = *reinterpret_cast<const uint4 *>(rawp + (2 + 2 * half) * 512);
+                    const uint32_t auxw = *reinterpret_cast<const uint32_t *>(
+                        smem + S::RAW + slot * R::SLOT + 4 * R::ITEM + rg * R::AUXB + lane * 4);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&raw_empty[slot]);
+                    d = h2f_bits(auxw);
+                    dm = h2f_bits(auxw >> 16);
+                    const uint32_t scw[4] = {c0.x, c0.y, c0.z, c0.w};
+#pragma unroll
+                    for (int qq = 0; qq < 2; qq++) {
+                        const int q = 2 * half + qq;
+                        const unsigned c = 4 * n + q;
+                        const int as = c % kASlots;
+                        bwait(&st_empty[as], ((c / kASlots) & 1) ^ 1, &abort_s, p.err);
+                        const uint4 wv = qq ? qb : qa;
+                        const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+                        dq_q2k_quarter(w4, scw[q] & 0x0f0f0f0fu, smem + S::A + as * S::A_BYTES + r * 16);
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&st_full[as]);
+                        if (q == 0) {
+                            // Amin row: m_0..m_15 (the high nibbles of the scale bytes)
+                            const int ms = n & 1;
+                            bwait(&mn_empty[ms], ((n >> 1) & 1) ^ 1, &abort_s, p.err);
+                            uint32_t mw[8];
+#pragma unroll
+                            for (int i = 0; i < 8; i++) {
+                                const uint32_t sw = scw[i >> 1] >> (16 * (i & 1));
+                                const float m0 = (float)((sw >> 4) & 0xfu), m1 = (float)((sw >> 12) & 0xfu);
+                                mw[i] = __half_as_ushort(__float2half_rn(m0)) |
+                                        ((uint32_t)__half_as_ushort(__float2half_rn(m1)) << 16);
+                            }
+                            uint8_t *am = smem + S::AMIN + ms * S::AMIN_BYTES + r * 16;
+                            *reinterpret_cast<uint4 *>(am) = make_uint4(mw[0], mw[1], mw[2], mw[3]);
+                            *reinterpret_cast<uint4 *>(am + 2048) = make_uint4(mw[4], mw[5], mw[6], mw[7]);
+                            fence_proxy_async_smem();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&mn_full[ms]);
+                        }
+                    }
+                } else if constexpr (FMT == 2) {
+                    // Q4_0: chunk 0 = the eight block scales, chunk 1+b = qs of block b
+                    const uint4 c0 = *reinterpret_cast<const uint4 *>(rawp);
+                    uint32_t wq[16];
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        const uint4 v = *reinterpret_cast<const uint4 *>(rawp + (1 + 4 * half + c) * 512);
+                        wq[4 * c] = v.x;
+                        wq[4 * c + 1] = v.y;
+                        wq[4 * c + 2] = v.z;
+                        wq[4 * c + 3] = v.w;
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&raw_empty[slot]);
+                    const uint32_t dsc[4] = {c0.x, c0.y, c0.z, c0.w};
+#pragma unroll
+                    for (int qq = 0; qq < 2; qq++) {
+                        const int q = 2 * half + qq;
+                        const unsigned c = 4 * n + q;
+                        const int as = c % kASlots;
+                        bwait(&st_empty[as], ((c / kASlots) & 1) ^ 1, &abort_s, p.err);
+                        uint32_t w8[8];
+#pragma unroll
+                        for (int i = 0; i < 8; i++) w8[i] = wq[8 * qq + i];
+                        dq_q40_quarter(w8, half ? dsc[2 + qq] : dsc[qq], smem + S::A + as * S::A_BYTES + r * 16);
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&st_full[as]);
                     }
                 } else {
                     // Q8_0: chunk 0 = the eight block scales, chunks 1+2b, 2+2b = qs of block b

@@ -456,15 +456,6 @@ __global__ void __launch_bounds__(Ring<FMT>::W * 32, 1) k_gemv(GemvParams p) {
     // Stream the first items before waiting on the previous grid.
     if (lane == 0)
         for (int j = 0; j < NST && j < n_total; j++) issue(j);
-    // Pull the next kernel's matrix into L2 while this one runs: this CTA's
-    // share, in 16 KB requests spread over its warps.
-    if (p.pf_bytes && lane == 0) {
-        const size_t per = ((p.pf_bytes + gridDim.x - 1) / gridDim.x + 15) & ~(size_t)15;
-        const size_t b0 = (size_t)blockIdx.x * per;
-        const size_t lim = b0 < p.pf_bytes ? min(per, p.pf_bytes - b0) : 0;
-        for (size_t off = (size_t)warp * 16384; off < lim; off += (size_t)W * 16384)
-            prefetch_l2(reinterpret_cast<const uint8_t *>(p.pf) + b0 + off, (unsigned)min((size_t)16384, lim - off));
-    }
     if (p.pdl) {
         pdl_launch_dependents();
         pdl_wait();

@@ -306,13 +306,22 @@ class InferenceEngine:
                                               _ptr(out)), self.backend.handle)
         return out.tolist()
 
-    def decode_batch(self, items: Sequence[tuple[int, int, int]], want_logits: bool = False):
-        """items: (seq_id, token, position) per sequence; returns (tokens, logits)."""
+    def decode_batch(self, items: Sequence[tuple[int, int, int]], want_logits: bool = False,
+                     page_ids: Optional[Sequence[Sequence[int]]] = None):
+        """items: (seq_id, token, position) per sequence; page_ids: optional
+        scheduler page list per item (Scheduler::allocate_kv_pages,
+        src/scheduler.rs:333-361); returns (tokens, logits)."""
         n = len(items)
         arr = (L.DecodeItem * max(n, 1))()
+        keep = []
         for i, (sid, tok, pos) in enumerate(items):
             arr[i].seq_id, arr[i].token, arr[i].position = sid, tok, pos
             arr[i].n_pages, arr[i].page_ids = 0, None
+            if page_ids is not None:
+                pg = np.ascontiguousarray(np.asarray(page_ids[i], np.uint32))
+                keep.append(pg)
+                arr[i].n_pages = pg.size
+                arr[i].page_ids = pg.ctypes.data_as(C.POINTER(C.c_uint32))
         toks = np.zeros(max(n, 1), np.uint32)
         logits = np.empty((n, self.info.vocab_rows), np.float32) if want_logits else None
         L.check(self._lib.nexus_cuda_decode_batch(self.model, arr, n, _ptr(toks),

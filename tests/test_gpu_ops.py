@@ -102,7 +102,7 @@ def test_qmatvec_input_edge_cases(backend, oracle, nb):
         assert rel_err(y[t], oracle.qmatvec(oracle.Q4_K, q, n, k, x[t])) < REL_TOL
 
 
-@pytest.mark.parametrize("fmt", ["Q4_K", "Q8_0"])
+@pytest.mark.parametrize("fmt", FORMATS)
 @pytest.mark.parametrize("m", [8, 16, 17, 64])
 @pytest.mark.parametrize("shape", [(4096, 4096), (1024, 4096), (4096, 14336)], ids=lambda s: f"{s[0]}x{s[1]}")
 def test_qgemm_batched(backend, oracle, nb, shape, m, fmt):
@@ -120,7 +120,7 @@ def test_qgemm_batched(backend, oracle, nb, shape, m, fmt):
     w.close()
 
 
-@pytest.mark.parametrize("fmt", ["Q4_K", "Q8_0"])
+@pytest.mark.parametrize("fmt", FORMATS)
 def test_qgemm_edge_cases(backend, oracle, nb, fmt):
     """Zero, huge, tiny and mixed-scale tokens; a partial 128-row tile."""
     rng = np.random.default_rng(61)
