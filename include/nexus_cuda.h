@@ -93,7 +93,6 @@ typedef struct {
 
 #define NEXUS_CFG_NO_GRAPH 0x1u  /* launch kernels directly instead of a CUDA graph */
 #define NEXUS_CFG_NO_PDL 0x2u    /* no programmatic dependent launch between kernels */
-#define NEXUS_CFG_NO_PREFETCH 0x4u /* no L2 prefetch of the next matrix during each decode GEMV */
 
 typedef struct nexus_cuda_backend nexus_cuda_backend;
 
@@ -324,6 +323,9 @@ typedef struct {
     int head_format;        /* output (LM head); -1 = no output.weight (tied) */
     int norm_format;        /* attn_norm/ffn_norm/output_norm */
     int threads;            /* generator threads (0 = all cores) */
+    uint32_t repeat_chunks; /* 0 = every element drawn; n = each tensor repeats its first
+                               n * 65536 drawn elements (quick generation of very large
+                               models; the kernels' work is unchanged) */
 } nexus_synth_config;
 int nexus_synth_model_write(const char *path, const nexus_synth_config *cfg);
 

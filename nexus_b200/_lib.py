@@ -84,7 +84,7 @@ class SynthConfig(C.Structure):
                 ("context_length", C.c_uint32), ("rope_theta", C.c_float), ("weight_std", C.c_float),
                 ("seed", C.c_uint64), ("attn_format", C.c_int), ("ffn_format", C.c_int),
                 ("embd_format", C.c_int), ("head_format", C.c_int), ("norm_format", C.c_int),
-                ("threads", C.c_int)]
+                ("threads", C.c_int), ("repeat_chunks", C.c_uint32)]
 
 
 P = C.c_void_p

@@ -35,10 +35,13 @@ CONFIGS = {
     "llama8b_q8": dict(num_layers=32, hidden_size=4096, num_heads=32, num_kv_heads=8, ff_dim=14336,
                        vocab_size=128256, context_length=8448, rope_theta=500000.0, attn_format=Q8_0,
                        ffn_format=Q8_0, embd_format=Q8_0, head_format=Q8_0, norm_format=Q8_0),
-    # Llama-3-70B shape, Q4_K attention, Q2_K FFN, Q8_0 embedding/head (assumed)
+    # Llama-3-70B shape, Q4_K attention, Q2_K FFN, Q8_0 embedding/head (assumed).
+    # Each tensor repeats its first 64 x 65536 drawn elements (4 Mi values, a
+    # few MB of quantized bytes) so the 27 GB file is written in seconds; the
+    # kernels stream every byte from its own address all the same.
     "llama70b": dict(num_layers=80, hidden_size=8192, num_heads=64, num_kv_heads=8, ff_dim=28672,
                      vocab_size=128256, context_length=4352, rope_theta=500000.0, attn_format=Q4_K,
-                     ffn_format=Q2_K, embd_format=Q8_0, head_format=Q8_0, norm_format=Q4_K),
+                     ffn_format=Q2_K, embd_format=Q8_0, head_format=Q8_0, norm_format=Q4_K, repeat_chunks=64),
 }
 
 

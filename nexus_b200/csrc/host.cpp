@@ -429,22 +429,29 @@ int synth_model_write(const char *path, const nexus_synth_config *cfg, std::stri
         const size_t CH = 65536;
         size_t nchunks = (n + CH - 1) / CH;
         size_t be = (size_t)block_elems(t.fmt), bb = (size_t)block_bytes(t.fmt);
+        // drawn chunks; with repeat_chunks the rest copy them (a whole chunk
+        // is whole blocks, so its quantized bytes repeat exactly)
+        const size_t drawn = C.repeat_chunks ? std::min<size_t>(nchunks, C.repeat_chunks) : nchunks;
         auto work = [&](int tid) {
             std::vector<float> vals(CH);
-            for (size_t c = (size_t)tid; c < nchunks; c += (size_t)threads) {
+            for (size_t c = (size_t)tid; c < drawn; c += (size_t)threads) {
                 size_t s = c * CH, cnt = std::min(CH, n - s);
                 if (t.ones) std::fill(vals.begin(), vals.begin() + cnt, 1.0f);
                 else gen_normal(C.seed, stream, s, cnt, C.weight_std, vals.data());
                 quantize_host(t.fmt, vals.data(), cnt, buf.data() + s / be * bb);
             }
         };
-        int nt = (int)std::min<size_t>((size_t)threads, nchunks);
+        int nt = (int)std::min<size_t>((size_t)threads, drawn);
         if (nt <= 1) {
             work(0);
         } else {
             std::vector<std::thread> pool;
             for (int k = 0; k < nt; k++) pool.emplace_back(work, k);
             for (auto &th : pool) th.join();
+        }
+        for (size_t c = drawn; c < nchunks; c++) {
+            const size_t s = c * CH, cnt = std::min(CH, n - s), src = (c % drawn) * CH;
+            memcpy(buf.data() + s / be * bb, buf.data() + src / be * bb, cnt / be * bb);
         }
         ok = fwrite(buf.data(), 1, buf.size(), fp) == buf.size();
     }

@@ -380,14 +380,18 @@ def tp_plan(num_heads: int, num_kv_heads: int, head_dim: int, ff_dim: int, vocab
 def write_synthetic_model(path: str, *, num_layers: int, hidden_size: int, num_heads: int, num_kv_heads: int,
                           ff_dim: int, vocab_size: int, context_length: int, rope_theta: float,
                           attn_format: int, ffn_format: int, embd_format: int, head_format: int,
-                          norm_format: int, weight_std: float = 0.02, seed: int = 0, threads: int = 0) -> None:
-    """Seeded LLaMA-style GGUF v3 in nexus-convert's file conventions."""
+                          norm_format: int, weight_std: float = 0.02, seed: int = 0, threads: int = 0,
+                          repeat_chunks: int = 0) -> None:
+    """Seeded LLaMA-style GGUF v3 in nexus-convert's file conventions
+    (repeat_chunks > 0: each tensor repeats its first repeat_chunks * 65536
+    drawn elements, for quick generation of very large models)."""
     lib = L.load()
     cfg = L.SynthConfig(num_layers=num_layers, hidden_size=hidden_size, num_heads=num_heads,
                         num_kv_heads=num_kv_heads, ff_dim=ff_dim, vocab_size=vocab_size,
                         context_length=context_length, rope_theta=rope_theta, weight_std=weight_std, seed=seed,
                         attn_format=attn_format, ffn_format=ffn_format, embd_format=embd_format,
-                        head_format=head_format, norm_format=norm_format, threads=threads)
+                        head_format=head_format, norm_format=norm_format, threads=threads,
+                        repeat_chunks=repeat_chunks)
     L.check(lib.nexus_synth_model_write(str(path).encode(), C.byref(cfg)))
 
 
