@@ -149,9 +149,15 @@ enum {
     NEXUS_OP_QMATVEC = 9,     /* Y[m,n] = X[m,k] @ W[n,k]^T with W in a block format */
     NEXUS_OP_ROPE = 10,       /* rope_single over every head, src/kernel/mod.rs:258-271 */
     NEXUS_OP_ARGMAX = 11,     /* greedy_token, src/engine/mod.rs:809-817 */
-    NEXUS_OP_KV_QUANTIZE = 12 /* PackedKvBuffer::add of one vector, src/engine/mod.rs:209-232:
+    NEXUS_OP_KV_QUANTIZE = 12, /* PackedKvBuffer::add of one vector, src/engine/mod.rs:209-232:
                                  a = len floats, k = bits; out = ceil(len*bits/8) packed bytes
                                  followed by the f32 min and f32 scale */
+    NEXUS_OP_ATTENTION_PACKED = 13 /* KvCache::attention_decode over packed buffers
+                                 (src/engine/mod.rs:452-499 with KvCacheBuffer::Quantized):
+                                 a = q (m*k floats); b = keys, c = values, each n rows of
+                                 ceil(kv_heads*k*bits/8) bytes (PackedKvBuffer layout,
+                                 src/engine/mod.rs:187-232) followed by n f32 mins and n f32
+                                 scales; format = bits_k | bits_v << 8 (1..8 each) */
 };
 
 typedef struct {

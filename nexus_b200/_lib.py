@@ -37,6 +37,7 @@ FORMAT_IDS = {v: k for k, v in FORMAT_NAMES.items()}
 # op kinds
 OP_MATMUL, OP_ATTENTION, OP_LAYER_NORM, OP_RMS_NORM, OP_ADD, OP_MUL, OP_SOFTMAX = range(7)
 OP_QUANTIZE, OP_DEQUANTIZE, OP_QMATVEC, OP_ROPE, OP_ARGMAX, OP_KV_QUANTIZE = 7, 8, 9, 10, 11, 12
+OP_ATTENTION_PACKED = 13
 
 CFG_NO_GRAPH = 0x1
 CFG_NO_PDL = 0x2

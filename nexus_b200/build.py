@@ -32,6 +32,7 @@ UNITS = {
     "kernels_gemv_q2k.cu": [],
     "kernels_gemm.cu": [],
     "kernels_attn.cu": [],
+    "kernels_attn_pk.cu": [],
     "kernels_misc.cu": [],
     "engine.cu": [],
     "noalloc.cu": [],

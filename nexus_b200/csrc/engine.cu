@@ -720,6 +720,78 @@ extern "C" int nexus_cuda_execute(nexus_cuda_backend *b, const nexus_op *op) {
         if (e == cudaSuccess) e = e2;
         break;
     }
+    case NEXUS_OP_ATTENTION_PACKED: {
+        // packed keys/values: [n][bpt] codes, n mins, n scales, per stream
+        size_t hq = op->m, seq = op->n, hd = op->k, hkv = op->kv_heads ? op->kv_heads : op->m;
+        const int bk = op->format & 0xff, bv = (op->format >> 8) & 0xff;
+        if (seq == 0 || hkv == 0 || hq % hkv || bk < 1 || bk > 8 || bv < 1 || bv > 8 || (hd != 32 && hd != 64 && hd != 128))
+            return set_err(b, NEXUS_E_INVALID, "attention_packed: bad shape or bits");
+        const size_t kv_dim = hkv * hd, bpk = (kv_dim * bk + 7) / 8, bpv = (kv_dim * bv + 7) / 8;
+        const size_t offk = (seq * bpk + 15) / 16 * 16, offv = (seq * bpv + 15) / 16 * 16;
+        out_bytes = hq * hd * 4;
+        NX_CUDA(b, stage_in(op->a, hq * hd * 4, dev, A, st));
+        NX_CUDA(b, stage_out(op->out, out_bytes, dev, O));
+        uint8_t *kb = nullptr, *vb = nullptr;
+        DevSeq *ds = nullptr;
+        uint32_t *sid = nullptr;
+        float *part = nullptr;
+        unsigned *ctr = nullptr;
+        const int nsplit = (int)std::min<size_t>(64, std::max<size_t>(1, (seq + 63) / 64));
+        const size_t G = hq / hkv;
+        NX_CUDA(b, dalloc(&kb, offk + 8 * seq));
+        NX_CUDA(b, dalloc(&vb, offv + 8 * seq));
+        NX_CUDA(b, dalloc(&ds, 1));
+        NX_CUDA(b, dalloc(&sid, 1));
+        NX_CUDA(b, dalloc(&part, hkv * nsplit * G * (hd + 2)));
+        NX_CUDA(b, dalloc(&ctr, hkv));
+        const cudaMemcpyKind kind = dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+        const uint8_t *sk = static_cast<const uint8_t *>(op->b), *sv = static_cast<const uint8_t *>(op->c);
+        NX_CUDA(b, cudaMemcpyAsync(kb, sk, seq * bpk, kind, st));
+        NX_CUDA(b, cudaMemcpyAsync(kb + offk, sk + seq * bpk, 8 * seq, kind, st));
+        NX_CUDA(b, cudaMemcpyAsync(vb, sv, seq * bpv, kind, st));
+        NX_CUDA(b, cudaMemcpyAsync(vb + offv, sv + seq * bpv, 8 * seq, kind, st));
+        DevSeq hs = {};
+        hs.seq_len = (uint32_t)seq;
+        hs.slot = (uint32_t)(seq - 1);
+        NX_CUDA(b, cudaMemsetAsync(sid, 0, 4, st));
+        NX_CUDA(b, cudaMemsetAsync(ctr, 0, hkv * 4, st));
+        NX_CUDA(b, cudaMemcpyAsync(ds, &hs, sizeof(hs), cudaMemcpyHostToDevice, st));
+        AttnParams p = {};
+        p.hq = (int)hq;
+        p.hkv = (int)hkv;
+        p.head_dim = (int)hd;
+        p.m = 1;
+        p.q = (const float *)A.d;
+        p.out = (float *)O.d;
+        p.scale = op->scale != 0.0f ? op->scale : 1.0f / sqrtf((float)hd);
+        p.bits_k = bk;
+        p.bits_v = bv;
+        p.kp_data = kb;
+        p.vp_data = vb;
+        p.kp_min = reinterpret_cast<const float *>(kb + offk);
+        p.kp_scale = p.kp_min + seq;
+        p.vp_min = reinterpret_cast<const float *>(vb + offv);
+        p.vp_scale = p.vp_min + seq;
+        p.pk_bpt_k = bpk;
+        p.pk_bpt_v = bpv;
+        p.pk_seq_tokens = seq;
+        p.seqs = ds;
+        p.seq_ids = sid;
+        p.kv_dim = (int)kv_dim;
+        p.nsplit = nsplit;
+        p.part = part;
+        p.counters = ctr;
+        e = launch_attention(p, st);
+        cudaError_t e2 = cudaStreamSynchronize(st);
+        cudaFree(kb);
+        cudaFree(vb);
+        cudaFree(ds);
+        cudaFree(sid);
+        cudaFree(part);
+        cudaFree(ctr);
+        if (e == cudaSuccess) e = e2;
+        break;
+    }
     default: return set_err(b, NEXUS_E_INVALID, "unknown op kind");
     }
     if (e != cudaSuccess) return set_err(b, NEXUS_E_CUDA, std::string("execute: ") + cudaGetErrorString(e));
@@ -896,7 +968,8 @@ struct nexus_cuda_model {
     std::vector<uint32_t> seq_len;
     uint32_t max_seq = 0, max_batch = 1, bits_k = 0, bits_v = 0;
     size_t bpt_k = 0, bpt_v = 0;
-    int nsplit[kMaxChunk + 1] = {};
+    int nsplit[kMaxChunk + 1] = {};     // attention slices per (sequence, KV head), float cache
+    int nsplit_pk[kMaxChunk + 1] = {};  // the same for the packed-cache tensor-core kernel
     cudaGraphExec_t graph[kMaxChunk + 1] = {};
     bool use_graph = true, use_pdl = true;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
@@ -1211,6 +1284,10 @@ static int model_load(nexus_cuda_backend *b, const char *path, nexus_cuda_model 
     // kernel uses only as many as the current context needs
     int max_split = std::max(1, std::min(64, (int)((m->max_seq + 63) / 64)));
     for (int mm = 1; mm <= MC; mm++) m->nsplit[mm] = max_split;
+    // the packed-cache kernel: about 8 CTAs per SM over the whole step (its
+    // CTAs stream whole 64-token tiles and need no more slices than that)
+    for (int mm = 1; mm <= MC; mm++)
+        m->nsplit_pk[mm] = std::max(1, std::min(max_split, (148 * 8 + mm * (int)hkv_l - 1) / (mm * (int)hkv_l)));
     NX_CUDA(b, malloc_tracked(m, &m->part, (size_t)MC * hkv_l * max_split * G * (D + 2)));
     NX_CUDA(b, malloc_tracked(m, &m->counters, (size_t)MC * hkv_l));
     NX_CUDA(b, cudaMemset(m->counters, 0, (size_t)MC * hkv_l * 4));
@@ -1440,6 +1517,7 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         a.seq_ids = m->seq_ids;
         a.kv_dim = kv_dim;
         a.nsplit = m->nsplit[mc];
+        if (a.bits_k > 0 && attention_pk_supported(a)) a.nsplit = m->nsplit_pk[mc];
         a.part = m->part;
         a.counters = m->counters;
         a.pdl = pdl;

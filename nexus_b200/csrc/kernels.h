@@ -117,6 +117,10 @@ struct AttnParams {
     int pdl;
 };
 cudaError_t launch_attention(const AttnParams &p, cudaStream_t st);
+// packed-cache attention on the tensor cores (kernels_attn_pk.cu): head_dim
+// 128, G in {1, 2, 4, 8}, bits in {2, 3, 4, 6, 8}; launch_attention routes there
+bool attention_pk_supported(const AttnParams &p);
+cudaError_t launch_attention_pk(const AttnParams &p, cudaStream_t st);
 
 // packed KV append (PackedKvBuffer::add, src/engine/mod.rs:209-232) for m tokens
 struct KvPackParams {

@@ -271,6 +271,7 @@ static cudaError_t launch_attn_g(const AttnParams &p, cudaStream_t st) {
 
 cudaError_t launch_attention(const AttnParams &p, cudaStream_t st) {
     if (p.hkv <= 0 || p.hq % p.hkv != 0 || p.nsplit < 1 || p.nsplit > 64) return cudaErrorInvalidValue;
+    if (p.bits_k > 0 && attention_pk_supported(p)) return launch_attention_pk(p, st);
     switch (p.head_dim) {
     case 32: return launch_attn_g<1>(p, st);
     case 64: return launch_attn_g<2>(p, st);

@@ -210,6 +210,25 @@ class CudaBackend:
                           m=num_q_heads, n=seq, k=head_dim, kv_heads=num_kv_heads, scale=scale))
         return out
 
+    def attention_packed(self, q: np.ndarray, keys: tuple, values: tuple, num_q_heads: int, num_kv_heads: int,
+                         head_dim: int, bits_k: int, bits_v: int, scale: float = 0.0) -> np.ndarray:
+        """Decode attention over packed caches; keys/values = (codes [seq][bpt] u8,
+        mins [seq] f32, scales [seq] f32) as PackedKvBuffer holds them."""
+        q = np.ascontiguousarray(q, np.float32)
+
+        def blob(kv):
+            data, mins, scales = kv
+            return np.concatenate([np.ascontiguousarray(data, np.uint8).ravel(),
+                                   np.ascontiguousarray(mins, np.float32).view(np.uint8),
+                                   np.ascontiguousarray(scales, np.float32).view(np.uint8)])
+        kb, vb = blob(keys), blob(values)
+        seq = np.asarray(keys[1]).size
+        out = np.empty(num_q_heads * head_dim, np.float32)
+        self.execute(L.Op(kind=L.OP_ATTENTION_PACKED, a=_ptr(q), b=_ptr(kb), c=_ptr(vb), out=_ptr(out),
+                          m=num_q_heads, n=seq, k=head_dim, kv_heads=num_kv_heads, scale=scale,
+                          format=bits_k | (bits_v << 8)))
+        return out
+
 
 class QWeight:
     """A quantized matrix resident on the device in the GEMV tile layout."""

@@ -5,6 +5,8 @@ identical, KV cache lengths equal.  The tiny configuration (4 layers,
 hidden 256, all Q4_K) runs in full: 128-token prompt (seed 1) + 64 greedy
 tokens.  The 8B shape is checked on a short prompt.
 """
+import os
+
 import numpy as np
 import pytest
 
@@ -128,6 +130,32 @@ def test_tiny_packed_kv(nb, oracle, tiny_path, bits):
     e.close()
     b.close()
     assert gen == refgen
+
+
+@pytest.mark.parametrize("bits", [(4, 4), (3, 2)])
+def test_head_dim_128_packed_kv(nb, oracle, bits):
+    """Packed KV on a head_dim-128 model (the tensor-core attention kernel):
+    a 140-token prefill in one step, then three decode steps."""
+    path = nb.model_path("tp_small")
+    b = nb.CudaBackend(device=0, kv_bits=bits)
+    e = nb.InferenceEngine(b)
+    e.load_model(path)
+    m = oracle.Model(path, kv_bits=bits, threads=os.cpu_count() or 1)
+    p = prompt(5, 140, 8192)
+    ref = m.prefill(p)
+    got, tok = e.prefill(p)
+    errs = [float(np.max(np.abs(got - ref)))]
+    assert tok == oracle.greedy(ref)
+    for i in range(3):
+        ref = m.decode(tok, len(p) + i)
+        got, tok2 = e.decode_with_cache(tok, len(p) + i)
+        errs.append(float(np.max(np.abs(got - ref))))
+        assert tok2 == oracle.greedy(ref)
+        tok = tok2
+    e.close()
+    b.close()
+    print(f"head_dim 128, packed kv {bits}: max |logit diff| = {max(errs):.3e}")
+    assert max(errs) < 2e-2, errs
 
 
 def test_kv_overflow_is_an_error_not_a_shift(nb, tiny_path):

@@ -229,6 +229,67 @@ def test_attention_op(backend, hq, hkv, d, seq):
     assert np.max(np.abs(out - ref)) < 1e-4
 
 
+def _packed_stream(oracle, bits, x):
+    """PackedKvBuffer of rows x [seq][kv_dim] (src/engine/mod.rs:209-232):
+    (codes, mins, scales) and the values the cache reads back (value_at)."""
+    seq, kv_dim = x.shape
+    pk = oracle.PackedKv(bits, kv_dim, seq)
+    for t in range(seq):
+        pk.add(t, x[t])
+    return pk.raw(seq), pk.get_all(seq).reshape(seq, kv_dim)
+
+
+def _attention_ref(q, kval, vval, hq, hkv, d):
+    g = hq // hkv
+    ref = np.zeros(hq * d)
+    for h in range(hq):
+        kh = kval[:, (h // g) * d:(h // g + 1) * d].astype(np.float64)
+        vh = vval[:, (h // g) * d:(h // g + 1) * d].astype(np.float64)
+        s = kh @ q[h * d:(h + 1) * d].astype(np.float64) / np.sqrt(d)
+        p = np.exp(s - s.max())
+        ref[h * d:(h + 1) * d] = (p / p.sum()) @ vh
+    return ref
+
+
+@pytest.mark.parametrize("hq,hkv,d,seq,bits", [
+    (32, 8, 128, 1, (4, 4)), (32, 8, 128, 577, (4, 4)), (32, 8, 128, 4133, (4, 4)),
+    (64, 8, 128, 300, (4, 4)), (8, 8, 128, 130, (4, 4)), (16, 8, 128, 70, (4, 4)),
+    (32, 8, 128, 515, (3, 2)), (32, 8, 128, 515, (3, 4)), (32, 8, 128, 515, (6, 6)),
+    (32, 8, 128, 515, (8, 8)), (32, 8, 128, 515, (2, 2)), (64, 8, 128, 260, (8, 4)),
+    (8, 4, 64, 200, (4, 4)), (8, 4, 32, 65, (3, 2)), (32, 8, 128, 100, (5, 7))])
+def test_attention_packed_op(backend, oracle, hq, hkv, d, seq, bits):
+    """Decode attention over packed K/V (head_dim 128 with bits 2/3/4/6/8 runs on
+    the tensor-core kernel, the rest on the per-element one) against float64
+    attention over the values the packed cache reads back."""
+    rng = np.random.default_rng(90 + seq + 7 * bits[0] + bits[1])
+    q = (rng.standard_normal(hq * d) * 2.0).astype(np.float32)
+    k = (rng.standard_normal((seq, hkv * d)) + 0.3).astype(np.float32)
+    v = rng.standard_normal((seq, hkv * d)).astype(np.float32)
+    kraw, kval = _packed_stream(oracle, bits[0], k)
+    vraw, vval = _packed_stream(oracle, bits[1], v)
+    out = backend.attention_packed(q, kraw, vraw, hq, hkv, d, bits[0], bits[1])
+    ref = _attention_ref(q, kval, vval, hq, hkv, d)
+    err = np.max(np.abs(out - ref))
+    assert err < 2e-4 * max(1.0, np.max(np.abs(ref))), err
+
+
+def test_attention_packed_extreme_scales(backend, oracle):
+    """Per-token scales spanning 2^-20 .. 2^10 and a constant token (range 0 ->
+    scale 1.0): the value weights stay in f16 range relative to their maximum."""
+    rng = np.random.default_rng(97)
+    hq, hkv, d, seq = 32, 8, 128, 300
+    q = rng.standard_normal(hq * d).astype(np.float32)
+    mag = np.exp2(rng.uniform(-20, 10, seq)).astype(np.float32)[:, None]
+    k = (rng.standard_normal((seq, hkv * d)) * 0.05).astype(np.float32)
+    v = (rng.standard_normal((seq, hkv * d)) * mag).astype(np.float32)
+    v[7] = 0.25
+    kraw, kval = _packed_stream(oracle, 4, k)
+    vraw, vval = _packed_stream(oracle, 4, v)
+    out = backend.attention_packed(q, kraw, vraw, hq, hkv, d, 4, 4)
+    ref = _attention_ref(q, kval, vval, hq, hkv, d)
+    assert np.max(np.abs(out - ref)) < 2e-4 * np.max(np.abs(ref))
+
+
 def test_dequantize_truncated_payload_is_an_error(backend, oracle, nb):
     q = oracle.quantize(oracle.Q4_K, np.ones(512, np.float32))
     with pytest.raises(nb.NexusError) as e:
