@@ -62,6 +62,32 @@ __device__ __forceinline__ int active_splits(int seq_len, int nsplit_grid) {
     return max(1, min(s, nsplit_grid));
 }
 
+// Completes NV partial sums spread over the warp with one transpose-reduce:
+// at each xor step a lane keeps the half of its values that its lane bit
+// selects and adds the partner's copy of that half (31 shuffles for 32
+// values instead of 160).  Afterwards value i is complete in lane i >> 1 as
+// element i & 1 (NV = 64), in lane i (NV = 32), or in lanes
+// i << s .. (i << s) + 2^s - 1 (NV = 32 >> s, all holding the same sum).
+template <int NV>
+__device__ __forceinline__ void transpose_reduce(float (&v)[NV], int lane) {
+#pragma unroll
+    for (int step = 0; step < 5; step++) {
+        const int o = 16 >> step;
+        const int n = NV >> step;  // values per lane before this step
+        if (n >= 2) {
+            const bool up = (lane & o) != 0;
+#pragma unroll
+            for (int i = 0; i < n / 2; i++) {
+                const float keep = up ? v[n / 2 + i] : v[i];
+                const float send = up ? v[i] : v[n / 2 + i];
+                v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+            }
+        } else {
+            v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+        }
+    }
+}
+
 template <int VEC, int G>
 __global__ void __launch_bounds__(kAttnWarps * 32) k_attn(AttnParams p) {
     constexpr int D = VEC * 32;
@@ -89,14 +115,27 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attn(AttnParams p) {
     if (split >= nsplit) return;
     const int per = (seq_len + nsplit - 1) / nsplit;
     const int t0 = split * per, t1 = min(seq_len, t0 + per);
-    float m[G], l[G], o[G][VEC];
+    // After the batch's dot products are reduced, lane `lane` holds R of its
+    // kBatch x G scores (token j, head g): index lane * R + r when there are
+    // 32 or more, else lane >> SH, repeated in 2^SH lanes of which the first
+    // ("lead") carries it.  Every lane keeps the running maximum of the
+    // head(s) it holds and its lead share of that head's softmax sum; the
+    // batch's weights and rescale factors meet in shared memory.
+    constexpr int NV = kBatch * G;
+    constexpr int R = NV >= 32 ? NV / 32 : 1;
+    constexpr int SH = NV >= 32 ? 0 : (NV == 16 ? 1 : NV == 8 ? 2 : NV == 4 ? 3 : 4);
+    __shared__ float sm_p[NW][kBatch][G], sm_c[NW][G];
+    const bool lead = (lane & ((1 << SH) - 1)) == 0;
+    float ml[R], ll[R], o[G][VEC];
 #pragma unroll
-    for (int g = 0; g < G; g++) {
-        m[g] = -INFINITY;
-        l[g] = 0.0f;
+    for (int r = 0; r < R; r++) {
+        ml[r] = -INFINITY;
+        ll[r] = 0.0f;
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++)
 #pragma unroll
         for (int i = 0; i < VEC; i++) o[g][i] = 0.0f;
-    }
 
     const bool packed = p.bits_k > 0;
     const int e0 = h * D + lane * VEC;
@@ -118,45 +157,70 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attn(AttnParams p) {
                                  p.bits_v, p.vp_min[mi], p.vp_scale[mi], vv[j]);
             }
         }
+        float pd[NV];
 #pragma unroll
-        for (int j = 0; j < kBatch; j++) {
-            if (base + j >= t1) break;
-            float dot[G];
+        for (int j = 0; j < kBatch; j++)
 #pragma unroll
             for (int g = 0; g < G; g++) {
                 float s = 0.0f;
 #pragma unroll
                 for (int i = 0; i < VEC; i++) s += qv[g][i] * kv[j][i];
-                dot[g] = s;
+                pd[j * G + g] = s;
             }
+        transpose_reduce<NV>(pd, lane);
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1)
+        for (int r = 0; r < R; r++) {
+            const int idx = NV >= 32 ? lane * R + r : lane >> SH;
+            const int j = idx / G, g = idx % G;
+            const float s = base + j < t1 ? pd[r] * p.scale : -INFINITY;
+            // the lanes of one head differ in lane bits 2..4 (token j)
+            float mx = s;
 #pragma unroll
-                for (int g = 0; g < G; g++) dot[g] += __shfl_xor_sync(0xffffffffu, dot[g], off);
-#pragma unroll
-            for (int g = 0; g < G; g++) {
-                const float s = dot[g] * p.scale;
-                const float mn = fmaxf(m[g], s);
-                const float corr = expf(m[g] - mn);
-                const float pe = expf(s - mn);
-                l[g] = l[g] * corr + pe;
-#pragma unroll
-                for (int i = 0; i < VEC; i++) o[g][i] = o[g][i] * corr + pe * vv[j][i];
-                m[g] = mn;
+            for (int off = 4; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float mn = fmaxf(ml[r], mx);  // finite: token base is valid
+            const float corr = expf(ml[r] - mn);
+            const float pe = expf(s - mn);
+            ml[r] = mn;
+            ll[r] = ll[r] * corr + (lead ? pe : 0.0f);
+            if (lead) {
+                sm_p[warp][j][g] = pe;
+                if (j == 0) sm_c[warp][g] = corr;
             }
         }
+        __syncwarp();
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            const float c = sm_c[warp][g];
+#pragma unroll
+            for (int i = 0; i < VEC; i++) o[g][i] *= c;
+        }
+#pragma unroll
+        for (int j = 0; j < kBatch; j++)
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                const float pe = sm_p[warp][j][g];
+#pragma unroll
+                for (int i = 0; i < VEC; i++) o[g][i] = fmaf(pe, vv[j][i], o[g][i]);
+            }
+        __syncwarp();
     }
 
     // merge the warps of this CTA
 #pragma unroll
-    for (int g = 0; g < G; g++) {
-        if (lane == 0) {
-            sm_m[warp][g] = m[g];
-            sm_l[warp][g] = l[g];
+    for (int r = 0; r < R; r++) {
+        float l = ll[r];
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+        const int idx = NV >= 32 ? lane * R + r : lane >> SH;
+        if (lead && idx < G) {
+            sm_m[warp][idx] = ml[r];
+            sm_l[warp][idx] = l;
         }
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++)
 #pragma unroll
         for (int i = 0; i < VEC; i++) sm_o[warp][g][lane * VEC + i] = o[g][i];
-    }
     __syncthreads();
     if (nsplit == 1) {
         // the whole context is this CTA's slice: normalize and write directly
