@@ -351,7 +351,7 @@ def run_workload_p(args):
     import nexus_b200 as nb
     n_req, gen = 64, args.steps
     path = nb.model_path("llama8b_q8", threads=cpu_threads())
-    ctx = np.random.default_rng(2).integers(1024, 8193, n_req)
+    ctx = np.random.default_rng(2).integers(args.p_ctx[0], args.p_ctx[1] + 1, n_req)
     be = nb.CudaBackend(device=0, kv_bits=(4, 4), max_batch=n_req, max_seq_len=int(ctx.max()) + gen + args.warmup + 8)
     eng = nb.InferenceEngine(be)
     eng.load_model(path)
@@ -382,11 +382,16 @@ def run_workload_p(args):
     torch.cuda.synchronize()
     dev_ms = 0.0
     t0 = time.perf_counter()
+    if args.profile_range:
+        torch.cuda.profiler.start()
     with ClockSampler(0) as clk:
         for _ in range(gen):
             step()
             dev_ms += eng.last_step_ms()
     wall = time.perf_counter() - t0
+    if args.profile_range:
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
     mean_ctx = float(ctx.mean()) + args.warmup + gen / 2
     kv_bytes = 2 * eng.info.num_layers * mean_ctx * (eng.info.num_kv_heads * eng.info.head_dim * 4 // 8 + 8) * n_req
     step_bytes = eng.info.weight_bytes + kv_bytes
@@ -394,7 +399,7 @@ def run_workload_p(args):
             "value": n_req * gen / (dev_ms / 1000.0), "unit": "tok/s", "n_gpus": 1, "steps": gen,
             "warmup": args.warmup, "ms_per_step": dev_ms / gen, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f16 tensor-core (exact Q8_0 hi/lo) + f32", "data": "synthetic",
-            "config": {"workload": "llama8b_q8, 64 requests, ctx U[1024,8192] seed 2, KV 4/4-bit packed, "
+            "config": {"workload": f"llama8b_q8, 64 requests, ctx U[{args.p_ctx[0]},{args.p_ctx[1]}] seed 2, KV 4/4-bit packed, "
                                    "16-token pages", "model": "llama8b_q8", "global_batch": n_req,
                        "mean_ctx": mean_ctx, "l2": "inputs larger than L2 (weights + KV per step)"},
             "e2e": {"value": n_req * gen / wall, "unit": "tok/s", "h2d_bytes_per_step": 28 * n_req,
@@ -482,6 +487,11 @@ def main():
                          "device-chained decode steps; prints a short JSON line")
     ap.add_argument("--workload", default="E", choices=["E", "P", "X"],
                     help="E: 8B Q4_K b=1 (+b=32) [default]; P: 8B Q8_0, packed KV, 64 requests; X: 70B shape, TP")
+    ap.add_argument("--p-ctx", nargs=2, type=int, default=[1024, 8192], metavar=("LO", "HI"),
+                    help="workload P context lengths, uniform in [LO, HI] (a smaller range gives a smaller ncu case)")
+    ap.add_argument("--profile-range", action="store_true",
+                    help="workload P: bracket the timed steps with cudaProfilerStart/Stop "
+                         "(for ncu --profile-from-start off)")
     ap.add_argument("--sweep", action="store_true", help="config S: quantized matvec/matmul sweep, one JSON line per case")
     ap.add_argument("--matvec", nargs=4, metavar=("FMT", "N", "K", "M"), help="one config-S case, three launches")
     args = ap.parse_args()

@@ -1,5 +1,7 @@
 // kernels_gemm.cu -- activation preparation and launch of the tcgen05 GEMM
 // (kernels_gemm.cuh) for batched decode and prefill.
+#include <algorithm>
+
 #include "kernels_gemm.cuh"
 
 namespace nx {
@@ -138,10 +140,21 @@ static int sm_count_cached() {
     return dev < 16 && sm_count[dev] ? sm_count[dev] : 148;
 }
 
+// Token tile of a GEMM: 16 or 32 tokens; 64 for the block formats (their
+// 64-token tile fits the shared memory and needs no per-super-block
+// epilogue) when the 128-row tiles alone cover the SMs.  Matrices with fewer
+// row tiles fill the machine by splitting K, and there the shorter units of
+// the 64-token tile measured slower than two 32-token passes.
+static int token_tile(int fmt, int m, int n) {
+    const bool min_term = fmt == 12 || fmt == 10;  // GemmFmt<fmt>::MIN
+    if (m <= 16) return 16;
+    if (m <= 32 || min_term || (n + 127) / 128 < sm_count_cached()) return 32;
+    return 64;
+}
+
 // Tiles and K split of one GEMM: the split minimises waves x (super-blocks
 // per unit + one for the pipeline fill).
-static GemmShape plan(int m, int n, int k) {
-    const int nt = m <= 16 ? 16 : 32;
+static GemmShape plan(int m, int n, int k, int nt) {
     GemmShape g;
     g.n_sb = k / 256;
     g.groups = (n + 31) / 32;
@@ -168,7 +181,7 @@ static GemmShape plan(int m, int n, int k) {
 template <int FMT, int NT, int EPI>
 static cudaError_t launch_nt_epi(const GemvParams &p, const GemmScratch &sc, cudaStream_t st) {
     using S = Smem<FMT, NT>;
-    GemmShape g = plan(p.m, p.n, p.k);
+    GemmShape g = plan(p.m, p.n, p.k, NT);
     const int sms = sm_count_cached();
     const long long units0 = (long long)g.n_tt * g.n_rt;
     if (g.nsplit > 1) {
@@ -206,7 +219,11 @@ static cudaError_t launch_nt(const GemvParams &p, const GemmScratch &sc, cudaStr
 
 template <int FMT>
 static cudaError_t launch_fmt(const GemvParams &p, const GemmScratch &sc, cudaStream_t st) {
-    return p.m <= 16 ? launch_nt<FMT, 16>(p, sc, st) : launch_nt<FMT, 32>(p, sc, st);
+    const int nt = token_tile(FMT, p.m, p.n);
+    if constexpr (!GemmFmt<FMT>::MIN) {
+        if (nt == 64) return launch_nt<FMT, 64>(p, sc, st);
+    }
+    return nt == 16 ? launch_nt<FMT, 16>(p, sc, st) : launch_nt<FMT, 32>(p, sc, st);
 }
 
 }  // namespace qg
@@ -214,13 +231,16 @@ static cudaError_t launch_fmt(const GemvParams &p, const GemmScratch &sc, cudaSt
 bool gemm_supported(int fmt) { return fmt == 12 || fmt == 8 || fmt == 10 || fmt == 2; }
 
 GemmScratchSize gemm_scratch_size(int m, int n, int k) {
-    const qg::GemmShape g = qg::plan(m, n, k);
-    const int nt = m <= 16 ? 16 : 32;
-    GemmScratchSize z;
-    z.bimg_bytes = (size_t)g.n_tt * g.n_sb * qg::bimg_sb_bytes(nt);
-    z.tok_scale_floats = (size_t)g.mpad;
-    z.part_floats = g.nsplit > 1 ? (size_t)g.nsplit * g.mpad * g.npad : 0;
-    z.counter_slots = (size_t)g.n_tt * g.n_rt;
+    // enough for either token tile a format may choose at this m
+    GemmScratchSize z = {};
+    for (int fmt : {12, 8}) {
+        const int nt = qg::token_tile(fmt, m, n);
+        const qg::GemmShape g = qg::plan(m, n, k, nt);
+        z.bimg_bytes = std::max(z.bimg_bytes, (size_t)g.n_tt * g.n_sb * qg::bimg_sb_bytes(nt));
+        z.tok_scale_floats = std::max(z.tok_scale_floats, (size_t)g.mpad);
+        z.part_floats = std::max(z.part_floats, g.nsplit > 1 ? (size_t)g.nsplit * g.mpad * g.npad : (size_t)0);
+        z.counter_slots = std::max(z.counter_slots, (size_t)g.n_tt * g.n_rt);
+    }
     return z;
 }
 

@@ -20,6 +20,9 @@
 // to 256, so the hi and lo halves of the tokens are stacked along N (one MMA
 // of N = 2*NT per K step) rather than issued as two MMAs.
 //
+// Token tiles: 16 or 32 tokens; the block formats (Q8_0, Q4_0: no min term,
+// no per-super-block epilogue scale) also run 64-token tiles (MMA N = 128),
+// so a 64-token batch dequantizes every weight tile once.
 // CTA roles (one CTA per SM, persistent over work units):
 //   warps 0-7  dequantize (warp w: row group w&3 of the 128-row tile, half
 //              w>>2 of each super-block) and run the epilogue (half w>>2 of
@@ -353,7 +356,7 @@ template <int FMT, int NT, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     k_qgemm(GemvParams p, GemmShape g, const uint8_t *__restrict__ bimg, const float *__restrict__ tok_scale) {
     using GF = GemmFmt<FMT>;
-    static_assert(NT == 16 || NT == 32, "token tile");
+    static_assert(NT == 16 || NT == 32 || (NT == 64 && !GF::MIN), "token tile");
     using S = Smem<FMT, NT>;
     using R = Raw<FMT>;
     constexpr int H = NT / 2;  // tokens per epilogue warp
@@ -552,24 +555,34 @@ __global__ void __launch_bounds__(kThreads, 1)
             bwait(&acc_full[ab], (nn >> 1) & 1, &abort_s, p.err);
             __syncwarp();
             tc_fence_after();
-            float dh[H], dl[H], eh[H], el[H];
             const uint32_t col = tmem + t_lane + ab * 4 * NT + half * H;
-            tmem_ld<H>(col, dh);
-            tmem_ld<H>(col + NT, dl);
             if constexpr (GF::MIN) {
+                float dh[H], dl[H], eh[H], el[H];
+                tmem_ld<H>(col, dh);
+                tmem_ld<H>(col + NT, dl);
                 tmem_ld<H>(col + 2 * NT, eh);
                 tmem_ld<H>(col + 3 * NT, el);
-            }
-            tmem_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[ab]);
-            if constexpr (GF::MIN) {
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[ab]);
 #pragma unroll
                 for (int t = 0; t < H; t++) acc[t] = fmaf(d, dh[t] + dl[t], fmaf(-dm, eh[t] + el[t], acc[t]));
             } else {
+                // hi and lo token columns, 16 at a time (H = 32 for the 64-token tile)
+                constexpr int HC = H < 16 ? H : 16;
 #pragma unroll
-                for (int t = 0; t < H; t++) acc[t] += dh[t] + dl[t];
+                for (int c0 = 0; c0 < H; c0 += HC) {
+                    float dh[HC], dl[HC];
+                    tmem_ld<HC>(col + c0, dh);
+                    tmem_ld<HC>(col + NT + c0, dl);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int t = 0; t < HC; t++) acc[c0 + t] += dh[t] + dl[t];
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[ab]);
             }
         };
         for (int u = blockIdx.x; u < n_units; u += gridDim.x) {

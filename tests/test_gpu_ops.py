@@ -103,7 +103,7 @@ def test_qmatvec_input_edge_cases(backend, oracle, nb):
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
-@pytest.mark.parametrize("m", [8, 16, 17, 64])
+@pytest.mark.parametrize("m", [8, 16, 17, 64, 100])
 @pytest.mark.parametrize("shape", [(4096, 4096), (1024, 4096), (4096, 14336)], ids=lambda s: f"{s[0]}x{s[1]}")
 def test_qgemm_batched(backend, oracle, nb, shape, m, fmt):
     """Batches of 8+ tokens run on the tcgen05 GEMM; tokens 0, m/2 and m-1
@@ -115,6 +115,23 @@ def test_qgemm_batched(backend, oracle, nb, shape, m, fmt):
     x = rng.standard_normal((m, k)).astype(np.float32)
     y = w.matvec(x)
     for t in sorted({0, m // 2, m - 1}):
+        ref = oracle.qmatvec(getattr(oracle, fmt), q, n, k, x[t], threads=16)
+        assert rel_err(y[t], ref) < REL_TOL, (t, rel_err(y[t], ref))
+    w.close()
+
+
+@pytest.mark.parametrize("fmt", ["Q8_0", "Q4_0"])
+@pytest.mark.parametrize("m", [33, 64, 130])
+def test_qgemm_wide_matrix_token_tile(backend, oracle, nb, m, fmt):
+    """Matrices whose 128-row tiles cover every SM run the block formats with
+    64-token tiles (m > 32); padded tokens in the last tile stay unused."""
+    n, k = 149 * 128 + 32, 512
+    rng = np.random.default_rng(63 + m)
+    q = oracle.quantize(getattr(oracle, fmt), weights(rng, n * k))
+    w = nb.QWeight(backend, getattr(nb, fmt), n, k, q)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    y = w.matvec(x)
+    for t in sorted({0, 31, 32, m // 2, m - 1}):
         ref = oracle.qmatvec(getattr(oracle, fmt), q, n, k, x[t], threads=16)
         assert rel_err(y[t], ref) < REL_TOL, (t, rel_err(y[t], ref))
     w.close()
