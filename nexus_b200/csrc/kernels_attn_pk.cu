@@ -29,8 +29,10 @@
 // tokens (32 for 6- and 8-bit codes) of one KV head at a time and all G query
 // heads sharing it; lane (g, c) = (lane / 4, lane % 4) holds, per 16-token
 // block, tokens g and g + 8 of head c's scores and dims 16g .. 16g+15 of head
-// c's output.  Warps and slices merge as in the float kernel (partials + the
-// last slice to finish, deterministic order).
+// c's output.  Tiles reach shared memory by cp.async into two stages per warp,
+// the next tile's copies issued before the current tile's math.  Warps and
+// slices merge as in the float kernel (partials + the last slice to finish,
+// deterministic order).
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <math.h>
@@ -148,44 +150,36 @@ __device__ __forceinline__ constexpr float vfactor(int d) {
     return BV == 4 ? ((d & 1) ? 16.0f : 1.0f) : BV == 2 ? (float)(1 << (2 * (d & 3))) : 1.0f;
 }
 
-// loads of NWORDS 32-bit words from an address aligned to ALIGN bytes
-template <int NWORDS, int ALIGN>
-__device__ __forceinline__ void load_words(const uint8_t *p, uint32_t (&w)[NWORDS]) {
-    if constexpr (ALIGN % 16 == 0 && NWORDS % 4 == 0) {
-#pragma unroll
-        for (int i = 0; i < NWORDS / 4; i++) {
-            const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(p) + i);
-            w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
-        }
-    } else if constexpr (ALIGN % 8 == 0 && NWORDS % 2 == 0) {
-#pragma unroll
-        for (int i = 0; i < NWORDS / 2; i++) {
-            const uint2 v = __ldcg(reinterpret_cast<const uint2 *>(p) + i);
-            w[2 * i] = v.x; w[2 * i + 1] = v.y;
-        }
-    } else {
-#pragma unroll
-        for (int i = 0; i < NWORDS; i++) w[i] = __ldcg(reinterpret_cast<const uint32_t *>(p) + i);
-    }
-}
-
-// the lane's V block: 2*BV bytes at a 2*BV-aligned offset
-template <int BV>
-__device__ __forceinline__ void load_vblock(const uint8_t *p, uint32_t (&w)[vwords<BV>()]) {
-    if constexpr (BV % 2 == 0) {
-        load_words<BV / 2, 2 * BV>(p, w);
-    } else {
-        const uint16_t *h = reinterpret_cast<const uint16_t *>(p);
-#pragma unroll
-        for (int i = 0; i < vwords<BV>(); i++) {
-            const uint32_t lo = __ldcg(h + 2 * i);
-            const uint32_t hi = 2 * i + 1 < BV ? (uint32_t)__ldcg(h + 2 * i + 1) : 0u;
-            w[i] = lo | (hi << 16);
-        }
-    }
-}
-
 __device__ __forceinline__ float pow2f(int e) { return __int_as_float((127 + e) << 23); }
+
+// asynchronous global -> shared copies (no registers held while in flight)
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// Shared-memory row of tile token tt in the V buffer.  4-bit rows (64 B) are
+// permuted so that the four tokens 2c+r (c = 0..3) one fragment load reads
+// fall in both halves of the banks; 8-bit rows (128 B) XOR their 16-byte
+// units with the token instead.
+template <int BV>
+__device__ __forceinline__ int vrow(int tt) { return BV == 4 ? tt ^ ((tt >> 1) & 1) : tt; }
+template <int BV>
+__device__ __forceinline__ int vunit(int tt, int u) { return BV == 8 ? u ^ (tt & 7) : u; }
+
+// Per-warp tile buffers: K rows, V rows (16*bits bytes each), and the four
+// per-token floats (kmin, kscale, vmin, vscale); two stages.
+template <int BK, int BV, int TT>
+struct PkTile {
+    static constexpr int K = 0;
+    static constexpr int V = K + TT * 16 * BK;
+    static constexpr int MS = V + TT * 16 * BV;
+    static constexpr int BYTES = MS + TT * 16;
+};
 
 // signed 7-bit digit k (0 = lowest) of qi = d2*2^14 + d1*2^7 + d0
 __device__ __forceinline__ int qdigit(int qi, int k) {
@@ -212,7 +206,6 @@ __global__ void __launch_bounds__(kPkWarps * 32) k_attn_pk(AttnParams p) {
     __shared__ float sQa[G], sQb[G];
     __shared__ int sE[G];
     __shared__ __align__(16) uint32_t sP[NW][NG][TT][4];  // per token: 8 f16 columns (head hi, lo)
-    __shared__ __align__(16) float4 sMS[NW][TT];          // kmin, kscale, vmin, vscale
     __shared__ float sO[NW][G][D];
     __shared__ float sM[NW][G], sL[NW][G];
     __shared__ float sw[64][G], sls[64][G], sMg[G], sLg[G];
@@ -307,41 +300,89 @@ __global__ void __launch_bounds__(kPkWarps * 32) k_attn_pk(AttnParams p) {
             for (int r = 0; r < 4; r++) acc[hg][i][r] = 0.0f;
     }
     const size_t mi0 = (size_t)sid * p.pk_seq_tokens;
-    const uint8_t *kbase = p.kp_data + (size_t)sid * p.pk_seq_stride_k + (size_t)h * (16 * BK) + (size_t)c * (4 * BK);
-    const uint8_t *vbase = p.vp_data + (size_t)sid * p.pk_seq_stride_v + (size_t)h * (16 * BV) + (size_t)gq * (2 * BV);
-    for (int base = t0 + warp * TT; base < t1; base += NW * TT) {
-        // issue every load of the tile: K (tokens base+16mt+gq, +8), V (tokens
-        // base+16kc+2c+{0,1,8,9}), and the per-token min/scale into smem
+    const uint8_t *kseq = p.kp_data + (size_t)sid * p.pk_seq_stride_k + (size_t)h * (16 * BK);
+    const uint8_t *vseq = p.vp_data + (size_t)sid * p.pk_seq_stride_v + (size_t)h * (16 * BV);
+    using TL = PkTile<BK, BV, TT>;
+    extern __shared__ __align__(16) uint8_t pk_dyn[];
+    uint8_t *wbuf = pk_dyn + (size_t)warp * 2 * TL::BYTES;
+    // copies of the tile at `base` into stage st: the KV head's row segment of
+    // every token (tokens past the slice repeat its last one) and min/scale
+    auto issue = [&](int base, int st) {
+        uint8_t *b = wbuf + st * TL::BYTES;
+#pragma unroll
+        for (int i = 0; i < TT * BK / 32; i++) {
+            const int ch = lane + 32 * i, tt = ch / BK, part = ch % BK;
+            const int tok = min(base + tt, t1 - 1);
+            cp_async16(b + TL::K + tt * 16 * BK + part * 16, kseq + (size_t)tok * p.pk_bpt_k + part * 16);
+        }
+#pragma unroll
+        for (int i = 0; i < TT * BV / 32; i++) {
+            const int ch = lane + 32 * i, tt = ch / BV, part = ch % BV;
+            const int tok = min(base + tt, t1 - 1);
+            cp_async16(b + TL::V + vrow<BV>(tt) * 16 * BV + vunit<BV>(tt, part) * 16,
+                       vseq + (size_t)tok * p.pk_bpt_v + part * 16);
+        }
+#pragma unroll
+        for (int i = 0; i < TT / 32; i++) {
+            const int tt = lane + 32 * i, tok = min(base + tt, t1 - 1);
+            float *ms = reinterpret_cast<float *>(b + TL::MS) + 4 * tt;
+            cp_async4(ms + 0, p.kp_min + mi0 + tok);
+            cp_async4(ms + 1, p.kp_scale + mi0 + tok);
+            cp_async4(ms + 2, p.vp_min + mi0 + tok);
+            cp_async4(ms + 3, p.vp_scale + mi0 + tok);
+        }
+    };
+    int base = t0 + warp * TT, st = 0;
+    if (base < t1) issue(base, 0);
+    cp_async_commit();
+    for (; base < t1; base += NW * TT, st ^= 1) {
+        // the next tile's copies go out before this tile's math
+        if (base + NW * TT < t1) issue(base + NW * TT, st ^ 1);
+        cp_async_commit();
+        cp_async_wait1();
+        __syncwarp();
+        const uint8_t *tb = wbuf + st * TL::BYTES;
+        const float4 *sMS = reinterpret_cast<const float4 *>(tb + TL::MS);
         uint32_t wk[MT][2][BK];
         uint32_t wv[MT][4][NVW];
 #pragma unroll
         for (int mt = 0; mt < MT; mt++)
 #pragma unroll
             for (int r = 0; r < 2; r++) {
-                const int tok = min(base + 16 * mt + gq + 8 * r, t1 - 1);
-                load_words<BK, (4 * BK) % 16 == 0 ? 16 : (4 * BK) % 8 == 0 ? 8 : 4>(kbase + (size_t)tok * p.pk_bpt_k,
-                                                                                    wk[mt][r]);
+                const uint32_t *src = reinterpret_cast<const uint32_t *>(tb + TL::K + (16 * mt + gq + 8 * r) * 16 * BK +
+                                                                         c * 4 * BK);
+#pragma unroll
+                for (int i = 0; i < BK; i++) wk[mt][r][i] = src[i];
             }
 #pragma unroll
         for (int kc = 0; kc < MT; kc++)
 #pragma unroll
             for (int r = 0; r < 4; r++) {
-                const int tok = min(base + 16 * kc + 2 * c + (r & 1) + 8 * (r >> 1), t1 - 1);
-                load_vblock<BV>(vbase + (size_t)tok * p.pk_bpt_v, wv[kc][r]);
-            }
+                const int tt = 16 * kc + 2 * c + (r & 1) + 8 * (r >> 1);
+                const int byte = gq * 2 * BV;  // the lane's 2*BV bytes inside the row
+                const uint8_t *row = tb + TL::V + vrow<BV>(tt) * 16 * BV;
+                if constexpr (BV == 8) {
+                    const uint4 v = *reinterpret_cast<const uint4 *>(row + vunit<BV>(tt, gq) * 16);
+                    wv[kc][r][0] = v.x; wv[kc][r][1] = v.y; wv[kc][r][2] = v.z; wv[kc][r][3] = v.w;
+                } else if constexpr (BV == 4) {
+                    const uint2 v = *reinterpret_cast<const uint2 *>(row + byte);
+                    wv[kc][r][0] = v.x; wv[kc][r][1] = v.y;
+                } else if constexpr (BV % 2 == 0) {
 #pragma unroll
-        for (int i = 0; i < TT / 32; i++) {
-            const int tok = min(base + lane + 32 * i, t1 - 1);
-            sMS[warp][lane + 32 * i] = make_float4(__ldcg(p.kp_min + mi0 + tok), __ldcg(p.kp_scale + mi0 + tok),
-                                                   __ldcg(p.vp_min + mi0 + tok), __ldcg(p.vp_scale + mi0 + tok));
-        }
-        __syncwarp();
+                    for (int i = 0; i < NVW; i++) wv[kc][r][i] = reinterpret_cast<const uint32_t *>(row + byte)[i];
+                } else {
+                    const uint16_t *hp = reinterpret_cast<const uint16_t *>(row + byte);
+#pragma unroll
+                    for (int i = 0; i < NVW; i++)
+                        wv[kc][r][i] = (uint32_t)hp[2 * i] | (2 * i + 1 < BV ? (uint32_t)hp[2 * i + 1] << 16 : 0u);
+                }
+            }
 
         // scores: exact integer q . codes per (token, head)
         float s2[NG][MT][2], u2[NG][MT][2];
 #pragma unroll
         for (int mt = 0; mt < MT; mt++) {
-            const float4 ms0 = sMS[warp][16 * mt + gq], ms1 = sMS[warp][16 * mt + gq + 8];
+            const float4 ms0 = sMS[16 * mt + gq], ms1 = sMS[16 * mt + gq + 8];
 #pragma unroll
             for (int hg = 0; hg < NG; hg++) {
                 int ck[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
@@ -400,7 +441,7 @@ __global__ void __launch_bounds__(kPkWarps * 32) k_attn_pk(AttnParams p) {
                     const int tt = 16 * mt + gq + 8 * r;
                     const float pe = exp2f(s2[hg][mt][r] - ms_);
                     L[hg] += pe;
-                    MN[hg] = fmaf(pe, sMS[warp][tt].z, MN[hg]);
+                    MN[hg] = fmaf(pe, sMS[tt].z, MN[hg]);
                     const float P = exp2f(u2[hg][mt][r] - mps);
                     const __half hi = __float2half_rn(P);
                     const __half lo = __float2half_rn(P - __half2float(hi));
@@ -533,16 +574,22 @@ __global__ void __launch_bounds__(kPkWarps * 32) k_attn_pk(AttnParams p) {
 
 template <int BK, int BV, int NG>
 cudaError_t launch_pk_t(const AttnParams &p, cudaStream_t st) {
+    constexpr int TT = (BK > 4 || BV > 4) ? 32 : 64;
+    constexpr int smem = kPkWarps * 2 * PkTile<BK, BV, TT>::BYTES;
+    auto fn = k_attn_pk<BK, BV, NG>;
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.hkv, p.nsplit, p.m);
     cfg.blockDim = dim3(kPkWarps * 32);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = p.pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, k_attn_pk<BK, BV, NG>, p);
+    return cudaLaunchKernelEx(&cfg, fn, p);
 }
 
 template <int BK, int BV>
