@@ -89,7 +89,7 @@ __device__ __forceinline__ void transpose_reduce(float (&v)[NV], int lane) {
 }
 
 template <int VEC, int G>
-__global__ void __launch_bounds__(kAttnWarps * 32) k_attn(AttnParams p) {
+__global__ void __launch_bounds__(kAttnWarps * 32, G <= 4 ? 2 : 1) k_attn(AttnParams p) {
     constexpr int D = VEC * 32;
     constexpr int NW = kAttnWarps;
     const int h = blockIdx.x, split = blockIdx.y, t = blockIdx.z;

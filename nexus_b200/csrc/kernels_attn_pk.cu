@@ -192,9 +192,9 @@ __device__ __forceinline__ int qdigit(int qi, int k) {
 }
 
 template <int BK, int BV, int NG>
-__global__ void __launch_bounds__(kPkWarps * 32) k_attn_pk(AttnParams p) {
+__global__ void __launch_bounds__(kPkWarps * 32, NG == 1 ? 4 : 2) k_attn_pk(AttnParams p) {
     constexpr int D = kPkD, NW = kPkWarps, G = 4 * NG;  // G: heads per KV head, padded
-    constexpr int MT = (BK > 4 || BV > 4) ? 2 : 4;       // 16-token blocks per tile
+    constexpr int MT = 2;                                // 16-token blocks per tile
     constexpr int TT = 16 * MT;
     constexpr int NVW = vwords<BV>();
     const int h = blockIdx.x, split = blockIdx.y, t = blockIdx.z;
@@ -574,7 +574,7 @@ __global__ void __launch_bounds__(kPkWarps * 32) k_attn_pk(AttnParams p) {
 
 template <int BK, int BV, int NG>
 cudaError_t launch_pk_t(const AttnParams &p, cudaStream_t st) {
-    constexpr int TT = (BK > 4 || BV > 4) ? 32 : 64;
+    constexpr int TT = 32;
     constexpr int smem = kPkWarps * 2 * PkTile<BK, BV, TT>::BYTES;
     auto fn = k_attn_pk<BK, BV, NG>;
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

@@ -18,25 +18,36 @@ __device__ __forceinline__ void q4k_kpos(int e, int &quarter, int &pos) {
     pos = hi * 32 + 4 * i + pw;
 }
 
-// One CTA per (token, group of 4 super-blocks): optional RMSNorm
-// ((x*rstd)*w, src/kernel/mod.rs:199-209), a power-of-two scale per token
-// keeping |x| < 2^10 (so the 32-element sub-block sums stay below 2^15, well
-// inside f16 range), the f16 hi/lo split, and the sub-block sums.  Image rows
-// per quarter: tokens' hi halves (rows 0..NT-1), then lo halves (NT..2NT-1).
+// One 1024-thread CTA per token: optional RMSNorm ((x*rstd)*w,
+// src/kernel/mod.rs:199-209), a power-of-two scale per token keeping
+// |x| < 2^10 (so the 32-element sub-block sums stay below 2^15, well inside
+// f16 range), the f16 hi/lo split, and the sub-block sums.  The row is read
+// once for its statistics; four groups of 256 threads then take one
+// super-block each at a time.  Image rows per quarter: tokens' hi halves
+// (rows 0..NT-1), then lo halves (NT..2NT-1).
+constexpr int kPrepThreads = 1024;
 template <int FMT, int NT>
-__global__ void __launch_bounds__(256) k_gemm_prep(const float *__restrict__ x, int x_stride,
-                                                   const float *__restrict__ norm_w, float eps, int m, int k,
-                                                   uint8_t *__restrict__ bimg, float *__restrict__ tok_scale) {
+__global__ void __launch_bounds__(kPrepThreads) k_gemm_prep(const float *__restrict__ x, int x_stride,
+                                                            const float *__restrict__ norm_w, float eps, int m, int k,
+                                                            uint8_t *__restrict__ bimg, float *__restrict__ tok_scale,
+                                                            int pdl) {
+    if (pdl) {
+        // the GEMM that follows may start its weight stream now; x is final
+        // (and the previous GEMM has finished reading the image) after the wait
+        pdl_launch_dependents();
+        pdl_wait();
+    }
+    constexpr int NWP = kPrepThreads / 32;
     const int tok = blockIdx.x, tt = tok / NT, n = tok % NT;
     const int n_sb = k / 256;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    __shared__ float red_s[8], red_m[8];
+    const int lane = threadIdx.x & 31;
+    __shared__ float red_s[NWP], red_m[NWP];
     __shared__ float rstd_s, inv_s;
     const bool valid = tok < m;
     const float *xr = x + (size_t)tok * x_stride;
     if (valid) {
         float ss = 0.0f, mx = 0.0f;
-        for (int i = tid; i < k; i += 256) {
+        for (int i = threadIdx.x; i < k; i += kPrepThreads) {
             const float v = xr[i];
             ss += v * v;
             mx = fmaxf(mx, fabsf(norm_w ? v * norm_w[i] : v));
@@ -44,13 +55,13 @@ __global__ void __launch_bounds__(256) k_gemm_prep(const float *__restrict__ x, 
         ss = warp_sum(ss);
         mx = warp_max(mx);
         if (lane == 0) {
-            red_s[warp] = ss;
-            red_m[warp] = mx;
+            red_s[threadIdx.x >> 5] = ss;
+            red_m[threadIdx.x >> 5] = mx;
         }
         __syncthreads();
-        if (tid == 0) {
+        if (threadIdx.x == 0) {
             float s = 0.0f, M = 0.0f;
-            for (int w = 0; w < 8; w++) {
+            for (int w = 0; w < NWP; w++) {
                 s += red_s[w];
                 M = fmaxf(M, red_m[w]);
             }
@@ -62,13 +73,14 @@ __global__ void __launch_bounds__(256) k_gemm_prep(const float *__restrict__ x, 
             const float inv = top > 0.0f && isfinite(top) ? ldexpf(1.0f, 10 - e2) : 1.0f;
             rstd_s = rstd;
             inv_s = inv;
-            if (blockIdx.y == 0) tok_scale[tok] = 1.0f / inv;
+            tok_scale[tok] = 1.0f / inv;
         }
         __syncthreads();
     }
     const float rstd = valid ? rstd_s : 1.0f, inv = valid ? inv_s : 1.0f;
-    const int sb_end = min(n_sb, (int)(blockIdx.y + 1) * 4);
-    for (int s = blockIdx.y * 4; s < sb_end; s++) {
+    // thread tid of a 256-thread group handles element tid of its super-block
+    const int tid = threadIdx.x & 255, warp = tid >> 5;
+    for (int s = threadIdx.x >> 8; s < n_sb; s += kPrepThreads / 256) {
         float v = 0.0f;
         if (valid) {
             v = xr[s * 256 + tid];
@@ -192,17 +204,34 @@ static cudaError_t launch_nt_epi(const GemvParams &p, const GemmScratch &sc, cud
     const size_t need = (size_t)g.n_tt * g.n_sb * bimg_sb_bytes(NT);
     if (!sc.bimg || need > sc.bimg_bytes || !sc.tok_scale || (size_t)g.mpad > sc.tok_scale_floats)
         return cudaErrorInvalidValue;
-    dim3 pg(g.mpad, (g.n_sb + 3) / 4);
-    k_gemm_prep<FMT, NT><<<pg, 256, 0, st>>>(p.x, p.x_stride, p.norm_w, p.eps, p.m, p.k, sc.bimg, sc.tok_scale);
-    cudaError_t e = cudaGetLastError();
+    dim3 pg(g.mpad);
+    // programmatic dependent launch: the prep waits for the previous kernel;
+    // the GEMM allocates TMEM and streams weights during the prep and waits
+    // for it before reading the image or writing results
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t pc = {};
+    pc.gridDim = pg;
+    pc.blockDim = dim3(kPrepThreads);
+    pc.stream = st;
+    pc.attrs = attr;
+    pc.numAttrs = p.pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&pc, k_gemm_prep<FMT, NT>, p.x, p.x_stride, p.norm_w, p.eps, p.m, p.k, sc.bimg,
+                                       sc.tok_scale, p.pdl);
     if (e != cudaSuccess) return e;
     auto fn = k_qgemm<FMT, NT, EPI>;
     e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
     if (e != cudaSuccess) return e;
     const long long units = units0 * g.nsplit;
-    const int grid = (int)(units < sms ? units : sms);
-    fn<<<grid, kThreads, S::TOTAL, st>>>(p, g, sc.bimg, sc.tok_scale);
-    return cudaGetLastError();
+    cudaLaunchConfig_t gc = {};
+    gc.gridDim = dim3((unsigned)(units < sms ? units : sms));
+    gc.blockDim = dim3(kThreads);
+    gc.dynamicSmemBytes = S::TOTAL;
+    gc.stream = st;
+    gc.attrs = attr;
+    gc.numAttrs = p.pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&gc, fn, p, g, (const uint8_t *)sc.bimg, (const float *)sc.tok_scale);
 }
 
 template <int FMT, int NT>

@@ -445,6 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 9) {
         // ---- prepared activations: one quarter per slot, sub-block sums per super-block ----
+        if (p.pdl) pdl_wait();  // the image is the previous kernel's output
         unsigned n = 0, c = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
@@ -493,17 +494,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr uint32_t idesc = umma_idesc<2 * NT>();
         const uint32_t a0 = smem_u32(smem + S::A), b0 = smem_u32(smem + S::B);
         const uint32_t amin0 = smem_u32(smem + S::AMIN), bmin0 = smem_u32(smem + S::BMIN);
-        unsigned n = 0, c = 0;
+        unsigned n = 0, c = 0, nu = 0;
         bool ok = true;
-        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, nu++) {
             int tt, rt, ks, s0, s1;
             unit_coords(g, u, tt, rt, ks, s0, s1);
-            for (int s = s0; s < s1 && ok; s++, n++) {
-                const int ab = n & 1;
-                const uint32_t dcol = tmem + ab * 4 * NT, ecol = dcol + 2 * NT;
-                ok = __all_sync(0xffffffffu, bwait(&acc_empty[ab], ((n >> 1) & 1) ^ 1, &abort_s, p.err));
+            if constexpr (!GF::MIN) {
+                // block formats: one accumulator per work unit
+                const int ab = nu & 1;
+                ok = __all_sync(0xffffffffu, bwait(&acc_empty[ab], ((nu >> 1) & 1) ^ 1, &abort_s, p.err));
                 if (!ok) break;
                 tc_fence_after();
+            }
+            for (int s = s0; s < s1 && ok; s++, n++) {
+                const int ab = GF::MIN ? (int)(n & 1) : (int)(nu & 1);
+                const uint32_t dcol = tmem + ab * 4 * NT, ecol = dcol + 2 * NT;
+                if constexpr (GF::MIN) {
+                    ok = __all_sync(0xffffffffu, bwait(&acc_empty[ab], ((n >> 1) & 1) ^ 1, &abort_s, p.err));
+                    if (!ok) break;
+                    tc_fence_after();
+                }
                 for (int q = 0; q < kQuarters; q++, c++) {
                     const int as = c % kASlots, bs = as;
                     ok = __all_sync(0xffffffffu, bwait(&st_full[as], (c / kASlots) & 1, &abort_s, p.err));
@@ -517,7 +527,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int am = 0; am < GF::A_MATS; am++) {
                             const uint64_t ad =
                                 umma_desc(a0 + as * S::A_BYTES + am * S::A_MAT + kk * 2 * 2048, 2048, 128);
-                            umma_f16_w(dcol, ad, bd, idesc, (q | kk | am) != 0);
+                            umma_f16_w(dcol, ad, bd, idesc, (q | kk | am) != 0 || (!GF::MIN && s != s0));
                         }
                     }
                     umma_commit_w(&st_empty[as]);
@@ -532,8 +542,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         umma_commit_w(&mn_empty[ms]);
                     }
                 }
-                if (ok) umma_commit_w(&acc_full[ab]);
+                if (GF::MIN && ok) umma_commit_w(&acc_full[ab]);
             }
+            if (!GF::MIN && ok) umma_commit_w(&acc_full[nu & 1]);
         }
         // all MMAs issued so far have completed before TMEM is released
         umma_commit_w(&mma_done);
@@ -550,42 +561,104 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t t_lane = (uint32_t)(32 * rg) << 16;
         unsigned n = 0;
         float pd = 0.0f, pdm = 0.0f;  // scales of the previous super-block
+        // super-block formats: fold one super-block's D and E into acc with its scales
         auto epilogue_sb = [&](unsigned nn, float d, float dm, float (&acc)[H]) {
+            if constexpr (!GF::MIN) return;
             const int ab = nn & 1;
             bwait(&acc_full[ab], (nn >> 1) & 1, &abort_s, p.err);
             __syncwarp();
             tc_fence_after();
             const uint32_t col = tmem + t_lane + ab * 4 * NT + half * H;
-            if constexpr (GF::MIN) {
-                float dh[H], dl[H], eh[H], el[H];
-                tmem_ld<H>(col, dh);
-                tmem_ld<H>(col + NT, dl);
-                tmem_ld<H>(col + 2 * NT, eh);
-                tmem_ld<H>(col + 3 * NT, el);
+            constexpr int HM = GF::MIN ? H : 8;  // (block formats never get here)
+            float dh[HM], dl[HM], eh[HM], el[HM];
+            tmem_ld<HM>(col, dh);
+            tmem_ld<HM>(col + NT, dl);
+            tmem_ld<HM>(col + 2 * NT, eh);
+            tmem_ld<HM>(col + 3 * NT, el);
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[ab]);
+#pragma unroll
+            for (int t = 0; t < HM; t++) acc[t] = fmaf(d, dh[t] + dl[t], fmaf(-dm, eh[t] + el[t], acc[t]));
+        };
+        // block formats: the accumulator of work unit nu (all its super-blocks)
+        auto unit_acc = [&](unsigned nu, float (&acc)[H]) {
+            const int ab = nu & 1;
+            bwait(&acc_full[ab], (nu >> 1) & 1, &abort_s, p.err);
+            __syncwarp();
+            tc_fence_after();
+            const uint32_t col = tmem + t_lane + ab * 4 * NT + half * H;
+            constexpr int HC = H < 16 ? H : 16;
+#pragma unroll
+            for (int c0 = 0; c0 < H; c0 += HC) {
+                float dh[HC], dl[HC];
+                tmem_ld<HC>(col + c0, dh);
+                tmem_ld<HC>(col + NT + c0, dl);
                 tmem_wait_ld();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[ab]);
 #pragma unroll
-                for (int t = 0; t < H; t++) acc[t] = fmaf(d, dh[t] + dl[t], fmaf(-dm, eh[t] + el[t], acc[t]));
-            } else {
-                // hi and lo token columns, 16 at a time (H = 32 for the 64-token tile)
-                constexpr int HC = H < 16 ? H : 16;
+                for (int t = 0; t < HC; t++) acc[c0 + t] = dh[t] + dl[t];
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[ab]);
+        };
+        // results of one work unit: the fused epilogue, or this split's partial
+        // sums (the last split of the tile adds them in split order)
+        bool waited = false;
+        auto unit_output = [&](int tt, int rt, int ks, const float (&acc)[H]) {
+            if (p.pdl && !waited) {
+                pdl_wait();  // token scales, residuals and outputs follow the previous kernels
+                waited = true;
+            }
+            const int grp = 4 * rt + rg;
+            const int tok0 = tt * NT + half * H;
+            if (g.nsplit == 1) {
+                if (grp < g.groups) {
 #pragma unroll
-                for (int c0 = 0; c0 < H; c0 += HC) {
-                    float dh[HC], dl[HC];
-                    tmem_ld<HC>(col + c0, dh);
-                    tmem_ld<HC>(col + NT + c0, dl);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int t = 0; t < HC; t++) acc[c0 + t] += dh[t] + dl[t];
+                    for (int t = 0; t < H; t++)
+                        if (tok0 + t < p.m) gemv_epilogue<EPI>(p, grp, tok0 + t, lane, acc[t] * tok_scale[tok0 + t]);
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[ab]);
+            } else {
+                float *part = p.part + ((size_t)ks * g.mpad + tok0) * g.npad + 128 * rt + r;
+#pragma unroll
+                for (int t = 0; t < H; t++) __stcg(part + (size_t)t * g.npad, acc[t]);
+                __threadfence();
+                asm volatile("bar.sync 1, %0;" ::"r"(kDqWarps * 32) : "memory");
+                if (threadIdx.x == 0) {
+                    const unsigned tile = (unsigned)(tt * g.n_rt + rt);
+                    last_s = atomicAdd(&p.counters[tile], 1u) == (unsigned)(g.nsplit - 1);
+                    if (last_s) p.counters[tile] = 0;
+                }
+                asm volatile("bar.sync 1, %0;" ::"r"(kDqWarps * 32) : "memory");
+                if (last_s) {
+                    __threadfence();
+                    if (grp < g.groups) {
+                        const float *pp = p.part + (size_t)tok0 * g.npad + 128 * rt + r;
+#pragma unroll
+                        for (int t = 0; t < H; t++) {
+                            float tot = 0.0f;
+                            for (int k2 = 0; k2 < g.nsplit; k2++)
+                                tot += __ldcg(pp + ((size_t)k2 * g.mpad + t) * g.npad);
+                            if (tok0 + t < p.m) gemv_epilogue<EPI>(p, grp, tok0 + t, lane, tot * tok_scale[tok0 + t]);
+                        }
+                    }
+                }
             }
         };
-        for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+        // block formats finish a unit after dequantizing the next unit's first
+        // super-block, so the MMAs of the unit's tail overlap that work
+        bool pend = false;
+        int p_tt = 0, p_rt = 0, p_ks = 0;
+        unsigned p_nu = 0, nu = 0;
+        auto finish_pending = [&]() {
+            if (!pend) return;
+            float acc[H];
+            unit_acc(p_nu, acc);
+            unit_output(p_tt, p_rt, p_ks, acc);
+            pend = false;
+        };
+        for (int u = blockIdx.x; u < n_units; u += gridDim.x, nu++) {
             int tt, rt, ks, s0, s1;
             unit_coords(g, u, tt, rt, ks, s0, s1);
             float acc[H];
@@ -753,48 +826,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (lane == 0) mbar_arrive(&st_full[as]);
                     }
                 }
-                if (s > s0) epilogue_sb(n - 1, pd, pdm, acc);
-                pd = d;
-                pdm = dm;
+                if constexpr (GF::MIN) {
+                    if (s > s0) epilogue_sb(n - 1, pd, pdm, acc);
+                    pd = d;
+                    pdm = dm;
+                } else if (s == s0) {
+                    finish_pending();
+                }
             }
-            epilogue_sb(n - 1, pd, pdm, acc);
-
-            // ---- unit output ----
-            const int grp = 4 * rt + rg;
-            const int tok0 = tt * NT + half * H;
-            if (g.nsplit == 1) {
-                if (grp < g.groups) {
-#pragma unroll
-                    for (int t = 0; t < H; t++)
-                        if (tok0 + t < p.m) gemv_epilogue<EPI>(p, grp, tok0 + t, lane, acc[t] * tok_scale[tok0 + t]);
-                }
+            if constexpr (GF::MIN) {
+                epilogue_sb(n - 1, pd, pdm, acc);
+                unit_output(tt, rt, ks, acc);
             } else {
-                float *part = p.part + ((size_t)ks * g.mpad + tok0) * g.npad + 128 * rt + r;
-#pragma unroll
-                for (int t = 0; t < H; t++) __stcg(part + (size_t)t * g.npad, acc[t]);
-                __threadfence();
-                asm volatile("bar.sync 1, %0;" ::"r"(kDqWarps * 32) : "memory");
-                if (threadIdx.x == 0) {
-                    const unsigned tile = (unsigned)(tt * g.n_rt + rt);
-                    last_s = atomicAdd(&p.counters[tile], 1u) == (unsigned)(g.nsplit - 1);
-                    if (last_s) p.counters[tile] = 0;
-                }
-                asm volatile("bar.sync 1, %0;" ::"r"(kDqWarps * 32) : "memory");
-                if (last_s) {
-                    __threadfence();
-                    if (grp < g.groups) {
-                        const float *pp = p.part + (size_t)tok0 * g.npad + 128 * rt + r;
-#pragma unroll
-                        for (int t = 0; t < H; t++) {
-                            float tot = 0.0f;
-                            for (int k2 = 0; k2 < g.nsplit; k2++)
-                                tot += __ldcg(pp + ((size_t)k2 * g.mpad + t) * g.npad);
-                            if (tok0 + t < p.m) gemv_epilogue<EPI>(p, grp, tok0 + t, lane, tot * tok_scale[tok0 + t]);
-                        }
-                    }
-                }
+                pend = true;
+                p_tt = tt;
+                p_rt = rt;
+                p_ks = ks;
+                p_nu = nu;
             }
         }
+        if constexpr (!GF::MIN) finish_pending();
     }
 
     tc_fence_before();

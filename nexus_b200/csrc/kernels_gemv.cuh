@@ -7,15 +7,17 @@
 // decoded in registers.
 //
 // Arithmetic.  Each token's input vector is re-expressed, per 256-element
-// super-block s, as x_i ~= u_s * z_i with z_i a 16-bit integer
-// (u_s = max|x|/32767), split as z = 256*h + l (h signed, l unsigned byte).
+// super-block s, as x_i ~= u_s * z_i with z_i a 24-bit integer
+// (u_s = max|x|/(2^23-1)), split as z = 65536*h + 256*m + l (h signed, m and
+// l unsigned bytes).
 // A weight element of every supported format is (scale)*(small integer q) -
 // (offset), so each super-block's contribution is
 //     u_s * ( d * sum_j sc_j * sum_{i in j} q_i z_i  -  dmin * sum_j m_j * sum_{i in j} z_i )
 // where the inner sums are exact 32-bit integer dot products (dp4a on four
-// bytes at a time).  The only rounding beyond f32 accumulation is the 16-bit
-// representation of x (|error| <= max|x|/65534 per super-block), which keeps
-// per-output relative error near 1e-5, far inside the 1e-3 parity bound.
+// bytes at a time).  The only rounding beyond f32 accumulation is the 24-bit
+// representation of x (|error| <= max|x|/(2^24-2) per super-block), so even
+// heavy-tailed inputs (a few large elements setting a super-block's step, as
+// in SwiGLU outputs) keep per-output errors near f32 rounding.
 //
 // Parallel layout.  An item is one (row group g of 32 rows, super-block s)
 // tile: C*512 contiguous bytes (tiles.cuh).  Warps form teams of S warps; a
@@ -54,6 +56,7 @@ struct Fmt<10> { static constexpr int C = 5; static constexpr bool AUX = true; }
 // x of one token for one super-block, in shared memory
 struct XSb {
     const uint4 *zh;  // 16 x uint4: signed high bytes of z for 256 elements
+    const uint4 *zm;  // 16 x uint4: unsigned middle bytes
     const uint4 *zl;  // 16 x uint4: unsigned low bytes
     const int *sz;    // 16 ints: sum of z over each 16-element group
     float u;
@@ -78,21 +81,25 @@ __device__ __forceinline__ float sb_dot_q4k(const uint4 *c, const XSb &x, int pa
     const uint32_t scl = s0 & 0x3f3f3f3fu, mnl = s1 & 0x3f3f3f3fu;
     const uint32_t sch = (s2 & 0x0f0f0f0fu) | ((s0 >> 2) & 0x30303030u);
     const uint32_t mnh = ((s2 >> 4) & 0x0f0f0f0fu) | ((s1 >> 2) & 0x30303030u);
-    int bh = 0, bl = 0, bh16 = 0, bl16 = 0, mn = 0;
+    int bh = 0, bm = 0, bl = 0, bh16 = 0, bm16 = 0, bl16 = 0;
+    float mn = 0.0f;
     constexpr int CPP = 8 / P;  // qs chunks per part (whole sub-block pairs)
 #pragma unroll
     for (int k = 0; k < CPP; k++) {
         const int cc = part * CPP + k;
         const uint4 q = NX_CH(1 + cc);
-        const uint4 zhl = x.zh[cc], zll = x.zl[cc], zhh = x.zh[8 + cc], zlh = x.zl[8 + cc];
-        int ah = 0, al = 0, ah2 = 0, al2 = 0;
+        const uint4 zhl = x.zh[cc], zml = x.zm[cc], zll = x.zl[cc];
+        const uint4 zhh = x.zh[8 + cc], zmh = x.zm[8 + cc], zlh = x.zl[8 + cc];
+        int ah = 0, am = 0, al = 0, ah2 = 0, am2 = 0, al2 = 0;
 #define NX_Q4K_STEP(W)                                              \
     {                                                               \
         const uint32_t lo = q.W & 0x0f0f0f0fu;                      \
         const uint32_t hi = q.W & 0xf0f0f0f0u;                      \
         ah = dp4a_us(lo, zhl.W, ah);                                \
+        am = dp4a_uu(lo, zml.W, am);                                \
         al = dp4a_uu(lo, zll.W, al);                                \
         ah2 = dp4a_us(hi, zhh.W, ah2);                              \
+        am2 = dp4a_uu(hi, zmh.W, am2);                              \
         al2 = dp4a_uu(hi, zlh.W, al2);                              \
     }
         NX_Q4K_STEP(x) NX_Q4K_STEP(y) NX_Q4K_STEP(z) NX_Q4K_STEP(w)
@@ -100,20 +107,24 @@ __device__ __forceinline__ float sb_dot_q4k(const uint4 *c, const XSb &x, int pa
         const int j = cc >> 1;
         const int sl = (int)byte_of(scl, j), sh = (int)byte_of(sch, j);
         bh += sl * ah;
+        bm += sl * am;
         bl += sl * al;
         bh16 += sh * ah2;
+        bm16 += sh * am2;
         bl16 += sh * al2;
         if ((cc & 1) == 0) {
-            // min term of sub-blocks j and j + 4 (32 elements each)
-            mn += (int)byte_of(mnl, j) * (x.sz[2 * j] + x.sz[2 * j + 1]) +
-                  (int)byte_of(mnh, j) * (x.sz[8 + 2 * j] + x.sz[8 + 2 * j + 1]);
+            // min term of sub-blocks j and j + 4 (32 elements each); the z sums
+            // reach 2^28, so their products with the mins are taken in f32
+            mn += (float)byte_of(mnl, j) * (float)(x.sz[2 * j] + x.sz[2 * j + 1]) +
+                  (float)byte_of(mnh, j) * (float)(x.sz[8 + 2 * j] + x.sz[8 + 2 * j + 1]);
         }
     }
-    // |bh16|, |bl16| < 2^29 (16 * 63 * 8 chunks * 16 products of <= 15*255);
-    // the factor 16 is exact in f32
+    // |b*16| < 2^29 (16 * 63 * 8 chunks * 16 products of <= 15*255); the
+    // factor 16 is exact in f32
     const float hsum = (float)bh + 0.0625f * (float)bh16;
+    const float msum = (float)bm + 0.0625f * (float)bm16;
     const float lsum = (float)bl + 0.0625f * (float)bl16;
-    return x.u * (d * (256.0f * hsum + lsum) - dmin * (float)mn);
+    return x.u * (d * (65536.0f * hsum + (256.0f * msum + lsum)) - dmin * mn);
 }
 
 // Q8_0 super-block: chunk 0 = eight f16 scales, chunks 1+2b, 2+2b = qs of block b
@@ -128,6 +139,7 @@ __device__ __forceinline__ float sb_dot_q80(const uint4 *c, const XSb &x, int pa
         const int b = part * BPP + k;
         const uint4 q0 = NX_CH(1 + 2 * b), q1 = NX_CH(2 + 2 * b);
         const uint4 h0 = x.zh[2 * b], h1 = x.zh[2 * b + 1], l0 = x.zl[2 * b], l1 = x.zl[2 * b + 1];
+        const uint4 m0 = x.zm[2 * b], m1 = x.zm[2 * b + 1];
         int ah = dp4a_ss(q0.x, h0.x, 0);
         ah = dp4a_ss(q0.y, h0.y, ah);
         ah = dp4a_ss(q0.z, h0.z, ah);
@@ -136,6 +148,14 @@ __device__ __forceinline__ float sb_dot_q80(const uint4 *c, const XSb &x, int pa
         ah = dp4a_ss(q1.y, h1.y, ah);
         ah = dp4a_ss(q1.z, h1.z, ah);
         ah = dp4a_ss(q1.w, h1.w, ah);
+        int am = dp4a_su(q0.x, m0.x, 0);
+        am = dp4a_su(q0.y, m0.y, am);
+        am = dp4a_su(q0.z, m0.z, am);
+        am = dp4a_su(q0.w, m0.w, am);
+        am = dp4a_su(q1.x, m1.x, am);
+        am = dp4a_su(q1.y, m1.y, am);
+        am = dp4a_su(q1.z, m1.z, am);
+        am = dp4a_su(q1.w, m1.w, am);
         int al = dp4a_su(q0.x, l0.x, 0);
         al = dp4a_su(q0.y, l0.y, al);
         al = dp4a_su(q0.z, l0.z, al);
@@ -145,7 +165,7 @@ __device__ __forceinline__ float sb_dot_q80(const uint4 *c, const XSb &x, int pa
         al = dp4a_su(q1.z, l1.z, al);
         al = dp4a_su(q1.w, l1.w, al);
         const float db = h2f_bits(sw[b >> 1] >> (16 * (b & 1)));
-        acc += db * (256.0f * (float)ah + (float)al);
+        acc += db * (65536.0f * (float)ah + (256.0f * (float)am + (float)al));
     }
     return x.u * acc;
 }
@@ -162,21 +182,24 @@ __device__ __forceinline__ float sb_dot_q40(const uint4 *c, const XSb &x, int pa
         const int b = part * BPP + k;
         const uint4 q = NX_CH(1 + b);
         const uint4 hl = x.zh[2 * b], hh = x.zh[2 * b + 1], ll = x.zl[2 * b], lh = x.zl[2 * b + 1];
-        int ah = 0, al = 0;
+        const uint4 ml = x.zm[2 * b], mh = x.zm[2 * b + 1];
+        int ah = 0, am = 0, al = 0;
 #define NX_Q40_STEP(W)                                  \
     {                                                   \
         const uint32_t lo = q.W & 0x0f0f0f0fu;          \
         const uint32_t hi = (q.W >> 4) & 0x0f0f0f0fu;   \
         ah = dp4a_us(lo, hl.W, ah);                     \
         ah = dp4a_us(hi, hh.W, ah);                     \
+        am = dp4a_uu(lo, ml.W, am);                     \
+        am = dp4a_uu(hi, mh.W, am);                     \
         al = dp4a_uu(lo, ll.W, al);                     \
         al = dp4a_uu(hi, lh.W, al);                     \
     }
         NX_Q40_STEP(x) NX_Q40_STEP(y) NX_Q40_STEP(z) NX_Q40_STEP(w)
 #undef NX_Q40_STEP
-        const int s32 = x.sz[2 * b] + x.sz[2 * b + 1];
+        const int s32 = x.sz[2 * b] + x.sz[2 * b + 1];  // < 2^28
         const float db = h2f_bits(sw[b >> 1] >> (16 * (b & 1)));
-        acc += db * (256.0f * (float)ah + (float)(al - 8 * s32));
+        acc += db * (65536.0f * (float)ah + (256.0f * (float)am + ((float)al - 8.0f * (float)s32)));
     }
     return x.u * acc;
 }
@@ -188,20 +211,25 @@ __device__ __forceinline__ float sb_dot_q2k(const uint4 *c, uint32_t aux, const 
     const float d = h2f_bits(aux), dmin = h2f_bits(aux >> 16);
     const uint4 c0 = NX_CH(0);
     const uint32_t scw[4] = {c0.x, c0.y, c0.z, c0.w};
-    int bh = 0, bl = 0, mn = 0;
+    int bh = 0, bm = 0, bl = 0;
+    float mn = 0.0f;
     constexpr int JPP = 16 / P;
 #pragma unroll
     for (int k = 0; k < JPP; k++) {
         const int j = part * JPP + k;
         const uint4 qq = NX_CH(1 + (j >> 2));
         const uint32_t qw = (j & 3) == 0 ? qq.x : (j & 3) == 1 ? qq.y : (j & 3) == 2 ? qq.z : qq.w;
-        const uint4 h = x.zh[j], l = x.zl[j];
+        const uint4 h = x.zh[j], mm = x.zm[j], l = x.zl[j];
         const uint32_t p0 = qw & 0x03030303u, p1 = (qw >> 2) & 0x03030303u;
         const uint32_t p2 = (qw >> 4) & 0x03030303u, p3 = (qw >> 6) & 0x03030303u;
         int ah = dp4a_us(p0, h.x, 0);
         ah = dp4a_us(p1, h.y, ah);
         ah = dp4a_us(p2, h.z, ah);
         ah = dp4a_us(p3, h.w, ah);
+        int am = dp4a_uu(p0, mm.x, 0);
+        am = dp4a_uu(p1, mm.y, am);
+        am = dp4a_uu(p2, mm.z, am);
+        am = dp4a_uu(p3, mm.w, am);
         int al = dp4a_uu(p0, l.x, 0);
         al = dp4a_uu(p1, l.y, al);
         al = dp4a_uu(p2, l.z, al);
@@ -209,10 +237,11 @@ __device__ __forceinline__ float sb_dot_q2k(const uint4 *c, uint32_t aux, const 
         const uint32_t sb = byte_of(scw[j >> 2], j & 3);
         const int sc = (int)(sb & 15u), m = (int)(sb >> 4);
         bh += sc * ah;
+        bm += sc * am;
         bl += sc * al;
-        mn += m * x.sz[j];
+        mn += (float)m * (float)x.sz[j];
     }
-    return x.u * (d * (256.0f * (float)bh + (float)bl) - dmin * (float)mn);
+    return x.u * (d * (65536.0f * (float)bh + (256.0f * (float)bm + (float)bl)) - dmin * mn);
 }
 #undef NX_CH
 
@@ -224,20 +253,22 @@ __device__ __forceinline__ float sb_dot(const uint4 *c, uint32_t aux, const XSb 
     else return sb_dot_q2k<P>(c, aux, x, part);
 }
 
-// Shared-memory bytes of the prepared input of one token: zh[k], zl[k],
-// sz[k/16], u[k/256], padded to 16 bytes so every token's image is aligned.
+// Shared-memory bytes of the prepared input of one token: zh[k], zm[k],
+// zl[k], sz[k/16], u[k/256], padded to 16 bytes so every token's image is
+// aligned.
 __host__ __device__ __forceinline__ size_t tok_smem_bytes(int k) {
-    return ((size_t)2 * k + (size_t)4 * (k / 16) + (size_t)4 * (k / 256) + 15) / 16 * 16;
+    return ((size_t)3 * k + (size_t)4 * (k / 16) + (size_t)4 * (k / 256) + 15) / 16 * 16;
 }
 
-// Prepare super-block s of one token: 16-bit quantization of x (times the
+// Prepare super-block s of one token: 24-bit quantization of x (times the
 // RMSNorm weight when fused) from the lane's 8 values v (elements
 // 8*lane .. 8*lane+7).  The quantization is scale-invariant, so RMSNorm's
 // rstd is not needed here: the caller multiplies u[s] by rstd once the sum of
 // squares, accumulated in *ss, is known.  (x*rstd)*w and rstd*(x*w) agree to
-// f32 rounding, far below the 16-bit step.
+// f32 rounding, far below the 24-bit step.
 __device__ __forceinline__ void prep_sb_vals(float (&v)[8], const float (&w)[8], bool has_w, int s, int lane,
-                                             uint32_t *zh, uint32_t *zl, int *sz, float *u, float *ss) {
+                                             uint32_t *zh, uint32_t *zm, uint32_t *zl, int *sz, float *u,
+                                             float *ss) {
 #pragma unroll
     for (int i = 0; i < 8; i++) *ss += v[i] * v[i];
     if (has_w) {
@@ -248,29 +279,34 @@ __device__ __forceinline__ void prep_sb_vals(float (&v)[8], const float (&w)[8],
 #pragma unroll
     for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
     amax = warp_max(amax);
-    const float inv = (amax > 0.0f && amax <= 3.0e38f) ? 32767.0f / amax : 0.0f;
+    const float inv = (amax > 0.0f && amax <= 3.0e38f) ? 8388607.0f / amax : 0.0f;
     int z[8], psum = 0;
 #pragma unroll
     for (int i = 0; i < 8; i++) {
-        z[i] = __float2int_rn(v[i] * inv);
+        // v * inv can round to 2^23 for the largest element; the top byte is signed
+        z[i] = max(-8388607, min(8388607, __float2int_rn(v[i] * inv)));
         psum += z[i];
     }
-    uint32_t h0 = 0, h1 = 0, l0 = 0, l1 = 0;
+    uint32_t h0 = 0, h1 = 0, m0 = 0, m1 = 0, l0 = 0, l1 = 0;
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        h0 |= ((uint32_t)(z[i] >> 8) & 0xffu) << (8 * i);
-        h1 |= ((uint32_t)(z[4 + i] >> 8) & 0xffu) << (8 * i);
+        h0 |= ((uint32_t)(z[i] >> 16) & 0xffu) << (8 * i);
+        h1 |= ((uint32_t)(z[4 + i] >> 16) & 0xffu) << (8 * i);
+        m0 |= ((uint32_t)(z[i] >> 8) & 0xffu) << (8 * i);
+        m1 |= ((uint32_t)(z[4 + i] >> 8) & 0xffu) << (8 * i);
         l0 |= ((uint32_t)z[i] & 0xffu) << (8 * i);
         l1 |= ((uint32_t)z[4 + i] & 0xffu) << (8 * i);
     }
     const int wi = 64 * s + 2 * lane;
     zh[wi] = h0;
     zh[wi + 1] = h1;
+    zm[wi] = m0;
+    zm[wi + 1] = m1;
     zl[wi] = l0;
     zl[wi + 1] = l1;
     psum += __shfl_xor_sync(0xffffffffu, psum, 1);
     if ((lane & 1) == 0) sz[16 * s + (lane >> 1)] = psum;
-    if (lane == 0) u[s] = amax / 32767.0f;
+    if (lane == 0) u[s] = amax / 8388607.0f;
 }
 
 // One warp prepares super-blocks warp, warp + W, ... of one token.  All of a
@@ -279,7 +315,8 @@ __device__ __forceinline__ void prep_sb_vals(float (&v)[8], const float (&w)[8],
 constexpr int kPrepBatch = 4;
 template <int W>
 __device__ __forceinline__ float prep_token(const float *__restrict__ x, const float *__restrict__ nw, int n_sb,
-                                            int warp, int lane, uint32_t *zh, uint32_t *zl, int *sz, float *u) {
+                                            int warp, int lane, uint32_t *zh, uint32_t *zm, uint32_t *zl, int *sz,
+                                            float *u) {
     float ss = 0.0f;
     for (int base = warp; base < n_sb; base += W * kPrepBatch) {
         float4 xa[kPrepBatch], xb[kPrepBatch], wa[kPrepBatch], wb[kPrepBatch];
@@ -307,7 +344,7 @@ __device__ __forceinline__ float prep_token(const float *__restrict__ x, const f
                     w[0] = wa[i].x; w[1] = wa[i].y; w[2] = wa[i].z; w[3] = wa[i].w;
                     w[4] = wb[i].x; w[5] = wb[i].y; w[6] = wb[i].z; w[7] = wb[i].w;
                 }
-                prep_sb_vals(v, w, nw != nullptr, s, lane, zh, zl, sz, u, &ss);
+                prep_sb_vals(v, w, nw != nullptr, s, lane, zh, zm, zl, sz, u, &ss);
             }
         }
     }
@@ -467,10 +504,11 @@ __global__ void __launch_bounds__(Ring<FMT>::W * 32, 1) k_gemv(GemvParams p) {
     for (int t = 0; t < M; t++) {
         uint8_t *tb = xs + tok_bytes * t;
         uint32_t *zh = reinterpret_cast<uint32_t *>(tb);
-        uint32_t *zl = reinterpret_cast<uint32_t *>(tb + k);
-        int *sz = reinterpret_cast<int *>(tb + 2 * k);
-        float *u = reinterpret_cast<float *>(tb + 2 * k + 4 * (k / 16));
-        float ss = prep_token<W>(p.x + (size_t)t * p.x_stride, p.norm_w, n_sb, warp, lane, zh, zl, sz, u);
+        uint32_t *zm = reinterpret_cast<uint32_t *>(tb + k);
+        uint32_t *zl = reinterpret_cast<uint32_t *>(tb + 2 * k);
+        int *sz = reinterpret_cast<int *>(tb + 3 * k);
+        float *u = reinterpret_cast<float *>(tb + 3 * k + 4 * (k / 16));
+        float ss = prep_token<W>(p.x + (size_t)t * p.x_stride, p.norm_w, n_sb, warp, lane, zh, zm, zl, sz, u);
         if (p.norm_w) {
             ss = warp_sum(ss);
             if (lane == 0) misc[warp * M + t] = ss;
@@ -484,7 +522,7 @@ __global__ void __launch_bounds__(Ring<FMT>::W * 32, 1) k_gemv(GemvParams p) {
             float ss = 0.0f;
             for (int w = 0; w < W; w++) ss += misc[w * M + t];
             const float rstd = 1.0f / sqrtf(ss / (float)k + p.eps);
-            float *u = reinterpret_cast<float *>(xs + tok_bytes * t + 2 * k + 4 * (k / 16));
+            float *u = reinterpret_cast<float *>(xs + tok_bytes * t + 3 * k + 4 * (k / 16));
             for (int s = threadIdx.x; s < n_sb; s += W * 32) u[s] *= rstd;
         }
         __syncthreads();
@@ -525,9 +563,10 @@ __global__ void __launch_bounds__(Ring<FMT>::W * 32, 1) k_gemv(GemvParams p) {
                 const uint8_t *tb = xs + tok_bytes * t;
                 XSb xsb;
                 xsb.zh = reinterpret_cast<const uint4 *>(tb) + 16 * s_sb;
-                xsb.zl = reinterpret_cast<const uint4 *>(tb + k) + 16 * s_sb;
-                xsb.sz = reinterpret_cast<const int *>(tb + 2 * k) + 16 * s_sb;
-                xsb.u = reinterpret_cast<const float *>(tb + 2 * k + 4 * (k / 16))[s_sb];
+                xsb.zm = reinterpret_cast<const uint4 *>(tb + k) + 16 * s_sb;
+                xsb.zl = reinterpret_cast<const uint4 *>(tb + 2 * k) + 16 * s_sb;
+                xsb.sz = reinterpret_cast<const int *>(tb + 3 * k) + 16 * s_sb;
+                xsb.u = reinterpret_cast<const float *>(tb + 3 * k + 4 * (k / 16))[s_sb];
                 acc[t] += sb_dot<FMT, 1>(cbase, auxw, xsb, 0);
             }
             // every lane has consumed the slot's values: refill it with item j + NST
