@@ -184,7 +184,7 @@ def run_reference(args):
     import nexus_b200 as nb
     path = nb.model_path(args.config, threads=cpu_threads())
     threads = cpu_threads()
-    warm = min(args.warmup, 1)
+    warm = min(args.warmup, 3)  # CPU steps take seconds: at most three untimed ones
     r = time_oracle(path, args.steps, warm, budget_s=args.ref_budget, threads=threads)
     line = {
         "impl": "reference", "metric": "decode tok/s, Llama-3-8B-shape Q4_K, b=1", "value": r["tok_s"],
