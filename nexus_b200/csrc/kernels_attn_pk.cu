@@ -25,8 +25,8 @@
 // maximum (of log2 p_t + log2 scale_t), so they stay in f16 range whatever the
 // scales.
 //
-// Layout: grid (Hkv, slices, batch), 4 warps.  A warp owns a tile of 64
-// tokens (32 for 6- and 8-bit codes) of one KV head at a time and all G query
+// Layout: grid (Hkv, slices, batch), 4 warps.  A warp owns a tile of 32
+// tokens of one KV head at a time and all G query
 // heads sharing it; lane (g, c) = (lane / 4, lane % 4) holds, per 16-token
 // block, tokens g and g + 8 of head c's scores and dims 16g .. 16g+15 of head
 // c's output.  Tiles reach shared memory by cp.async into two stages per warp,
