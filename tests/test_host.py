@@ -92,3 +92,24 @@ def test_synthetic_weights_are_seeded_normal(nb, oracle, tmp_path):
     w = read_tensor(path, "blk.0.attn_q.weight")
     assert w.size == 256 * 256
     assert abs(float(w.mean())) < 1e-3 and abs(float(w.std()) - 0.02) < 5e-4
+
+
+def test_bench_reference_arm_prints_one_contract_line():
+    """`bench.py --impl reference` (the oracle port on the host cores) prints one
+    JSON line with the contract's keys; the tiny config keeps it to seconds."""
+    import json
+    import subprocess
+    import sys
+    root = Path(__file__).resolve().parents[1]
+    r = subprocess.run([sys.executable, str(root / "bench.py"), "--impl", "reference", "--config", "tiny",
+                        "--steps", "2", "--warmup", "3"], capture_output=True, text=True, timeout=600, cwd=root)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "scaling", "vs_baseline", "dtype", "data", "config", "e2e", "cpu_baseline"):
+        assert key in d, key
+    assert d["impl"] == "reference" and d["value"] > 0 and d["warmup"] == 3
+    assert d["cpu_baseline"]["kind"] in ("port", "reference") and d["cpu_baseline"]["cores"] >= 1
+    assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
