@@ -286,10 +286,10 @@ int nexus_cuda_profile_decode(nexus_cuda_model *m, uint32_t seq_id, uint32_t tok
                               nexus_kernel_profile *out, int max_out, int *n_out);
 
 /* GQA decode attention that allocates nothing (no counterpart in the
- * reference).  For callers that must not allocate device memory while they
- * run -- inside a CUDA stream capture, in serving loops that cannot take the
- * device-wide synchronization of cudaMalloc/cudaFree, or in embedders whose
- * device memory comes from their own pool.  Same computation as
+ * reference).  For callers that cannot allocate device memory while they
+ * run -- serving loops that cannot take the device-wide synchronization of
+ * cudaMalloc/cudaFree, and embedders whose device memory is all handed to
+ * their own pool.  Same computation as
  * nexus_cuda_execute with NEXUS_OP_ATTENTION on device pointers: q is
  * num_q_heads*head_dim floats, k/v are seq_len rows of num_kv_heads*head_dim
  * floats, out is num_q_heads*head_dim floats, all device memory owned by the
@@ -298,7 +298,9 @@ int nexus_cuda_profile_decode(nexus_cuda_model *m, uint32_t seq_id, uint32_t tok
  * more return NEXUS_E_INVALID.  All calls share that array: calls that
  * overlap on the GPU race, so order them on one stream.  The first call on a
  * device looks up the array's address and should come before any stream
- * capture.  Synchronous on the backend's stream. */
+ * capture.  Synchronous on the backend's stream; the calling thread's current
+ * device is left as it was.  num_q_heads must be a nonzero multiple of
+ * num_kv_heads. */
 int nexus_cuda_attention_noalloc(nexus_cuda_backend *b, const float *q_dev, const float *k_dev,
                                  const float *v_dev, float *out_dev, size_t num_q_heads,
                                  size_t num_kv_heads, size_t head_dim, size_t seq_len, float scale);

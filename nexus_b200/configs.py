@@ -42,6 +42,16 @@ CONFIGS = {
     "llama70b": dict(num_layers=80, hidden_size=8192, num_heads=64, num_kv_heads=8, ff_dim=28672,
                      vocab_size=128256, context_length=4352, rope_theta=500000.0, attn_format=Q4_K,
                      ffn_format=Q2_K, embd_format=Q8_0, head_format=Q8_0, norm_format=Q4_K, repeat_chunks=64),
+    # parity subsamples of the long-context workloads (every element drawn):
+    # the config-P model's widths and formats with 2 layers (8k-token contexts
+    # on the packed cache) and the config-X model's with 2 layers (Q4_K
+    # attention, Q2_K FFN at the 70B widths)
+    "llama8b_q8_l2": dict(num_layers=2, hidden_size=4096, num_heads=32, num_kv_heads=8, ff_dim=14336,
+                          vocab_size=128256, context_length=8448, rope_theta=500000.0, attn_format=Q8_0,
+                          ffn_format=Q8_0, embd_format=Q8_0, head_format=Q8_0, norm_format=Q8_0),
+    "llama70b_l2": dict(num_layers=2, hidden_size=8192, num_heads=64, num_kv_heads=8, ff_dim=28672,
+                        vocab_size=128256, context_length=4352, rope_theta=500000.0, attn_format=Q4_K,
+                        ffn_format=Q2_K, embd_format=Q8_0, head_format=Q8_0, norm_format=Q4_K),
 }
 
 
@@ -56,9 +66,14 @@ def model_dir() -> Path:
     return d
 
 
-def model_path(name_or_cfg, seed: int = 0, threads: int = 0) -> Path:
-    """Path of the synthetic GGUF for a configuration, writing it on first use."""
-    from .engine import write_synthetic_model
+def model_path(name_or_cfg, seed: int = 0, threads: int = 0, writer=None) -> Path:
+    """Path of the synthetic GGUF for a configuration, writing it on first use.
+
+    writer: the function that writes the file (default: the CUDA library's
+    nexus_synth_model_write).  CPU-only callers pass the oracle's writer, which
+    produces the same bytes without loading the CUDA library."""
+    if writer is None:
+        from .engine import write_synthetic_model as writer
 
     cfg = dict(CONFIGS[name_or_cfg]) if isinstance(name_or_cfg, str) else dict(name_or_cfg)
     cfg["seed"] = seed
@@ -67,7 +82,7 @@ def model_path(name_or_cfg, seed: int = 0, threads: int = 0) -> Path:
     done = path.with_suffix(".ok")
     if not (path.exists() and done.exists()):
         tmp = path.with_suffix(".tmp")
-        write_synthetic_model(str(tmp), threads=threads, **cfg)
+        writer(str(tmp), threads=threads, **cfg)
         os.replace(tmp, path)
         done.write_text("ok")
     return path

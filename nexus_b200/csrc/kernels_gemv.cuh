@@ -29,7 +29,7 @@
 // 32g+i.  The S partial sums of a row group meet in shared memory behind a
 // named barrier of the team, and the team's first warp adds them in warp
 // order and applies the epilogue (deterministic).  CTAs are persistent, one
-// per SM, and prepare the input (16-bit quantization, RMSNorm folded into
+// per SM, and prepare the input (24-bit quantization, RMSNorm folded into
 // the per-super-block scale) once.  The first ring slots are filled before
 // griddepcontrol.wait, so under programmatic dependent launch a GEMV streams
 // weights while the previous kernel finishes.

@@ -1,10 +1,12 @@
 // noalloc.cu -- GQA decode attention for callers that cannot allocate memory.
 //
-// Some callers of this library must not allocate device memory while they
-// run: code inside a CUDA stream capture (cudaMalloc/cudaFree are not stream
-// operations, and cudaFree synchronizes the whole device), serving loops that
-// cannot afford that device-wide synchronization between steps, and embedders
-// whose device memory belongs to their own pool or arena.  The regular
+// Some callers of this library cannot allocate device memory while they run:
+// serving loops that cannot take the device-wide synchronization that
+// cudaFree (and often cudaMalloc) imposes between steps, embedders whose whole
+// device memory is handed to their own pool or arena up front (a cudaMalloc
+// would fail, or steal memory the pool has accounted for), and latency-bound
+// paths that must not meet an out-of-memory error in the middle of serving.
+// The regular
 // attention entry point (nexus_cuda_execute with NEXUS_OP_ATTENTION) obtains
 // its scratch -- the per-slice softmax partials, the per-head arrival counters
 // and the step descriptor -- with cudaMalloc on every call.  The entry point in
@@ -74,7 +76,8 @@ extern "C" int nexus_cuda_attention_noalloc(nexus_cuda_backend *b, const float *
         return nexus_backend_fail(b, NEXUS_E_INVALID, "attention_noalloc: NULL backend");
     if (!q_dev || !k_dev || !v_dev || !out_dev)
         return nexus_backend_fail(b, NEXUS_E_INVALID, "attention_noalloc: NULL device pointer");
-    if (seq_len == 0 || num_kv_heads == 0 || num_q_heads % num_kv_heads || seq_len > 0x7fffffffu)
+    if (seq_len == 0 || num_kv_heads == 0 || num_q_heads == 0 || num_q_heads % num_kv_heads ||
+        seq_len > 0x7fffffffu)
         return nexus_backend_fail(b, NEXUS_E_INVALID, "attention_noalloc: bad shape");
     if (head_dim != 32 && head_dim != 64 && head_dim != 128)
         return nexus_backend_fail(b, NEXUS_E_INVALID, "attention_noalloc: head_dim must be 32, 64 or 128");
@@ -90,6 +93,15 @@ extern "C" int nexus_cuda_attention_noalloc(nexus_cuda_backend *b, const float *
                                    " scratch bytes, more than the fixed 1 MiB")
                                       .c_str());
     if (dev < 0 || dev >= 64) return nexus_backend_fail(b, NEXUS_E_INVALID, "attention_noalloc: device ordinal >= 64");
+    // the backend's device is made current for the call; the caller's is restored on return
+    int caller_dev = -1;
+    if (cudaGetDevice(&caller_dev) != cudaSuccess) caller_dev = -1;
+    struct RestoreDevice {
+        int d;
+        ~RestoreDevice() {
+            if (d >= 0) cudaSetDevice(d);
+        }
+    } restore{caller_dev};
     cudaError_t e = cudaSetDevice(dev);
     void *base = nullptr;
     if (e == cudaSuccess) {

@@ -1313,3 +1313,518 @@ int orc_model_generate(orc_model *m, const uint32_t *prompt, size_t n, size_t ma
     free(logits);
     return rc;
 }
+
+/* ------------------------------------------------------------------------ */
+/* Layer-major prefill (a faster schedule of orc_model_prefill, same bits)   */
+/* ------------------------------------------------------------------------ */
+/* The reference prefill (src/engine/mod.rs:1149-1170) runs decode_with_cache
+ * once per prompt token.  Token p at layer l reads only the layer-l K/V of
+ * tokens 0..p, so running every token through layer l before layer l+1 gives
+ * the same values as long as each token's own arithmetic is unchanged: every
+ * matvec row below is the same sequential f32 sum (mul then add, in column
+ * order), merely computed for a tile of tokens at once (one dequantized row,
+ * many tokens), and attention for token p runs over exactly p + 1 cached
+ * positions.  Used to produce parity fixtures at long contexts; the result is
+ * checked bit for bit against orc_model_prefill by tests/test_oracle_batched.py. */
+
+#define ORC_TT 32 /* tokens per tile of the batched matvec */
+typedef float orc_v8 __attribute__((vector_size(32)));
+
+typedef struct {
+    int type;
+    const uint8_t *w;
+    size_t rows, cols, nt;
+    const float *xt; /* [cols][nt]: token-minor copy of the inputs */
+    float *y;        /* [nt][y_stride] */
+    size_t y_stride;
+    size_t r0, r1;
+    int rc;
+} qmm_job;
+
+__attribute__((target_clones("avx512f", "avx2", "default")))
+static void qmm_rows(qmm_job *j, float *row) {
+    const size_t nt = j->nt, K = j->cols;
+    for (size_t r = j->r0; r < j->r1; r++) {
+        orc_dequantize_range(j->type, j->w, r * K, K, row);
+        for (size_t t0 = 0; t0 < nt; t0 += ORC_TT) {
+            const size_t tn = nt - t0 < ORC_TT ? nt - t0 : ORC_TT;
+            if (tn == ORC_TT) {
+                orc_v8 a0 = {0}, a1 = {0}, a2 = {0}, a3 = {0};
+                for (size_t c = 0; c < K; c++) {
+                    const float *xp = j->xt + c * nt + t0;
+                    orc_v8 x0, x1, x2, x3;
+                    memcpy(&x0, xp, 32);
+                    memcpy(&x1, xp + 8, 32);
+                    memcpy(&x2, xp + 16, 32);
+                    memcpy(&x3, xp + 24, 32);
+                    const float wv = row[c];
+                    /* sum += w * x: a separately rounded product, then the add */
+                    a0 = a0 + wv * x0;
+                    a1 = a1 + wv * x1;
+                    a2 = a2 + wv * x2;
+                    a3 = a3 + wv * x3;
+                }
+                float acc[ORC_TT];
+                memcpy(acc, &a0, 32);
+                memcpy(acc + 8, &a1, 32);
+                memcpy(acc + 16, &a2, 32);
+                memcpy(acc + 24, &a3, 32);
+                for (size_t t = 0; t < ORC_TT; t++) j->y[(t0 + t) * j->y_stride + r] = acc[t];
+            } else {
+                for (size_t t = 0; t < tn; t++) {
+                    float sum = 0.0f;
+                    for (size_t c = 0; c < K; c++) sum += row[c] * j->xt[c * nt + t0 + t];
+                    j->y[(t0 + t) * j->y_stride + r] = sum;
+                }
+            }
+        }
+    }
+}
+
+static void *qmm_worker(void *arg) {
+    qmm_job *j = (qmm_job *)arg;
+    float *row = (float *)malloc(j->cols * sizeof(float));
+    if (!row) {
+        j->rc = ORC_E_NOMEM;
+        return NULL;
+    }
+    qmm_rows(j, row);
+    free(row);
+    return NULL;
+}
+
+/* Y[t][r] = sum_c W[r][c] * X[t][c] for nt tokens; rows split over threads. */
+static int orc_qmatmul(int type, const uint8_t *w, size_t rows, size_t cols, const float *x,
+                       size_t x_stride, size_t nt, float *y, size_t y_stride, int threads) {
+    size_t be, bb;
+    if (!block_geom(type, &be, &bb)) return ORC_E_UNSUPPORTED;
+    float *xt = (float *)malloc(cols * nt * sizeof(float) + 64);
+    if (!xt) return ORC_E_NOMEM;
+    for (size_t t = 0; t < nt; t++)
+        for (size_t c = 0; c < cols; c++) xt[c * nt + t] = x[t * x_stride + c];
+    if (threads < 1) threads = 1;
+    if (threads > 256) threads = 256;
+    if ((size_t)threads > rows) threads = rows ? (int)rows : 1;
+    pthread_t tid[256];
+    qmm_job jobs[256];
+    size_t per = rows / threads, extra = rows % threads, r = 0;
+    for (int t = 0; t < threads; t++) {
+        size_t n = per + ((size_t)t < extra ? 1 : 0);
+        jobs[t] = (qmm_job){type, w, rows, cols, nt, xt, y, y_stride, r, r + n, ORC_OK};
+        r += n;
+        pthread_create(&tid[t], NULL, qmm_worker, &jobs[t]);
+    }
+    int rc = ORC_OK;
+    for (int t = 0; t < threads; t++) {
+        pthread_join(tid[t], NULL);
+        if (jobs[t].rc) rc = jobs[t].rc;
+    }
+    free(xt);
+    return rc;
+}
+
+static int bmatmul(orc_model *m, const orc_wt *w, size_t rows, size_t cols, const float *x,
+                   size_t x_stride, size_t nt, float *y, size_t y_stride) {
+    if (!w->present) return ORC_E_MISSING_TENSOR;
+    if (w->elems < rows * cols) return ORC_E_SHAPE;
+    return orc_qmatmul(w->type, w->data, rows, cols, x, x_stride, nt, y, y_stride, m->threads);
+}
+
+/* attention_decode (:452-499) for one query head over `len` cached positions */
+static void attention_head(const orc_model *m, const orc_layer *L, size_t len, const float *q,
+                           size_t qh, float *scores, float *out) {
+    size_t D = m->info.head_dim, Hq = m->info.num_heads, Hkv = m->info.num_kv_heads;
+    size_t kv_dim = Hkv * D;
+    size_t group = Hq / Hkv;
+    if (group < 1) group = 1;
+    float scale = 1.0f / sqrtf((float)D);
+    size_t kvh = qh / group;
+    if (kvh > Hkv - 1) kvh = Hkv - 1;
+    for (size_t d = 0; d < D; d++) out[qh * D + d] = 0.0f;
+    for (size_t t = 0; t < len; t++) {
+        float score = 0.0f;
+        for (size_t d = 0; d < D; d++) score += q[qh * D + d] * kv_value(L, 0, t, kvh * D + d, kv_dim);
+        scores[t] = score * scale;
+    }
+    float mx = -INFINITY;
+    for (size_t t = 0; t < len; t++) mx = fmaxf(mx, scores[t]);
+    float sum_exp = 0.0f;
+    for (size_t t = 0; t < len; t++) {
+        scores[t] = expf(scores[t] - mx);
+        sum_exp += scores[t];
+    }
+    if (sum_exp <= 0.0f) return;
+    for (size_t d = 0; d < D; d++) {
+        float ws = 0.0f;
+        size_t dim = kvh * D + d;
+        for (size_t t = 0; t < len; t++) ws += (scores[t] / sum_exp) * kv_value(L, 1, t, dim, kv_dim);
+        out[qh * D + d] = ws;
+    }
+}
+
+typedef struct {
+    const orc_model *m;
+    const orc_layer *L;
+    const float *q;  /* [n][Q] */
+    float *out;      /* [n][Q] */
+    size_t p0, n, Q;
+    size_t w, nw;    /* this worker takes (token, head) pairs w, w + nw, ... */
+} attn_job;
+
+static void *attn_worker(void *arg) {
+    attn_job *j = (attn_job *)arg;
+    size_t Hq = j->m->info.num_heads;
+    float *scores = (float *)malloc((j->p0 + j->n + 1) * sizeof(float));
+    if (!scores) return (void *)1;
+    for (size_t i = j->w; i < j->n * Hq; i += j->nw) {
+        size_t t = i / Hq, qh = i % Hq;
+        attention_head(j->m, j->L, j->p0 + t + 1, j->q + t * j->Q, qh, scores, j->out + t * j->Q);
+    }
+    free(scores);
+    return NULL;
+}
+
+/* orc_model_prefill with a layer-major schedule: identical logits and KV. */
+int orc_model_prefill_batched(orc_model *m, const uint32_t *tokens, size_t n, float *logits) {
+    if (n == 0) return ORC_OK;
+    orc_model_info *I = &m->info;
+    if (n > I->max_seq_len) return ORC_E_INVALID; /* no shift-on-full in this schedule */
+    kv_clear(m);
+    size_t H = I->hidden_size, D = I->head_dim, F = I->ff_dim;
+    size_t Q = (size_t)I->num_heads * D, kv_dim = (size_t)I->num_kv_heads * D;
+    float eps = I->rms_norm_eps;
+    int rc = ORC_OK;
+    if (!m->embd.present) return ORC_E_MISSING_TENSOR;
+    size_t vocab_rows = m->embd.elems / H;
+    if (vocab_rows < 1) vocab_rows = 1;
+    float *hid = (float *)malloc(n * H * sizeof(float));
+    float *nrm = (float *)malloc(n * H * sizeof(float));
+    float *qb = (float *)malloc(n * Q * sizeof(float));
+    float *kb = (float *)malloc(n * kv_dim * sizeof(float));
+    float *vb = (float *)malloc(n * kv_dim * sizeof(float));
+    float *ab = (float *)malloc(n * Q * sizeof(float));
+    float *tb = (float *)malloc(n * H * sizeof(float));
+    float *gb = (float *)malloc(n * F * sizeof(float));
+    float *ub = (float *)malloc(n * F * sizeof(float));
+    float *wn = (float *)malloc(H * sizeof(float));
+    if (!hid || !nrm || !qb || !kb || !vb || !ab || !tb || !gb || !ub || !wn) {
+        rc = ORC_E_NOMEM;
+        goto done;
+    }
+    for (size_t p = 0; p < n; p++) {
+        size_t start = ((size_t)tokens[p] % vocab_rows) * H;
+        if (start + H > m->embd.elems) {
+            rc = ORC_E_SHAPE;
+            goto done;
+        }
+        orc_dequantize_range(m->embd.type, m->embd.data, start, H, hid + p * H);
+    }
+    for (uint32_t l = 0; l < I->num_layers && rc == ORC_OK; l++) {
+        orc_layer *L = &m->layers[l];
+        for (size_t p = 0; p < n && rc == ORC_OK; p++)
+            rc = wnorm(&L->attn_norm, H, hid + p * H, eps, nrm + p * H, wn);
+        if (!rc) rc = bmatmul(m, &L->q, Q, H, nrm, H, n, qb, Q);
+        if (!rc) rc = bmatmul(m, &L->k, kv_dim, H, nrm, H, n, kb, kv_dim);
+        if (!rc) rc = bmatmul(m, &L->v, kv_dim, H, nrm, H, n, vb, kv_dim);
+        if (rc) break;
+        for (size_t p = 0; p < n; p++) {
+            for (size_t h = 0; h + D <= Q; h += D) orc_rope_single(qb + p * Q + h, p, D, I->rope_freq_base);
+            for (size_t h = 0; h + D <= kv_dim; h += D)
+                orc_rope_single(kb + p * kv_dim + h, p, D, I->rope_freq_base);
+            kv_add(m, L, kb + p * kv_dim, vb + p * kv_dim);
+        }
+        {
+            int nw = m->threads < 1 ? 1 : (m->threads > 256 ? 256 : m->threads);
+            pthread_t tid[256];
+            attn_job jobs[256];
+            for (int w = 0; w < nw; w++) {
+                jobs[w] = (attn_job){m, L, qb, ab, 0, n, Q, (size_t)w, (size_t)nw};
+                pthread_create(&tid[w], NULL, attn_worker, &jobs[w]);
+            }
+            for (int w = 0; w < nw; w++) {
+                void *ret;
+                pthread_join(tid[w], &ret);
+                if (ret) rc = ORC_E_NOMEM;
+            }
+        }
+        if (!rc) rc = bmatmul(m, &L->o, H, H, ab, Q, n, tb, H);
+        if (rc) break;
+        for (size_t i = 0; i < n * H; i++) hid[i] += tb[i];
+        for (size_t p = 0; p < n && rc == ORC_OK; p++)
+            rc = wnorm(&L->ffn_norm, H, hid + p * H, eps, nrm + p * H, wn);
+        if (!rc) rc = bmatmul(m, &L->gate, F, H, nrm, H, n, gb, F);
+        if (!rc) rc = bmatmul(m, &L->up, F, H, nrm, H, n, ub, F);
+        if (rc) break;
+        for (size_t i = 0; i < n * F; i++) gb[i] = (gb[i] / (1.0f + expf(-gb[i]))) * ub[i];
+        rc = bmatmul(m, &L->down, H, F, gb, F, n, tb, H);
+        if (rc) break;
+        for (size_t i = 0; i < n * H; i++) hid[i] += tb[i];
+    }
+    if (rc == ORC_OK) {
+        /* the last token's logits, as decode_with_cache returns them */
+        memcpy(m->hidden, hid + (n - 1) * H, H * sizeof(float));
+        if (m->out_norm.present && m->out_norm.elems >= H) {
+            orc_dequantize_range(m->out_norm.type, m->out_norm.data, 0, H, m->norm_tmp);
+        } else {
+            for (size_t i = 0; i < H; i++) m->norm_tmp[i] = 1.0f;
+        }
+        orc_rms_norm(m->hidden, m->norm_tmp, H, eps, m->normed);
+        if (m->out_head.present) {
+            size_t rows = m->out_head.elems / H;
+            rc = orc_qmatvec(m->out_head.type, m->out_head.data, rows, H, m->normed, logits, m->threads);
+        } else {
+            memcpy(logits, m->normed, H * sizeof(float));
+        }
+    }
+done:
+    free(hid);
+    free(nrm);
+    free(qb);
+    free(kb);
+    free(vb);
+    free(ab);
+    free(tb);
+    free(gb);
+    free(ub);
+    free(wn);
+    return rc;
+}
+
+/* ------------------------------------------------------------------------ */
+/* Seeded synthetic GGUF writer (test infrastructure)                        */
+/* ------------------------------------------------------------------------ */
+/* Writes the same bytes as the shipped library's nexus_synth_model_write for
+ * the same configuration (checked by tests/test_oracle_batched.py), so the
+ * CPU-only legs (bench.py --impl reference) can produce their model file
+ * without loading the CUDA library.  File conventions follow nexus-convert
+ * (tools/nexus-convert/main.rs:190-383): blk.N.* tensor names sorted, [out,in]
+ * shapes, llama.* metadata keys sorted, general.alignment 32.  Element i of a
+ * tensor is a counter-based normal draw: pair p = i/2,
+ * r = splitmix64(splitmix64(seed ^ fnv1a(name)) + p), u1 = ((r>>40)+1)/2^24,
+ * u2 = (r & 0xffffff)/2^24, z = sqrt(-2 ln u1) * (cos|sin)(2 pi u2) for even|odd i. */
+static uint64_t orc_splitmix64(uint64_t x) {
+    x += 0x9e3779b97f4a7c15ull;
+    x = (x ^ (x >> 30)) * 0xbf58476d1ce4e5b9ull;
+    x = (x ^ (x >> 27)) * 0x94d049bb133111ebull;
+    return x ^ (x >> 31);
+}
+
+static uint64_t orc_fnv1a(const char *s) {
+    uint64_t h = 0xcbf29ce484222325ull;
+    for (; *s; s++) {
+        h ^= (unsigned char)*s;
+        h *= 0x100000001b3ull;
+    }
+    return h;
+}
+
+static void orc_gen_normal(uint64_t seed, uint64_t stream, size_t start, size_t count, float stdv,
+                           float *out) {
+    uint64_t base = orc_splitmix64(seed ^ stream);
+    for (size_t k = 0; k < count; k++) {
+        size_t i = start + k;
+        uint64_t r = orc_splitmix64(base + (uint64_t)(i / 2));
+        float u1 = (float)((r >> 40) + 1) * (1.0f / 16777216.0f);
+        float u2 = (float)(r & 0xffffffu) * (1.0f / 16777216.0f);
+        float rad = sqrtf(-2.0f * logf(u1));
+        float ang = 6.28318530717958647692f * u2;
+        float z = (i & 1) ? rad * sinf(ang) : rad * cosf(ang);
+        out[k] = stdv * z;
+    }
+}
+
+typedef struct {
+    char name[96];
+    uint32_t n_dims;
+    uint64_t shape[2];
+    int type;
+    int ones;
+} syn_tensor;
+
+static int syn_cmp(const void *a, const void *b) {
+    return strcmp(((const syn_tensor *)a)->name, ((const syn_tensor *)b)->name);
+}
+
+typedef struct {
+    uint8_t *p;
+    size_t n, cap;
+} syn_buf;
+
+static void sb_put(syn_buf *b, const void *src, size_t n) {
+    if (b->n + n > b->cap) {
+        b->cap = (b->n + n) * 2 + 256;
+        b->p = (uint8_t *)realloc(b->p, b->cap);
+    }
+    memcpy(b->p + b->n, src, n);
+    b->n += n;
+}
+static void sb_u32(syn_buf *b, uint32_t v) { sb_put(b, &v, 4); }
+static void sb_u64(syn_buf *b, uint64_t v) { sb_put(b, &v, 8); }
+static void sb_str(syn_buf *b, const char *s) {
+    sb_u64(b, strlen(s));
+    sb_put(b, s, strlen(s));
+}
+
+typedef struct {
+    const orc_synth_config *cfg;
+    const syn_tensor *t;
+    uint64_t stream;
+    size_t n, drawn, be, bb;
+    uint8_t *buf;
+    int tid, nt;
+} syn_job;
+
+#define SYN_CH 65536
+static void *syn_worker(void *arg) {
+    syn_job *j = (syn_job *)arg;
+    float *vals = (float *)malloc(SYN_CH * sizeof(float));
+    if (!vals) return (void *)1;
+    for (size_t c = (size_t)j->tid; c < j->drawn; c += (size_t)j->nt) {
+        size_t s = c * SYN_CH, cnt = j->n - s < SYN_CH ? j->n - s : SYN_CH;
+        if (j->t->ones) {
+            for (size_t i = 0; i < cnt; i++) vals[i] = 1.0f;
+        } else {
+            orc_gen_normal(j->cfg->seed, j->stream, s, cnt, j->cfg->weight_std, vals);
+        }
+        orc_quantize(j->t->type, vals, cnt, j->buf + s / j->be * j->bb);
+    }
+    free(vals);
+    return NULL;
+}
+
+int orc_synth_write(const char *path, const orc_synth_config *C) {
+    const int fmts[4] = {C->attn_format, C->ffn_format, C->embd_format, C->norm_format};
+    size_t be, bb;
+    if (C->num_heads == 0 || C->hidden_size % C->num_heads) return ORC_E_INVALID;
+    for (int i = 0; i < 4; i++)
+        if (!block_geom(fmts[i], &be, &bb) || fmts[i] == ORC_BF16) return ORC_E_UNSUPPORTED;
+    if (C->head_format >= 0 && (!block_geom(C->head_format, &be, &bb) || C->head_format == ORC_BF16))
+        return ORC_E_UNSUPPORTED;
+    uint64_t H = C->hidden_size, F = C->ff_dim, V = C->vocab_size;
+    uint64_t D = H / C->num_heads, KV = (uint64_t)C->num_kv_heads * D;
+    size_t nts = 3 + (size_t)C->num_layers * 9;
+    syn_tensor *ts = (syn_tensor *)calloc(nts, sizeof(syn_tensor));
+    if (!ts) return ORC_E_NOMEM;
+    size_t k = 0;
+#define SYN_ADD(nm, d0, d1, nd, ty, on)                                     \
+    do {                                                                    \
+        snprintf(ts[k].name, sizeof ts[k].name, "%s", nm);                  \
+        ts[k].n_dims = nd;                                                  \
+        ts[k].shape[0] = d0;                                                \
+        ts[k].shape[1] = d1;                                                \
+        ts[k].type = ty;                                                    \
+        ts[k].ones = on;                                                    \
+        k++;                                                                \
+    } while (0)
+    SYN_ADD("token_embd.weight", V, H, 2, C->embd_format, 0);
+    SYN_ADD("output_norm.weight", H, 0, 1, C->norm_format, 1);
+    if (C->head_format >= 0) SYN_ADD("output.weight", V, H, 2, C->head_format, 0);
+    for (uint32_t l = 0; l < C->num_layers; l++) {
+        char nm[96];
+#define SYN_L(role, d0, d1, nd, ty, on)                        \
+    snprintf(nm, sizeof nm, "blk.%u.%s.weight", l, role);     \
+    SYN_ADD(nm, d0, d1, nd, ty, on)
+        SYN_L("attn_norm", H, 0, 1, C->norm_format, 1);
+        SYN_L("attn_q", H, H, 2, C->attn_format, 0);
+        SYN_L("attn_k", KV, H, 2, C->attn_format, 0);
+        SYN_L("attn_v", KV, H, 2, C->attn_format, 0);
+        SYN_L("attn_output", H, H, 2, C->attn_format, 0);
+        SYN_L("ffn_norm", H, 0, 1, C->norm_format, 1);
+        SYN_L("ffn_gate", F, H, 2, C->ffn_format, 0);
+        SYN_L("ffn_up", F, H, 2, C->ffn_format, 0);
+        SYN_L("ffn_down", H, F, 2, C->ffn_format, 0);
+#undef SYN_L
+    }
+#undef SYN_ADD
+    nts = k;
+    qsort(ts, nts, sizeof(syn_tensor), syn_cmp);
+
+    const uint64_t ALIGN = 32;
+    syn_buf hb = {0};
+    sb_put(&hb, "GGUF", 4);
+    sb_u32(&hb, 3);
+    sb_u64(&hb, nts);
+    sb_u64(&hb, 12);
+    /* metadata in key order; value types: 4 = u32, 6 = f32, 8 = string */
+    sb_str(&hb, "general.alignment"); sb_u32(&hb, 4); sb_u32(&hb, (uint32_t)ALIGN);
+    sb_str(&hb, "general.architecture"); sb_u32(&hb, 8); sb_str(&hb, "llama");
+    sb_str(&hb, "general.name"); sb_u32(&hb, 8); sb_str(&hb, "nexus-synthetic");
+    sb_str(&hb, "llama.attention.head_count"); sb_u32(&hb, 4); sb_u32(&hb, C->num_heads);
+    sb_str(&hb, "llama.attention.head_count_kv"); sb_u32(&hb, 4); sb_u32(&hb, C->num_kv_heads);
+    {
+        float eps = 1e-5f;
+        uint32_t u;
+        memcpy(&u, &eps, 4);
+        sb_str(&hb, "llama.attention.layer_norm_rms_epsilon"); sb_u32(&hb, 6); sb_u32(&hb, u);
+    }
+    sb_str(&hb, "llama.block_count"); sb_u32(&hb, 4); sb_u32(&hb, C->num_layers);
+    sb_str(&hb, "llama.context_length"); sb_u32(&hb, 4); sb_u32(&hb, C->context_length);
+    sb_str(&hb, "llama.embedding_length"); sb_u32(&hb, 4); sb_u32(&hb, C->hidden_size);
+    sb_str(&hb, "llama.feed_forward_length"); sb_u32(&hb, 4); sb_u32(&hb, C->ff_dim);
+    {
+        uint32_t u;
+        memcpy(&u, &C->rope_theta, 4);
+        sb_str(&hb, "llama.rope.freq_base"); sb_u32(&hb, 6); sb_u32(&hb, u);
+    }
+    sb_str(&hb, "llama.vocab_size"); sb_u32(&hb, 4); sb_u32(&hb, C->vocab_size);
+    uint64_t off = 0;
+    uint64_t *sizes = (uint64_t *)calloc(nts, sizeof(uint64_t));
+    for (size_t i = 0; i < nts; i++) {
+        sb_str(&hb, ts[i].name);
+        sb_u32(&hb, ts[i].n_dims);
+        for (uint32_t d = 0; d < ts[i].n_dims; d++) sb_u64(&hb, ts[i].shape[d]);
+        sb_u32(&hb, (uint32_t)ts[i].type);
+        sb_u64(&hb, off);
+        uint64_t n = ts[i].shape[0] * (ts[i].n_dims > 1 ? ts[i].shape[1] : 1);
+        sizes[i] = orc_type_size(ts[i].type, n);
+        off += (sizes[i] + ALIGN - 1) / ALIGN * ALIGN;
+    }
+    while (hb.n % ALIGN) {
+        uint8_t z = 0;
+        sb_put(&hb, &z, 1);
+    }
+    int rc = ORC_OK;
+    FILE *fp = fopen(path, "wb");
+    if (!fp) rc = ORC_E_IO;
+    if (!rc && fwrite(hb.p, 1, hb.n, fp) != hb.n) rc = ORC_E_IO;
+    int threads = C->threads > 0 ? C->threads : (int)sysconf(_SC_NPROCESSORS_ONLN);
+    if (threads < 1) threads = 1;
+    if (threads > 256) threads = 256;
+    for (size_t i = 0; !rc && i < nts; i++) {
+        const syn_tensor *t = &ts[i];
+        size_t n = (size_t)(t->shape[0] * (t->n_dims > 1 ? t->shape[1] : 1));
+        size_t padded = (size_t)((sizes[i] + ALIGN - 1) / ALIGN * ALIGN);
+        uint8_t *buf = (uint8_t *)calloc(padded ? padded : 1, 1);
+        if (!buf) {
+            rc = ORC_E_NOMEM;
+            break;
+        }
+        block_geom(t->type, &be, &bb);
+        size_t nchunks = (n + SYN_CH - 1) / SYN_CH;
+        size_t drawn = C->repeat_chunks ? (nchunks < C->repeat_chunks ? nchunks : C->repeat_chunks) : nchunks;
+        int nt = (size_t)threads < drawn ? threads : (int)drawn;
+        if (nt < 1) nt = 1;
+        pthread_t tid[256];
+        syn_job jobs[256];
+        for (int w = 0; w < nt; w++) {
+            jobs[w] = (syn_job){C, t, orc_fnv1a(t->name), n, drawn, be, bb, buf, w, nt};
+            pthread_create(&tid[w], NULL, syn_worker, &jobs[w]);
+        }
+        for (int w = 0; w < nt; w++) {
+            void *ret;
+            pthread_join(tid[w], &ret);
+            if (ret) rc = ORC_E_NOMEM;
+        }
+        for (size_t c = drawn; c < nchunks; c++) {
+            size_t s = c * SYN_CH, cnt = n - s < SYN_CH ? n - s : SYN_CH, src = (c % drawn) * SYN_CH;
+            memcpy(buf + s / be * bb, buf + src / be * bb, cnt / be * bb);
+        }
+        if (!rc && fwrite(buf, 1, padded, fp) != padded) rc = ORC_E_IO;
+        free(buf);
+    }
+    if (fp && fclose(fp) != 0) rc = ORC_E_IO;
+    free(sizes);
+    free(hb.p);
+    free(ts);
+    return rc;
+}

@@ -143,6 +143,24 @@ size_t orc_model_seq_len(const orc_model *m, uint32_t layer);
 /* hidden state after the last decode (before the output norm), hidden_size floats */
 const float *orc_model_last_hidden(const orc_model *m);
 
+/* prefill with a layer-major schedule (every token through layer l before
+ * layer l+1): the same logits and KV cache bits as orc_model_prefill, much
+ * faster for long prompts.  n must not exceed max_seq_len. */
+int orc_model_prefill_batched(orc_model *m, const uint32_t *tokens, size_t n, float *logits);
+
+/* ---- seeded synthetic GGUF writer (same bytes as nexus_synth_model_write) ---- */
+typedef struct {
+    uint32_t num_layers, hidden_size, num_heads, num_kv_heads, ff_dim, vocab_size;
+    uint32_t context_length;
+    float rope_theta;
+    float weight_std;
+    uint64_t seed;
+    int attn_format, ffn_format, embd_format, head_format, norm_format;
+    int threads;
+    uint32_t repeat_chunks;
+} orc_synth_config;
+int orc_synth_write(const char *path, const orc_synth_config *cfg);
+
 #ifdef __cplusplus
 }
 #endif

@@ -20,6 +20,15 @@ F32, F16, Q4_0, Q8_0, Q2_K, Q4_K, BF16 = 0, 1, 2, 8, 10, 12, 28
 ORC_OK = 0
 
 
+class SynthConfig(C.Structure):
+    _fields_ = [("num_layers", C.c_uint32), ("hidden_size", C.c_uint32), ("num_heads", C.c_uint32),
+                ("num_kv_heads", C.c_uint32), ("ff_dim", C.c_uint32), ("vocab_size", C.c_uint32),
+                ("context_length", C.c_uint32), ("rope_theta", C.c_float), ("weight_std", C.c_float),
+                ("seed", C.c_uint64), ("attn_format", C.c_int), ("ffn_format", C.c_int), ("embd_format", C.c_int),
+                ("head_format", C.c_int), ("norm_format", C.c_int), ("threads", C.c_int),
+                ("repeat_chunks", C.c_uint32)]
+
+
 class ModelInfo(C.Structure):
     _fields_ = [("num_layers", C.c_uint32), ("hidden_size", C.c_uint32), ("ff_dim", C.c_uint32),
                 ("num_heads", C.c_uint32), ("num_kv_heads", C.c_uint32), ("head_dim", C.c_uint32),
@@ -75,6 +84,8 @@ def load() -> C.CDLL:
             "orc_model_generate": (C.c_int, [P, P, C.c_size_t, C.c_size_t, P]),
             "orc_model_seq_len": (C.c_size_t, [P, C.c_uint32]),
             "orc_model_last_hidden": (P, [P]),
+            "orc_model_prefill_batched": (C.c_int, [P, P, C.c_size_t, P]),
+            "orc_synth_write": (C.c_int, [C.c_char_p, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(lib, name)
@@ -82,6 +93,24 @@ def load() -> C.CDLL:
             fn.argtypes = args
         _lib = lib
     return _lib
+
+
+def write_synthetic_model(path: str, *, num_layers: int, hidden_size: int, num_heads: int, num_kv_heads: int,
+                          ff_dim: int, vocab_size: int, context_length: int, rope_theta: float,
+                          attn_format: int, ffn_format: int, embd_format: int, head_format: int,
+                          norm_format: int, weight_std: float = 0.02, seed: int = 0, threads: int = 0,
+                          repeat_chunks: int = 0) -> None:
+    """The seeded synthetic GGUF, byte-identical to the CUDA library's writer
+    (so CPU-only runs need not load that library)."""
+    cfg = SynthConfig(num_layers=num_layers, hidden_size=hidden_size, num_heads=num_heads,
+                      num_kv_heads=num_kv_heads, ff_dim=ff_dim, vocab_size=vocab_size,
+                      context_length=context_length, rope_theta=rope_theta, weight_std=weight_std, seed=seed,
+                      attn_format=attn_format, ffn_format=ffn_format, embd_format=embd_format,
+                      head_format=head_format, norm_format=norm_format, threads=threads,
+                      repeat_chunks=repeat_chunks)
+    rc = load().orc_synth_write(str(path).encode(), C.byref(cfg))
+    if rc != ORC_OK:
+        raise RuntimeError(f"oracle synthetic writer failed: {rc}")
 
 
 def _p(a: np.ndarray) -> int:
@@ -237,6 +266,15 @@ class Model:
         rc = self.lib.orc_model_prefill(self.h, _p(t) if t.size else None, t.size, _p(out))
         if rc != ORC_OK:
             raise RuntimeError(f"oracle prefill failed: {rc}")
+        return out
+
+    def prefill_batched(self, tokens) -> np.ndarray:
+        """prefill with the layer-major schedule: same bits as prefill()."""
+        t = np.ascontiguousarray(np.asarray(tokens, np.uint32))
+        out = np.zeros(self.info.vocab_rows, np.float32)
+        rc = self.lib.orc_model_prefill_batched(self.h, _p(t) if t.size else None, t.size, _p(out))
+        if rc != ORC_OK:
+            raise RuntimeError(f"oracle batched prefill failed: {rc}")
         return out
 
     def generate(self, prompt, max_tokens: int) -> list:

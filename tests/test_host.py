@@ -96,20 +96,36 @@ def test_synthetic_weights_are_seeded_normal(nb, oracle, tmp_path):
 
 def test_bench_reference_arm_prints_one_contract_line():
     """`bench.py --impl reference` (the oracle port on the host cores) prints one
-    JSON line with the contract's keys; the tiny config keeps it to seconds."""
+    JSON line with the contract's keys and the GPU arm's metric string, and
+    never loads the CUDA library (its model file comes from the oracle's
+    writer); the tiny config keeps it to seconds."""
     import json
     import subprocess
     import sys
     root = Path(__file__).resolve().parents[1]
-    r = subprocess.run([sys.executable, str(root / "bench.py"), "--impl", "reference", "--config", "tiny",
-                        "--steps", "2", "--warmup", "3"], capture_output=True, text=True, timeout=600, cwd=root)
+    probe = ("import runpy, sys\n"
+             "sys.argv = ['bench.py', '--impl', 'reference', '--config', 'tiny', '--steps', '2', '--warmup', '4']\n"
+             "try:\n    runpy.run_path('bench.py', run_name='__main__')\nexcept SystemExit as e:\n    rc = e.code\n"
+             "maps = open('/proc/self/maps').read()\n"
+             "print('LOADED_CUDA_LIB' if 'libnexus_cuda' in maps else 'NO_CUDA_LIB')\n"
+             "print('LOADED_ORACLE' if 'liboracle' in maps else 'NO_ORACLE')\n"
+             "sys.exit(rc or 0)\n")
+    r = subprocess.run([sys.executable, "-c", probe], capture_output=True, text=True, timeout=600, cwd=root)
     assert r.returncode == 0, r.stderr[-2000:]
     lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
     assert len(lines) == 1
+    assert "NO_CUDA_LIB" in r.stdout and "LOADED_ORACLE" in r.stdout, r.stdout
     d = json.loads(lines[0])
     for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
                 "scaling", "vs_baseline", "dtype", "data", "config", "e2e", "cpu_baseline"):
         assert key in d, key
-    assert d["impl"] == "reference" and d["value"] > 0 and d["warmup"] == 3
+    assert d["impl"] == "reference" and d["value"] > 0 and d["warmup"] == 4
     assert d["cpu_baseline"]["kind"] in ("port", "reference") and d["cpu_baseline"]["cores"] >= 1
+    assert d["cpu_baseline"]["single_core"]["cores"] == 1 and d["cpu_baseline"]["single_core"]["value"] > 0
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
+    # the GPU arm prints the same metric string (the driver pairs the two lines by it)
+    sys.path.insert(0, str(root))
+    import bench
+    assert d["metric"] == bench.METRIC
+    src = (root / "bench.py").read_text()
+    assert src.count('"metric": METRIC') == 2 and 'line["metric"]' not in src
