@@ -384,7 +384,8 @@ def run_workload_p(args):
     64 requests with context lengths uniform in [1024, 8192] (seed 2) of random
     token ids (seed 1 + request), then `steps` continuous decode steps that
     advance all 64 requests by one token each through nexus_cuda_decode_batch,
-    with scheduler-style 16-token page lists (src/scheduler.rs:333-361)."""
+    with scheduler-style 16-token page lists (src/scheduler.rs:333-361): every
+    request's KV lives in the pages its list names."""
     import torch
     import nexus_b200 as nb
     n_req, gen = 64, args.steps
@@ -397,13 +398,16 @@ def run_workload_p(args):
     toks, pos, pages, next_page = [], [], [], 0
     t0 = time.perf_counter()
     for r in range(n_req):
+        # the scheduler's allocation: ceil((prompt + max_tokens) / 16) ids from a
+        # running counter, bound before the prefill writes the request's KV
+        npg = (int(ctx[r]) + gen + args.warmup + 15) // 16
+        pages.append(list(range(next_page, next_page + npg)))
+        next_page += npg
+        eng.seq_set_pages(r, pages[r])
         prompt = np.random.default_rng(SEED_PROMPT + r).integers(0, V, int(ctx[r])).tolist()
         _, t = eng.prefill(prompt, seq_id=r, want_logits=False)
         toks.append(t)
         pos.append(int(ctx[r]))
-        npg = (int(ctx[r]) + gen + args.warmup + 15) // 16
-        pages.append(list(range(next_page, next_page + npg)))
-        next_page += npg
     torch.cuda.synchronize()
     prefill_s = time.perf_counter() - t0
 

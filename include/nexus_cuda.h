@@ -86,8 +86,10 @@ typedef struct {
     uint32_t kv_bits_v;    /* packed value bits (KvQuantType::val_bits, src/quant/mod.rs:150) */
     uint32_t max_batch;    /* largest decode_batch the model will see (>= 1) */
     uint32_t max_seq_len;  /* 0 = GGUF llama.context_length (src/engine/mod.rs:561) */
-    uint32_t page_tokens;  /* KV page size in tokens; 0 = 16 (src/scheduler.rs page size) */
-    uint32_t max_pages;    /* KV pages to reserve per rank; 0 = max_batch * pages(max_seq_len) */
+    uint32_t page_tokens;  /* KV page size in tokens, a power of two <= 4096; 0 = 16 (the
+                              scheduler's page size, src/scheduler.rs:333-361) */
+    uint32_t max_pages;    /* KV pages in the pool per rank; 0 = max_batch * ceil(max_seq_len /
+                              page_tokens) (every sequence can hold max_seq_len tokens) */
     uint32_t flags;        /* NEXUS_CFG_* */
 } nexus_cuda_config;
 
@@ -254,10 +256,27 @@ int nexus_cuda_prefill(nexus_cuda_model *m, uint32_t seq_id, const uint32_t *tok
 int nexus_cuda_generate(nexus_cuda_model *m, uint32_t seq_id, const uint32_t *prompt, size_t n,
                         size_t max_tokens, uint32_t *out);
 
+/* KV pages.  The KV cache of every layer is a pool of max_pages pages of
+ * page_tokens tokens (nexus_cuda_config); token t of a sequence lives in page
+ * page_ids[t / page_tokens] of its list, at slot t % page_tokens.  A sequence
+ * without a list uses the library's own pages [seq_id * P, (seq_id + 1) * P),
+ * P = ceil(max_seq_len / page_tokens), when the pool has them.  A page belongs
+ * to at most one sequence.
+ *
+ * Binds a request's page list (Scheduler::allocate_kv_pages,
+ * src/scheduler.rs:333-361, ceil((prompt + max_tokens) / 16) ids) to seq_id
+ * before its prefill.  The pages of tokens already cached must keep their
+ * place (the list may only extend or end after them); ids must be below
+ * max_pages and listed once; a page of another sequence is refused.
+ * n_pages = 0 releases the sequence's pages and clears its cache. */
+int nexus_cuda_seq_set_pages(nexus_cuda_model *m, uint32_t seq_id, const uint32_t *page_ids,
+                             uint32_t n_pages);
+
 /* One decode step for a batch of sequences (Scheduler::decode_batch items,
- * src/scheduler.rs:108-115,207-229).  page_ids lists the sequence's KV pages
- * (Scheduler::allocate_kv_pages, src/scheduler.rs:333-361); NULL = the
- * library's own per-sequence pages. */
+ * src/scheduler.rs:108-115,207-229).  page_ids (n_pages entries) is the
+ * sequence's KV page list, ScheduledDecode.kv_pages: it is bound as by
+ * nexus_cuda_seq_set_pages and must cover the token this step writes; NULL
+ * keeps the sequence's current list. */
 typedef struct {
     uint32_t seq_id;
     uint32_t token;

@@ -125,6 +125,7 @@ SIGNATURES = [
     ("nexus_cuda_model_get_info", C.c_int, [P, C.POINTER(ModelInfo)]),
     ("nexus_cuda_seq_reset", C.c_int, [P, C.c_uint32]),
     ("nexus_cuda_seq_len", C.c_int, [P, C.c_uint32, C.POINTER(C.c_uint32)]),
+    ("nexus_cuda_seq_set_pages", C.c_int, [P, C.c_uint32, P, C.c_uint32]),
     ("nexus_cuda_decode", C.c_int, [P, C.c_uint32, C.c_uint32, C.c_uint32, P, C.POINTER(C.c_uint32)]),
     ("nexus_cuda_prefill", C.c_int, [P, C.c_uint32, P, C.c_size_t, P, C.POINTER(C.c_uint32)]),
     ("nexus_cuda_generate", C.c_int, [P, C.c_uint32, P, C.c_size_t, C.c_size_t, P]),

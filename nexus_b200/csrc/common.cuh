@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "kernels.h"
+
 namespace nx {
 
 constexpr int kWarp = 32;
@@ -110,6 +112,13 @@ __device__ __forceinline__ void tma_load_1d_w(void *dst, const void *src, unsign
             smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
+}
+
+// Physical slot of token `tok` of cache row `sid` (KvPages in kernels.h).
+__device__ __forceinline__ size_t kv_phys(const KvPages &pg, uint32_t sid, uint32_t tok) {
+    if (!pg.table) return tok;
+    const uint32_t page = __ldg(pg.table + (size_t)sid * pg.per_seq + (tok >> pg.shift));
+    return ((size_t)page << pg.shift) | (tok & ((1u << pg.shift) - 1u));
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -649,8 +649,6 @@ extern "C" int nexus_cuda_execute(nexus_cuda_backend *b, const nexus_op *op) {
         kp.vp_min = mins + 2;
         kp.vp_scale = mins + 3;
         kp.pk_bpt_k = kp.pk_bpt_v = bpt;
-        kp.pk_seq_stride_k = kp.pk_seq_stride_v = bpt;
-        kp.pk_seq_tokens = 1;
         kp.seqs = ds;
         kp.seq_ids = sid;
         e = launch_kv_pack(kp, st);
@@ -704,7 +702,6 @@ extern "C" int nexus_cuda_execute(nexus_cuda_backend *b, const nexus_op *op) {
         p.scale = op->scale != 0.0f ? op->scale : 1.0f / sqrtf((float)hd);
         p.k_cache = (const float *)B.d;
         p.v_cache = (const float *)Cc.d;
-        p.seq_stride = 0;
         p.seqs = ds;
         p.seq_ids = sid;
         p.kv_dim = (int)kv_dim;
@@ -774,7 +771,6 @@ extern "C" int nexus_cuda_execute(nexus_cuda_backend *b, const nexus_op *op) {
         p.vp_scale = p.vp_min + seq;
         p.pk_bpt_k = bpk;
         p.pk_bpt_v = bpv;
-        p.pk_seq_tokens = seq;
         p.seqs = ds;
         p.seq_ids = sid;
         p.kv_dim = (int)kv_dim;
@@ -937,9 +933,28 @@ static constexpr int kMaxChunk = 256;  // tokens per fused step (prefill chunk, 
 struct Layer {
     float *attn_norm = nullptr, *ffn_norm = nullptr;
     Mat qkv, o, gateup, down;
-    float *k_cache = nullptr, *v_cache = nullptr;  // float KV [max_batch][max_seq][kv_dim]
-    uint8_t *kp = nullptr, *vp = nullptr;          // packed KV [max_batch][max_seq][bpt]
+    // KV page pool of this layer, [pool_pages * page_tokens] physical token
+    // slots: float rows of kv_dim, or packed rows of bpt bytes plus a min and
+    // a scale per slot
+    float *k_cache = nullptr, *v_cache = nullptr;
+    uint8_t *kp = nullptr, *vp = nullptr;
     float *kmin = nullptr, *kscale = nullptr, *vmin = nullptr, *vscale = nullptr;
+};
+
+// Host view of the KV pages (Scheduler::allocate_kv_pages,
+// src/scheduler.rs:333-361, hands each request ceil((prompt + max_tokens)/16)
+// page ids; ScheduledDecode carries them, :108-115).  Every sequence row has
+// a page list: the one its caller bound, or else the library's own pages
+// [sid * per_seq, (sid + 1) * per_seq).  Each page belongs to at most one
+// sequence.  The device table holds the same lists; rows are uploaded before
+// the next step after they change.
+struct PageMap {
+    uint32_t page_tokens = 16, shift = 4, per_seq = 0, pool = 0;
+    std::vector<uint32_t> table;     // [rows][per_seq]
+    std::vector<uint32_t> valid;     // usable leading entries of each row
+    std::vector<uint8_t> caller;     // 1: the row holds a caller's list
+    std::vector<int32_t> owner;      // [pool] sequence holding the page, or -1
+    std::vector<uint8_t> dirty;      // rows to upload
 };
 
 struct nexus_cuda_model {
@@ -966,6 +981,8 @@ struct nexus_cuda_model {
     DevSeq *h_seqs = nullptr;
     uint32_t *h_seq_ids = nullptr, *h_out_tokens = nullptr;
     std::vector<uint32_t> seq_len;
+    PageMap pm;
+    uint32_t *page_table = nullptr;   // device copy of pm.table
     uint32_t max_seq = 0, max_batch = 1, bits_k = 0, bits_v = 0;
     size_t bpt_k = 0, bpt_v = 0;
     int nsplit[kMaxChunk + 1] = {};     // attention slices per (sequence, KV head), float cache
@@ -1105,6 +1122,25 @@ static int model_load(nexus_cuda_backend *b, const char *path, nexus_cuda_model 
     m->max_batch = b->cfg.max_batch;
     m->bits_k = b->cfg.kv_bits_k;
     m->bits_v = b->cfg.kv_bits_v;
+    {
+        // KV pages: page_tokens a power of two, every sequence row able to
+        // list max_seq_len tokens, a pool of max_pages pages
+        PageMap &pm = m->pm;
+        pm.page_tokens = b->cfg.page_tokens ? b->cfg.page_tokens : 16;
+        if (pm.page_tokens > 4096 || (pm.page_tokens & (pm.page_tokens - 1)))
+            return set_err(b, NEXUS_E_INVALID, "page_tokens must be a power of two <= 4096");
+        pm.shift = 0;
+        while ((1u << pm.shift) < pm.page_tokens) pm.shift++;
+        pm.per_seq = (m->max_seq + pm.page_tokens - 1) / pm.page_tokens;
+        const uint64_t pool = b->cfg.max_pages ? (uint64_t)b->cfg.max_pages : (uint64_t)m->max_batch * pm.per_seq;
+        if (pool == 0 || pool > 0x7fffffffull) return set_err(b, NEXUS_E_INVALID, "bad KV page pool size");
+        pm.pool = (uint32_t)pool;
+        pm.table.assign((size_t)m->max_batch * pm.per_seq, 0u);
+        pm.valid.assign(m->max_batch, 0u);
+        pm.caller.assign(m->max_batch, 0);
+        pm.owner.assign(pm.pool, -1);
+        pm.dirty.assign(m->max_batch, 0);
+    }
     m->use_graph = !(b->cfg.flags & NEXUS_CFG_NO_GRAPH);
     m->use_pdl = !(b->cfg.flags & NEXUS_CFG_NO_PDL);
     cudaSetDevice(b->device);
@@ -1231,7 +1267,7 @@ static int model_load(nexus_cuda_backend *b, const char *path, nexus_cuda_model 
         weight_bytes += L.qkv.bytes + L.o.bytes + L.gateup.bytes + L.down.bytes;
         if (l == 0) I.body_format = tq->type;
         // KV cache (KvCache::new(num_kv_heads*head_dim, max_seq_len, kv_quant), :593-597)
-        const size_t toks = (size_t)m->max_batch * m->max_seq;
+        const size_t toks = (size_t)m->pm.pool * m->pm.page_tokens;  // physical slots of the page pool
         if (m->bits_k == 0) {
             NX_CUDA(b, malloc_tracked(m, &L.k_cache, toks * m->kvd_l));
             NX_CUDA(b, malloc_tracked(m, &L.v_cache, toks * m->kvd_l));
@@ -1280,10 +1316,14 @@ static int model_load(nexus_cuda_backend *b, const char *path, nexus_cuda_model 
     NX_CUDA(b, malloc_tracked(m, &m->logits, (size_t)MC * (m->has_head ? m->v_l : I.vocab_rows)));
     if (tp > 1) NX_CUDA(b, malloc_tracked(m, &m->logits_gather, (size_t)tp * MC * m->v_l));
     const int G = (int)(Hq / Hkv);
-    // context slices of >= 64 tokens, at most 64 per (sequence, KV head); the
-    // kernel uses only as many as the current context needs
-    int max_split = std::max(1, std::min(64, (int)((m->max_seq + 63) / 64)));
-    for (int mm = 1; mm <= MC; mm++) m->nsplit[mm] = max_split;
+    // context slices of >= 16 tokens, at most 64 per (sequence, KV head):
+    // enough for about two CTAs per SM over the step's sequences and KV heads
+    // (the kernel uses fewer when the context is short)
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, b->device);
+    int max_split = std::max(1, std::min(64, (int)((m->max_seq + 15) / 16)));
+    for (int mm = 1; mm <= MC; mm++)
+        m->nsplit[mm] = std::max(1, std::min(max_split, (2 * sms + mm * (int)hkv_l - 1) / (mm * (int)hkv_l)));
     // the packed-cache kernel: about 8 CTAs per SM over the whole step (its
     // CTAs stream whole 64-token tiles and need no more slices than that)
     for (int mm = 1; mm <= MC; mm++)
@@ -1310,12 +1350,112 @@ static int model_load(nexus_cuda_backend *b, const char *path, nexus_cuda_model 
     NX_CUDA(b, cudaEventCreate(&m->ev0));
     NX_CUDA(b, cudaEventCreate(&m->ev1));
     m->seq_len.assign(m->max_batch, 0);
+    NX_CUDA(b, malloc_tracked(m, &m->page_table, m->pm.table.size()));
+    NX_CUDA(b, cudaMemset(m->page_table, 0, m->pm.table.size() * 4));
     NX_CUDA(b, cudaDeviceSynchronize());
     guard.release();
     backend_retain(b);
     m->retained = true;
     *out = m;
     return NEXUS_OK;
+}
+
+// ---------------------------------------------------------------------------
+// KV pages
+// ---------------------------------------------------------------------------
+static KvPages dev_pages(const nexus_cuda_model *m) { return KvPages{m->page_table, m->pm.per_seq, m->pm.shift}; }
+
+static void pages_release(nexus_cuda_model *m, uint32_t sid) {
+    PageMap &pm = m->pm;
+    uint32_t *row = pm.table.data() + (size_t)sid * pm.per_seq;
+    for (uint32_t i = 0; i < pm.valid[sid]; i++)
+        if (pm.owner[row[i]] == (int32_t)sid) pm.owner[row[i]] = -1;
+    pm.valid[sid] = 0;
+    pm.caller[sid] = 0;
+}
+
+// Bind ids[0..n) as the page list of sequence sid.  Pages holding the
+// sequence's cached tokens must stay where they are; every page must be in
+// the pool, listed once and free or already this sequence's.
+static int pages_bind(nexus_cuda_model *m, uint32_t sid, const uint32_t *ids, uint32_t n) {
+    PageMap &pm = m->pm;
+    uint32_t *row = pm.table.data() + (size_t)sid * pm.per_seq;
+    if (pm.caller[sid] && pm.valid[sid] == n && std::equal(ids, ids + n, row)) return NEXUS_OK;  // unchanged
+    if (n > pm.per_seq)
+        return set_err(m->b, NEXUS_E_INVALID, "page list longer than max_seq_len / page_tokens entries");
+    const uint32_t cached = (m->seq_len[sid] + pm.page_tokens - 1) / pm.page_tokens;
+    if (n < cached) return set_err(m->b, NEXUS_E_INVALID, "page list shorter than the sequence's cached tokens");
+    for (uint32_t i = 0; i < cached; i++)
+        if (ids[i] != row[i])
+            return set_err(m->b, NEXUS_E_INVALID,
+                           "page list moves cached tokens (its first pages must be the ones the sequence was written "
+                           "to; reset the sequence to rebind)");
+    std::vector<uint32_t> sorted(ids, ids + n);
+    std::sort(sorted.begin(), sorted.end());
+    for (uint32_t i = 0; i < n; i++) {
+        if (sorted[i] >= pm.pool) return set_err(m->b, NEXUS_E_INVALID, "page id beyond the KV page pool (max_pages)");
+        if (i && sorted[i] == sorted[i - 1]) return set_err(m->b, NEXUS_E_INVALID, "page id listed twice");
+        const int32_t o = pm.owner[sorted[i]];
+        if (o >= 0 && o != (int32_t)sid)
+            return set_err(m->b, NEXUS_E_INVALID,
+                           "page " + std::to_string(sorted[i]) + " belongs to sequence " + std::to_string(o));
+    }
+    for (uint32_t i = 0; i < pm.valid[sid]; i++)
+        if (pm.owner[row[i]] == (int32_t)sid) pm.owner[row[i]] = -1;
+    std::copy(ids, ids + n, row);
+    for (uint32_t i = 0; i < n; i++) pm.owner[ids[i]] = (int32_t)sid;
+    pm.valid[sid] = n;
+    pm.caller[sid] = 1;
+    pm.dirty[sid] = 1;
+    return NEXUS_OK;
+}
+
+// A sequence without a caller's list uses the library's pages
+// [sid * per_seq, (sid + 1) * per_seq) of the pool (bound on first use).
+static int pages_default(nexus_cuda_model *m, uint32_t sid) {
+    PageMap &pm = m->pm;
+    if (pm.caller[sid] || pm.valid[sid]) return NEXUS_OK;
+    const uint64_t first = (uint64_t)sid * pm.per_seq;
+    const uint32_t n = first >= pm.pool ? 0u : (uint32_t)std::min<uint64_t>(pm.per_seq, pm.pool - first);
+    uint32_t *row = pm.table.data() + (size_t)sid * pm.per_seq;
+    for (uint32_t i = 0; i < n; i++) {
+        const int32_t o = pm.owner[first + i];
+        if (o >= 0 && o != (int32_t)sid)
+            return set_err(m->b, NEXUS_E_INVALID,
+                           "the library's pages of sequence " + std::to_string(sid) + " are bound to sequence " +
+                               std::to_string(o) + "; give this sequence a page list");
+    }
+    for (uint32_t i = 0; i < n; i++) {
+        row[i] = (uint32_t)(first + i);
+        pm.owner[first + i] = (int32_t)sid;
+    }
+    pm.valid[sid] = n;
+    pm.dirty[sid] = 1;
+    return NEXUS_OK;
+}
+
+// The sequence's pages must cover `tokens` tokens.
+static int pages_cover(nexus_cuda_model *m, uint32_t sid, uint64_t tokens) {
+    const PageMap &pm = m->pm;
+    if (tokens > (uint64_t)pm.valid[sid] * pm.page_tokens)
+        return set_err(m->b, NEXUS_E_INVALID,
+                       "the KV pages of sequence " + std::to_string(sid) + " hold " +
+                           std::to_string((uint64_t)pm.valid[sid] * pm.page_tokens) + " tokens; the step needs " +
+                           std::to_string(tokens));
+    return NEXUS_OK;
+}
+
+static cudaError_t pages_upload(nexus_cuda_model *m) {
+    PageMap &pm = m->pm;
+    for (uint32_t r = 0; r < m->max_batch; r++) {
+        if (!pm.dirty[r]) continue;
+        const size_t off = (size_t)r * pm.per_seq;
+        cudaError_t e = cudaMemcpyAsync(m->page_table + off, pm.table.data() + off, (size_t)pm.per_seq * 4,
+                                        cudaMemcpyHostToDevice, m->b->stream);
+        if (e != cudaSuccess) return e;
+        pm.dirty[r] = 0;
+    }
+    return cudaSuccess;
 }
 
 // Optional per-kernel timing of enqueue_step (profile mode only, never in a graph).
@@ -1449,7 +1589,7 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         g.qkv.rope_sin = m->rope_sin;
         g.qkv.k_cache = L.k_cache;
         g.qkv.v_cache = L.v_cache;
-        g.qkv.seq_stride = (size_t)m->max_seq * kv_dim;
+        g.qkv.pages = dev_pages(m);
         g.qkv.kv_scratch = packed ? m->kv_scratch : nullptr;
         g.qkv.seqs = m->seqs;
         g.qkv.seq_ids = m->seq_ids;
@@ -1471,9 +1611,7 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
             kp.vp_scale = L.vscale;
             kp.pk_bpt_k = m->bpt_k;
             kp.pk_bpt_v = m->bpt_v;
-            kp.pk_seq_stride_k = m->bpt_k * m->max_seq;
-            kp.pk_seq_stride_v = m->bpt_v * m->max_seq;
-            kp.pk_seq_tokens = m->max_seq;
+            kp.pages = dev_pages(m);
             kp.seqs = m->seqs;
             kp.seq_ids = m->seq_ids;
             kp.pdl = pdl;
@@ -1499,7 +1637,7 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         a.scale = 1.0f / sqrtf((float)D);
         a.k_cache = L.k_cache;
         a.v_cache = L.v_cache;
-        a.seq_stride = (size_t)m->max_seq * kv_dim;
+
         a.bits_k = (int)m->bits_k;
         a.bits_v = (int)m->bits_v;
         a.kp_data = L.kp;
@@ -1510,9 +1648,7 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         a.vp_scale = L.vscale;
         a.pk_bpt_k = m->bpt_k;
         a.pk_bpt_v = m->bpt_v;
-        a.pk_seq_stride_k = m->bpt_k * m->max_seq;
-        a.pk_seq_stride_v = m->bpt_v * m->max_seq;
-        a.pk_seq_tokens = m->max_seq;
+        a.pages = dev_pages(m);
         a.seqs = m->seqs;
         a.seq_ids = m->seq_ids;
         a.kv_dim = kv_dim;
@@ -1679,6 +1815,7 @@ static int host_step(nexus_cuda_model *m, const StepItem *items, int mc, float *
         m->h_seqs[t] = s;
         m->h_seq_ids[t] = items[t].sid;
     }
+    NX_CUDA(b, pages_upload(m));
     NX_CUDA(b, cudaMemcpyAsync(m->seqs, m->h_seqs, mc * sizeof(DevSeq), cudaMemcpyHostToDevice, st));
     NX_CUDA(b, cudaMemcpyAsync(m->seq_ids, m->h_seq_ids, mc * 4, cudaMemcpyHostToDevice, st));
     int rc = run_step(m, mc);
@@ -1745,11 +1882,29 @@ extern "C" int nexus_cuda_seq_len(nexus_cuda_model *m, uint32_t seq_id, uint32_t
     return NEXUS_OK;
 }
 
+// The sequence can take `add` more tokens: within max_seq_len and inside its
+// KV pages (the library's own pages are bound here when it has no list).
+extern "C" int nexus_cuda_seq_set_pages(nexus_cuda_model *m, uint32_t seq_id, const uint32_t *page_ids,
+                                        uint32_t n_pages) {
+    if (!m || (n_pages && !page_ids)) return set_err(m ? m->b : nullptr, NEXUS_E_INVALID, "NULL argument");
+    if (seq_id >= m->max_batch) return set_err(m->b, NEXUS_E_INVALID, "bad sequence id");
+    std::lock_guard<std::mutex> lk(m->b->mu);
+    if (n_pages == 0) {
+        // the request is done: its cache is cleared and its pages go back to the pool
+        m->seq_len[seq_id] = 0;
+        pages_release(m, seq_id);
+        return NEXUS_OK;
+    }
+    return pages_bind(m, seq_id, page_ids, n_pages);
+}
+
 static int check_slot(nexus_cuda_model *m, uint32_t sid, uint32_t add) {
     if (sid >= m->max_batch) return set_err(m->b, NEXUS_E_INVALID, "bad sequence id");
     if ((uint64_t)m->seq_len[sid] + add > m->max_seq)
         return set_err(m->b, NEXUS_E_INVALID, "KV cache full: the backend does not shift the cache (raise max_seq_len)");
-    return NEXUS_OK;
+    int rc = pages_default(m, sid);
+    if (!rc) rc = pages_cover(m, sid, (uint64_t)m->seq_len[sid] + add);
+    return rc;
 }
 
 static int check_position(nexus_cuda_model *m, uint64_t position) {
@@ -1843,6 +1998,7 @@ extern "C" int nexus_cuda_generate(nexus_cuda_model *m, uint32_t seq_id, const u
     m->h_seqs[0] = s;
     m->h_seq_ids[0] = seq_id;
     cudaStream_t st = b->stream;
+    NX_CUDA(b, pages_upload(m));
     NX_CUDA(b, cudaMemcpyAsync(m->seqs, m->h_seqs, sizeof(DevSeq), cudaMemcpyHostToDevice, st));
     NX_CUDA(b, cudaMemcpyAsync(m->seq_ids, m->h_seq_ids, 4, cudaMemcpyHostToDevice, st));
     uint32_t *ring = nullptr;
@@ -1882,18 +2038,23 @@ extern "C" int nexus_cuda_decode_batch(nexus_cuda_model *m, const nexus_decode_i
     std::vector<bool> seen(m->max_batch, false);
     for (size_t i = 0; i < n; i++) {
         const uint32_t sid = items[i].seq_id;
-        int rc = check_slot(m, sid, 1);
-        if (!rc) rc = check_position(m, items[i].position);
+        if (sid >= m->max_batch) return set_err(m->b, NEXUS_E_INVALID, "bad sequence id");
+        int rc = check_position(m, items[i].position);
         if (rc) return rc;
         if (seen[sid]) return set_err(m->b, NEXUS_E_INVALID, "a sequence appears twice in one decode batch");
         seen[sid] = true;
-        if (items[i].page_ids && items[i].n_pages) {
-            // pages are the library's own per-sequence ranges; a caller-provided
-            // table must cover the slot being written
-            const uint32_t pt = m->b->cfg.page_tokens ? m->b->cfg.page_tokens : 16;
-            if ((uint64_t)items[i].n_pages * pt < (uint64_t)m->seq_len[sid] + 1)
-                return set_err(m->b, NEXUS_E_INVALID, "page list shorter than the sequence");
+    }
+    // the scheduler's page lists (ScheduledDecode.kv_pages) become the
+    // sequences' device page tables; then every item must fit its pages
+    for (size_t i = 0; i < n; i++) {
+        const uint32_t sid = items[i].seq_id;
+        if (items[i].n_pages && !items[i].page_ids) return set_err(m->b, NEXUS_E_INVALID, "n_pages without page_ids");
+        if (items[i].page_ids) {
+            int rc = pages_bind(m, sid, items[i].page_ids, items[i].n_pages);
+            if (rc) return rc;
         }
+        int rc = check_slot(m, sid, 1);
+        if (rc) return rc;
     }
     NX_CUDA(m->b, cudaEventRecord(m->ev0, m->b->stream));
     const size_t V = m->info.vocab_rows;
@@ -1943,6 +2104,7 @@ extern "C" int nexus_cuda_profile_decode(nexus_cuda_model *m, uint32_t seq_id, u
         s.seq_len = slot + 1;
         m->h_seqs[0] = s;
         m->h_seq_ids[0] = seq_id;
+        NX_CUDA(b, pages_upload(m));
         NX_CUDA(b, cudaMemcpyAsync(m->seqs, m->h_seqs, sizeof(DevSeq), cudaMemcpyHostToDevice, st));
         NX_CUDA(b, cudaMemcpyAsync(m->seq_ids, m->h_seq_ids, 4, cudaMemcpyHostToDevice, st));
         NX_CUDA(b, enqueue_step(m, 1, &prof));

@@ -33,15 +33,27 @@ struct DevSeq {
     unsigned long long best;  // packed argmax accumulator of the head
 };
 
+// Paged KV cache (Scheduler::allocate_kv_pages, src/scheduler.rs:333-361):
+// token `tok` of the sequence in cache row `sid` lives at physical token
+// slot table[sid * per_seq + (tok >> shift)] * 2^shift + (tok & (2^shift - 1))
+// of the per-layer pool; table == nullptr means one contiguous sequence
+// (physical slot = tok), as the op-level entry points pass it.
+struct KvPages {
+    const uint32_t *table;  // [rows][per_seq] page ids
+    uint32_t per_seq;       // table entries per cache row
+    uint32_t shift;         // log2(tokens per page)
+};
+
 struct QkvEpilogue {
     int hq, hkv, head_dim;      // heads and dims (head_dim/2 a multiple of 16)
     float *q_out;               // [m][hq*head_dim]
     const float *rope_cos;      // [max_pos][head_dim/2] host-computed table
     const float *rope_sin;
-    // KV destinations: float cache [seq][max_seq][kv_dim] (k_cache/v_cache) or,
-    // when kv_scratch is set, the new K/V rows go to kv_scratch[m][2][kv_dim]
+    // KV destinations: the float cache pool [pages*page_tokens][kv_dim]
+    // (k_cache/v_cache, addressed through `pages`) or, when kv_scratch is set,
+    // the new K/V rows go to kv_scratch[m][2][kv_dim]
     float *k_cache, *v_cache;
-    size_t seq_stride;          // floats between sequences in k_cache/v_cache
+    KvPages pages;
     float *kv_scratch;
     const DevSeq *seqs;         // [m]
     const uint32_t *seq_ids;    // [m] cache row of each batch entry
@@ -98,16 +110,14 @@ struct AttnParams {
     const float *q;          // [m][hq*head_dim]
     float *out;              // [m][hq*head_dim]
     float scale;             // 1/sqrt(head_dim)
-    // float cache
+    // float cache pool [slots][kv_dim]
     const float *k_cache, *v_cache;
-    size_t seq_stride;       // floats between sequences
-    // packed cache (bits_k > 0): per sequence, per token bytes + mins + scales
+    // packed cache pool (bits_k > 0): per physical slot, bytes + min + scale
     int bits_k, bits_v;
     const uint8_t *kp_data, *vp_data;
     const float *kp_min, *kp_scale, *vp_min, *vp_scale;
     size_t pk_bpt_k, pk_bpt_v;     // bytes per token
-    size_t pk_seq_stride_k, pk_seq_stride_v;  // bytes between sequences
-    size_t pk_seq_tokens;    // tokens between sequences in min/scale arrays
+    KvPages pages;           // token -> physical slot of either cache
     const DevSeq *seqs;
     const uint32_t *seq_ids;
     int kv_dim;
@@ -128,7 +138,8 @@ struct KvPackParams {
     const float *kv_scratch;      // [m][2][kv_dim]
     uint8_t *kp_data, *vp_data;
     float *kp_min, *kp_scale, *vp_min, *vp_scale;
-    size_t pk_bpt_k, pk_bpt_v, pk_seq_stride_k, pk_seq_stride_v, pk_seq_tokens;
+    size_t pk_bpt_k, pk_bpt_v;
+    KvPages pages;
     const DevSeq *seqs;
     const uint32_t *seq_ids;
     int pdl;

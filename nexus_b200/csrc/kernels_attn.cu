@@ -9,8 +9,9 @@
 // Split-context ("flash decoding") layout: grid (Hkv, nsplit, batch).  Each
 // CTA owns one KV head, a contiguous slice of at least kTokensPerSplit tokens
 // of the context, and all G query heads sharing that KV head, so every K/V
-// element is read from HBM once.  The slice count adapts to the context
-// length (CTAs beyond it exit), so short contexts use few, full slices.
+// element is read from HBM once.  The launcher sizes the slice count so the
+// step's CTAs cover every SM about twice; a context too short for that many
+// slices leaves the extra CTAs to exit at once.
 // Eight warps stride over the slice; each warp issues the loads of kBatch
 // tokens before using any of them (one memory round trip per batch); lane i
 // holds head_dim/32 dims of each row.  Warps keep an online softmax per query
@@ -26,7 +27,7 @@ namespace nx {
 
 constexpr int kAttnWarps = 8;
 constexpr int kBatch = 8;
-constexpr int kTokensPerSplit = 64;
+constexpr int kTokensPerSplit = 16;  // a slice holds at least this many tokens
 
 template <int VEC>
 __device__ __forceinline__ void load_f32(const float *p, float (&v)[VEC]) {
@@ -145,16 +146,14 @@ __global__ void __launch_bounds__(kAttnWarps * 32, G <= 4 ? 2 : 1) k_attn(AttnPa
 #pragma unroll
         for (int j = 0; j < kBatch; j++) {
             const int tok = min(base + j, t1 - 1);
+            const size_t ph = kv_phys(p.pages, sid, (uint32_t)tok);
             if (!packed) {
-                const size_t off = (size_t)sid * p.seq_stride + (size_t)tok * p.kv_dim + e0;
+                const size_t off = ph * p.kv_dim + e0;
                 load_f32<VEC>(p.k_cache + off, kv[j]);
                 load_f32<VEC>(p.v_cache + off, vv[j]);
             } else {
-                const size_t mi = (size_t)sid * p.pk_seq_tokens + tok;
-                load_packed<VEC>(p.kp_data + (size_t)sid * p.pk_seq_stride_k + (size_t)tok * p.pk_bpt_k, e0,
-                                 p.bits_k, p.kp_min[mi], p.kp_scale[mi], kv[j]);
-                load_packed<VEC>(p.vp_data + (size_t)sid * p.pk_seq_stride_v + (size_t)tok * p.pk_bpt_v, e0,
-                                 p.bits_v, p.vp_min[mi], p.vp_scale[mi], vv[j]);
+                load_packed<VEC>(p.kp_data + ph * p.pk_bpt_k, e0, p.bits_k, p.kp_min[ph], p.kp_scale[ph], kv[j]);
+                load_packed<VEC>(p.vp_data + ph * p.pk_bpt_v, e0, p.bits_v, p.vp_min[ph], p.vp_scale[ph], vv[j]);
             }
         }
         float pd[NV];

@@ -299,9 +299,9 @@ __global__ void __launch_bounds__(kPkWarps * 32, NG == 1 ? 4 : 2) k_attn_pk(Attn
 #pragma unroll
             for (int r = 0; r < 4; r++) acc[hg][i][r] = 0.0f;
     }
-    const size_t mi0 = (size_t)sid * p.pk_seq_tokens;
-    const uint8_t *kseq = p.kp_data + (size_t)sid * p.pk_seq_stride_k + (size_t)h * (16 * BK);
-    const uint8_t *vseq = p.vp_data + (size_t)sid * p.pk_seq_stride_v + (size_t)h * (16 * BV);
+    // the KV head's segment of every physical slot; tokens map to slots through the page table
+    const uint8_t *kseq = p.kp_data + (size_t)h * (16 * BK);
+    const uint8_t *vseq = p.vp_data + (size_t)h * (16 * BV);
     using TL = PkTile<BK, BV, TT>;
     extern __shared__ __align__(16) uint8_t pk_dyn[];
     uint8_t *wbuf = pk_dyn + (size_t)warp * 2 * TL::BYTES;
@@ -312,24 +312,25 @@ __global__ void __launch_bounds__(kPkWarps * 32, NG == 1 ? 4 : 2) k_attn_pk(Attn
 #pragma unroll
         for (int i = 0; i < TT * BK / 32; i++) {
             const int ch = lane + 32 * i, tt = ch / BK, part = ch % BK;
-            const int tok = min(base + tt, t1 - 1);
-            cp_async16(b + TL::K + tt * 16 * BK + part * 16, kseq + (size_t)tok * p.pk_bpt_k + part * 16);
+            const size_t ph = kv_phys(p.pages, sid, (uint32_t)min(base + tt, t1 - 1));
+            cp_async16(b + TL::K + tt * 16 * BK + part * 16, kseq + ph * p.pk_bpt_k + part * 16);
         }
 #pragma unroll
         for (int i = 0; i < TT * BV / 32; i++) {
             const int ch = lane + 32 * i, tt = ch / BV, part = ch % BV;
-            const int tok = min(base + tt, t1 - 1);
+            const size_t ph = kv_phys(p.pages, sid, (uint32_t)min(base + tt, t1 - 1));
             cp_async16(b + TL::V + vrow<BV>(tt) * 16 * BV + vunit<BV>(tt, part) * 16,
-                       vseq + (size_t)tok * p.pk_bpt_v + part * 16);
+                       vseq + ph * p.pk_bpt_v + part * 16);
         }
 #pragma unroll
         for (int i = 0; i < TT / 32; i++) {
-            const int tt = lane + 32 * i, tok = min(base + tt, t1 - 1);
+            const int tt = lane + 32 * i;
+            const size_t ph = kv_phys(p.pages, sid, (uint32_t)min(base + tt, t1 - 1));
             float *ms = reinterpret_cast<float *>(b + TL::MS) + 4 * tt;
-            cp_async4(ms + 0, p.kp_min + mi0 + tok);
-            cp_async4(ms + 1, p.kp_scale + mi0 + tok);
-            cp_async4(ms + 2, p.vp_min + mi0 + tok);
-            cp_async4(ms + 3, p.vp_scale + mi0 + tok);
+            cp_async4(ms + 0, p.kp_min + ph);
+            cp_async4(ms + 1, p.kp_scale + ph);
+            cp_async4(ms + 2, p.vp_min + ph);
+            cp_async4(ms + 3, p.vp_scale + ph);
         }
     };
     int base = t0 + warp * TT, st = 0;

@@ -382,7 +382,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, int g, int t,
             kdst = q.kv_scratch + (size_t)t * 2 * kv_dim;
             vdst = kdst + kv_dim;
         } else {
-            const size_t base = (size_t)q.seq_ids[t] * q.seq_stride + (size_t)sq.slot * kv_dim;
+            const size_t base = kv_phys(q.pages, q.seq_ids[t], sq.slot) * kv_dim;
             kdst = q.k_cache + base;
             vdst = q.v_cache + base;
         }

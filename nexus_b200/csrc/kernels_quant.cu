@@ -10,6 +10,7 @@
 //   dequant_tiles : tiles -> f32, the inverse view (same bits as dequant_raw)
 #include <cuda_runtime.h>
 
+#include "common.cuh"
 #include "kernels.h"
 #include "quant_math.cuh"
 #include "tiles.cuh"
@@ -307,14 +308,13 @@ __global__ void k_kv_pack(KvPackParams p) {
     __syncthreads();
     const DevSeq sq = p.seqs[t];
     const uint32_t sid = p.seq_ids[t];
-    uint8_t *dst = (which ? p.vp_data : p.kp_data) + (size_t)sid * (which ? p.pk_seq_stride_v : p.pk_seq_stride_k) +
-                   (size_t)sq.slot * bpt;
+    const size_t ph = kv_phys(p.pages, sid, sq.slot);
+    uint8_t *dst = (which ? p.vp_data : p.kp_data) + ph * bpt;
     const uint8_t *src = reinterpret_cast<const uint8_t *>(words);
     for (size_t i = threadIdx.x; i < bpt; i += blockDim.x) dst[i] = src[i];
     if (threadIdx.x == 0) {
-        const size_t mi = (size_t)sid * p.pk_seq_tokens + sq.slot;
-        (which ? p.vp_min : p.kp_min)[mi] = mn;
-        (which ? p.vp_scale : p.kp_scale)[mi] = scale;
+        (which ? p.vp_min : p.kp_min)[ph] = mn;
+        (which ? p.vp_scale : p.kp_scale)[ph] = scale;
     }
 }
 

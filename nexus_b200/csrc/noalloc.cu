@@ -137,7 +137,6 @@ extern "C" int nexus_cuda_attention_noalloc(nexus_cuda_backend *b, const float *
         a.scale = scale != 0.0f ? scale : 1.0f / sqrtf((float)head_dim);
         a.k_cache = k_dev;
         a.v_cache = v_dev;
-        a.seq_stride = 0;
         a.seqs = seq;
         a.seq_ids = sid;
         a.kv_dim = (int)(num_kv_heads * head_dim);

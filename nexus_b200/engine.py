@@ -59,7 +59,7 @@ class CudaBackend:
     """``Backend`` trait implementation for BackendType::Cuda."""
 
     def __init__(self, device: int = 0, kv_bits: tuple[int, int] = (0, 0), max_batch: int = 1,
-                 max_seq_len: int = 0, flags: int = 0):
+                 max_seq_len: int = 0, flags: int = 0, page_tokens: int = 0, max_pages: int = 0):
         lib = L.load()
         cfg = L.Config()
         lib.nexus_cuda_config_default(C.byref(cfg))
@@ -68,6 +68,9 @@ class CudaBackend:
         cfg.max_batch = max_batch
         cfg.max_seq_len = max_seq_len
         cfg.flags = flags
+        if page_tokens:
+            cfg.page_tokens = page_tokens
+        cfg.max_pages = max_pages
         h = C.c_void_p()
         L.check(lib.nexus_cuda_backend_create(C.byref(cfg), C.byref(h)))
         self._lib = lib
@@ -329,14 +332,15 @@ class InferenceEngine:
                      page_ids: Optional[Sequence[Sequence[int]]] = None):
         """items: (seq_id, token, position) per sequence; page_ids: optional
         scheduler page list per item (Scheduler::allocate_kv_pages,
-        src/scheduler.rs:333-361); returns (tokens, logits)."""
+        src/scheduler.rs:333-361; an empty list keeps the sequence's current
+        pages); returns (tokens, logits)."""
         n = len(items)
         arr = (L.DecodeItem * max(n, 1))()
         keep = []
         for i, (sid, tok, pos) in enumerate(items):
             arr[i].seq_id, arr[i].token, arr[i].position = sid, tok, pos
             arr[i].n_pages, arr[i].page_ids = 0, None
-            if page_ids is not None:
+            if page_ids is not None and len(page_ids[i]):
                 pg = np.ascontiguousarray(np.asarray(page_ids[i], np.uint32))
                 keep.append(pg)
                 arr[i].n_pages = pg.size
@@ -347,6 +351,14 @@ class InferenceEngine:
                                                   None if logits is None else _ptr(logits)),
                 self.backend.handle)
         return toks[:n].tolist(), logits
+
+    def seq_set_pages(self, seq_id: int, page_ids: Optional[Sequence[int]]) -> None:
+        """Bind a request's KV page list (Scheduler::allocate_kv_pages,
+        src/scheduler.rs:333-361) before its prefill; None or [] releases the
+        pages and clears the sequence."""
+        pg = np.ascontiguousarray(np.asarray(page_ids if page_ids is not None else [], np.uint32))
+        L.check(self._lib.nexus_cuda_seq_set_pages(self.model, seq_id, _ptr(pg) if pg.size else None, pg.size),
+                self.backend.handle)
 
     def seq_len(self, seq_id: int = 0) -> int:
         v = C.c_uint32()
