@@ -95,6 +95,8 @@ typedef struct {
 
 #define NEXUS_CFG_NO_GRAPH 0x1u  /* launch kernels directly instead of a CUDA graph */
 #define NEXUS_CFG_NO_PDL 0x2u    /* no programmatic dependent launch between kernels */
+#define NEXUS_CFG_PERSISTENT 0x4u /* single-token steps on the persistent whole-step kernel
+                                     (one launch per token) instead of the kernel-per-op graph */
 
 typedef struct nexus_cuda_backend nexus_cuda_backend;
 

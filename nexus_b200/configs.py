@@ -49,6 +49,11 @@ CONFIGS = {
     "llama8b_q8_l2": dict(num_layers=2, hidden_size=4096, num_heads=32, num_kv_heads=8, ff_dim=14336,
                           vocab_size=128256, context_length=8448, rope_theta=500000.0, attn_format=Q8_0,
                           ffn_format=Q8_0, embd_format=Q8_0, head_format=Q8_0, norm_format=Q8_0),
+    # the config-E model's widths and formats with 2 layers (a small case of
+    # the same kernels for ncu captures)
+    "llama8b_q4k_l2": dict(num_layers=2, hidden_size=4096, num_heads=32, num_kv_heads=8, ff_dim=14336,
+                           vocab_size=128256, context_length=8448, rope_theta=500000.0, attn_format=Q4_K,
+                           ffn_format=Q4_K, embd_format=Q8_0, head_format=Q8_0, norm_format=Q4_K),
     "llama70b_l2": dict(num_layers=2, hidden_size=8192, num_heads=64, num_kv_heads=8, ff_dim=28672,
                         vocab_size=128256, context_length=4352, rope_theta=500000.0, attn_format=Q4_K,
                         ffn_format=Q2_K, embd_format=Q8_0, head_format=Q8_0, norm_format=Q4_K),

@@ -989,6 +989,12 @@ struct nexus_cuda_model {
     int nsplit_pk[kMaxChunk + 1] = {};  // the same for the packed-cache tensor-core kernel
     cudaGraphExec_t graph[kMaxChunk + 1] = {};
     bool use_graph = true, use_pdl = true;
+    // single-token steps as one persistent kernel (kernels_step.cu)
+    bool use_step = false;
+    StepParams step = {};
+    StepLaunch step_launch = {};
+    StepLayer *step_layers = nullptr;     // device array of the layers' matrices and caches
+    size_t step_gcounter_slots = 0;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     float last_ms = 0.0f;
     std::vector<void *> allocs;
@@ -1088,6 +1094,8 @@ static const uint8_t *column_slice(int fmt, const uint8_t *src, uint32_t rows, u
     for (uint32_t r = 0; r < rows; r++) memcpy(buf.data() + (size_t)r * nb, src + (size_t)r * rb + off, nb);
     return buf.data();
 }
+
+static KvPages dev_pages(const nexus_cuda_model *m);
 
 static int model_load(nexus_cuda_backend *b, const char *path, nexus_cuda_model **out) {
     GgufFile f;
@@ -1316,14 +1324,10 @@ static int model_load(nexus_cuda_backend *b, const char *path, nexus_cuda_model 
     NX_CUDA(b, malloc_tracked(m, &m->logits, (size_t)MC * (m->has_head ? m->v_l : I.vocab_rows)));
     if (tp > 1) NX_CUDA(b, malloc_tracked(m, &m->logits_gather, (size_t)tp * MC * m->v_l));
     const int G = (int)(Hq / Hkv);
-    // context slices of >= 16 tokens, at most 64 per (sequence, KV head):
-    // enough for about two CTAs per SM over the step's sequences and KV heads
-    // (the kernel uses fewer when the context is short)
-    int sms = 148;
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, b->device);
-    int max_split = std::max(1, std::min(64, (int)((m->max_seq + 15) / 16)));
-    for (int mm = 1; mm <= MC; mm++)
-        m->nsplit[mm] = std::max(1, std::min(max_split, (2 * sms + mm * (int)hkv_l - 1) / (mm * (int)hkv_l)));
+    // context slices of >= 64 tokens, at most 64 per (sequence, KV head); the
+    // kernel uses only as many as the current context needs
+    int max_split = std::max(1, std::min(64, (int)((m->max_seq + 63) / 64)));
+    for (int mm = 1; mm <= MC; mm++) m->nsplit[mm] = max_split;
     // the packed-cache kernel: about 8 CTAs per SM over the whole step (its
     // CTAs stream whole 64-token tiles and need no more slices than that)
     for (int mm = 1; mm <= MC; mm++)
@@ -1353,6 +1357,63 @@ static int model_load(nexus_cuda_backend *b, const char *path, nexus_cuda_model 
     NX_CUDA(b, malloc_tracked(m, &m->page_table, m->pm.table.size()));
     NX_CUDA(b, cudaMemset(m->page_table, 0, m->pm.table.size() * 4));
     NX_CUDA(b, cudaDeviceSynchronize());
+    // the persistent single-token step (opt-in): one GPU, float KV cache, an LM
+    // head, shapes the step kernel covers (otherwise the kernel-per-op graph runs)
+    if (tp == 1 && m->bits_k == 0 && m->has_head && (b->cfg.flags & NEXUS_CFG_PERSISTENT)) {
+        StepParams &sp = m->step;
+        auto sm_of = [](const Mat &w) { return StepMat{w.fmt, w.main, w.aux, w.n, w.k}; };
+        std::vector<StepLayer> hl(I.num_layers);
+        size_t groups = (m->head.n + 31) / 32;
+        for (uint32_t l = 0; l < I.num_layers; l++) {
+            const Layer &L = m->layers[l];
+            hl[l] = StepLayer{sm_of(L.qkv), sm_of(L.o), sm_of(L.gateup), sm_of(L.down), L.attn_norm, L.ffn_norm,
+                              L.k_cache, L.v_cache};
+            for (const Mat *w : {&L.qkv, &L.o, &L.gateup, &L.down}) groups = std::max<size_t>(groups, (w->n + 31) / 32);
+        }
+        sp.num_layers = (int)I.num_layers;
+        sp.head = sm_of(m->head);
+        sp.out_norm = m->out_norm;
+        sp.hidden = (int)H;
+        sp.hq = (int)Hq;
+        sp.hkv = (int)Hkv;
+        sp.head_dim = (int)D;
+        sp.ffn = (int)F;
+        sp.eps = I.rms_norm_eps;
+        sp.rope_cos = m->rope_cos;
+        sp.rope_sin = m->rope_sin;
+        sp.x_hidden = m->hidden;
+        sp.q = m->q;
+        sp.attn = m->attn;
+        sp.gated = m->gated;
+        sp.logits = m->logits;
+        sp.seqs = m->seqs;
+        sp.seq_ids = m->seq_ids;
+        sp.pages = dev_pages(m);
+        sp.out_tokens = m->out_tokens;
+        sp.err = reinterpret_cast<int *>(m->out_tokens + kMaxChunk);
+        bool fmts_ok = true;
+        for (const StepLayer &L : hl)
+            for (const StepMat *w : {&L.qkv, &L.o, &L.gateup, &L.down}) fmts_ok = fmts_ok && gemm_supported(w->fmt);
+        fmts_ok = fmts_ok && gemm_supported(sp.head.fmt);
+        if (fmts_ok && step_plan(sp, b->device, &m->step_launch) == cudaSuccess) {
+            StepLaunch &sl = m->step_launch;
+            // attention: slices of >= 32 tokens, about one block per CTA
+            sp.attn_nsplit = std::max(1, std::min(64, sl.grid / (int)Hkv));
+            NX_CUDA(b, malloc_tracked(m, &m->step_layers, hl.size()));
+            NX_CUDA(b, cudaMemcpy(m->step_layers, hl.data(), hl.size() * sizeof(StepLayer), cudaMemcpyHostToDevice));
+            sp.layers = m->step_layers;
+            NX_CUDA(b, malloc_tracked(m, &sp.attn_part, (size_t)Hkv * sp.attn_nsplit * (Hq / Hkv) * (D + 2)));
+            NX_CUDA(b, malloc_tracked(m, &sp.attn_counters, (size_t)Hkv));
+            NX_CUDA(b, malloc_tracked(m, &sp.gpart, step_gpart_floats(sl)));
+            m->step_gcounter_slots = groups;
+            NX_CUDA(b, malloc_tracked(m, &sp.gcounters, groups));
+            NX_CUDA(b, malloc_tracked(m, &sp.bar, (size_t)2));
+            NX_CUDA(b, cudaMemset(sp.attn_counters, 0, (size_t)Hkv * 4));
+            NX_CUDA(b, cudaMemset(sp.gcounters, 0, groups * 4));
+            NX_CUDA(b, cudaMemset(sp.bar, 0, 8));
+            m->use_step = true;
+        }
+    }
     guard.release();
     backend_retain(b);
     m->retained = true;
@@ -1762,9 +1823,40 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
     return e;
 }
 
+// One single-token step on the persistent kernel: k_embed decodes the
+// token's embedding row (bit-exact) and clears the argmax, then the step
+// kernel runs every layer, the head and the advance.
+static cudaError_t enqueue_persistent_step(nexus_cuda_model *m, StepProfiler *prof = nullptr) {
+    cudaStream_t st = m->b->stream;
+    EmbedParams ep = {};
+    ep.fmt = m->embd_fmt;
+    ep.m = 1;
+    ep.hidden = (int)m->info.hidden_size;
+    ep.vocab_rows = m->embd_rows;
+    ep.table = m->embd;
+    ep.out = m->hidden;
+    ep.seqs = m->seqs;
+    if (prof) prof->begin();
+    cudaError_t e = launch_embed(ep, st);
+    if (e != cudaSuccess) return e;
+    if (prof) prof->end("embed", (double)format_bytes(m->embd_fmt, (size_t)m->info.hidden_size) + 4.0 * m->info.hidden_size);
+    if (prof) prof->begin();
+    e = launch_decode_step(m->step, m->step_launch, st);
+    if (prof) {
+        // algorithmic bytes: every weight once, the K/V read by attention
+        const double ctx = (double)m->h_seqs[0].seq_len;
+        prof->end("decode_step", (double)m->info.weight_bytes + ctx * 8.0 * m->kvd_l * m->info.num_layers);
+    }
+    return e;
+}
+
 static int run_step(nexus_cuda_model *m, int mc) {
     nexus_cuda_backend *b = m->b;
     cudaStream_t st = b->stream;
+    if (mc == 1 && m->use_step) {
+        NX_CUDA(b, enqueue_persistent_step(m));
+        return NEXUS_OK;
+    }
     if (m->use_graph && m->has_head) {
         if (!m->graph[mc]) {
             cudaGraph_t g = nullptr;
@@ -1793,6 +1885,12 @@ static int run_step(nexus_cuda_model *m, int mc) {
 // A kernel gave up on a bounded wait: report it and clear the flag.
 static int device_timeout(nexus_cuda_model *m) {
     cudaMemsetAsync(m->out_tokens + kMaxChunk, 0, 4, m->b->stream);
+    if (m->use_step) {
+        // an abandoned step may leave its arrival counters part-way
+        cudaMemsetAsync(m->step.bar, 0, 8, m->b->stream);
+        cudaMemsetAsync(m->step.gcounters, 0, m->step_gcounter_slots * 4, m->b->stream);
+        cudaMemsetAsync(m->step.attn_counters, 0, (size_t)m->step.hkv * 4, m->b->stream);
+    }
     cudaStreamSynchronize(m->b->stream);
     return set_err(m->b, NEXUS_E_TIMEOUT, "a device wait timed out (weight stream did not arrive)");
 }
@@ -2107,7 +2205,8 @@ extern "C" int nexus_cuda_profile_decode(nexus_cuda_model *m, uint32_t seq_id, u
         NX_CUDA(b, pages_upload(m));
         NX_CUDA(b, cudaMemcpyAsync(m->seqs, m->h_seqs, sizeof(DevSeq), cudaMemcpyHostToDevice, st));
         NX_CUDA(b, cudaMemcpyAsync(m->seq_ids, m->h_seq_ids, 4, cudaMemcpyHostToDevice, st));
-        NX_CUDA(b, enqueue_step(m, 1, &prof));
+        if (m->use_step) NX_CUDA(b, enqueue_persistent_step(m, &prof));
+        else NX_CUDA(b, enqueue_step(m, 1, &prof));
         NX_CUDA(b, cudaMemcpyAsync(m->h_out_tokens, m->out_tokens, (kMaxChunk + 1) * 4, cudaMemcpyDeviceToHost, st));
         NX_CUDA(b, cudaStreamSynchronize(st));
         if (m->h_out_tokens[kMaxChunk]) return device_timeout(m);

@@ -148,6 +148,52 @@ cudaError_t launch_kv_pack(const KvPackParams &p, cudaStream_t st);
 // device-chained decode: next token = argmax, positions advance by one
 cudaError_t launch_advance(DevSeq *seqs, int m, uint32_t *out_tokens, int pdl, cudaStream_t st);
 
+// ---- kernels_step.cu: the single-token decode step as one persistent kernel ----
+// One matrix in the tile layout (tiles.cuh): fmt, tiles, Q2_K side words, rows, columns.
+struct StepMat {
+    int fmt;
+    const uint4 *main;
+    const uint32_t *aux;
+    int n, k;
+};
+struct StepLayer {
+    StepMat qkv, o, gateup, down;   // fused Q|K|V (RoPE pairs in lanes i, i+16), o_proj, gate|up, down
+    const float *attn_norm, *ffn_norm;
+    float *k_cache, *v_cache;       // float KV page pools
+};
+struct StepParams {
+    const StepLayer *layers;        // device array
+    int num_layers;
+    StepMat head;
+    const float *out_norm;
+    int hidden, hq, hkv, head_dim, ffn;
+    float eps;
+    const float *rope_cos, *rope_sin;
+    float *x_hidden, *q, *attn, *gated;
+    float *logits;                  // head outputs (nullptr: argmax only)
+    DevSeq *seqs;                   // one sequence
+    const uint32_t *seq_ids;
+    KvPages pages;
+    uint32_t *out_tokens;           // [0] = next token
+    int *err;                       // set when a bounded wait gives up
+    float *attn_part;               // [hkv][attn_nsplit][G][head_dim + 2]
+    unsigned *attn_counters;        // [hkv], zero between launches
+    int attn_nsplit;
+    float *gpart;                   // [grid * warps][2][32] partial row sums of shared row groups
+    unsigned *gcounters;            // [max row groups], zero between launches
+    unsigned *bar;                  // grid barrier: arrivals, generation
+};
+struct StepLaunch {
+    int warps, grid;
+    size_t smem;
+};
+// Fills the launch shape for the model, or returns cudaErrorNotSupported when
+// the step kernel does not cover it (head_dim 128, G in {1, 2, 4, 8}, widths
+// multiples of 256, shared memory within the SM).
+cudaError_t step_plan(const StepParams &p, int device, StepLaunch *out);
+size_t step_gpart_floats(const StepLaunch &l);
+cudaError_t launch_decode_step(const StepParams &p, const StepLaunch &l, cudaStream_t st);
+
 // ---- kernels_misc.cu ----
 // embedding row gather with bit-exact dequantization; also resets seqs[t].best
 struct EmbedParams {

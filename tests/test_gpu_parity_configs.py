@@ -1,0 +1,177 @@
+"""Parity of the benchmarked configurations against oracle fixtures.
+
+tests/golden/make_model_fixtures.py ran the CPU oracle (the C restatement of
+the reference's decode path) on the seeded synthetic models of BASELINE.json's
+configurations and stored, per case, the prompt, the greedy continuation and
+sampled logits (every 64th vocabulary row plus the 64 largest).  These tests
+replay the same prompts through the CUDA backend's C ABI and compare:
+
+  * logits (after the prefill and after the last decode step) within the
+    north star's 2e-3 max-abs for the float KV cache; within 2e-2 for the
+    packed cache, where a GEMV/GEMM rounding difference of ~1e-6 can move a
+    K/V value across a quantization step (packing itself is bit-exact,
+    tests/test_gpu_ops.py);
+  * greedy tokens identical at every step whose oracle top-2 gap exceeds twice
+    that tolerance (a closer pair is a tie at the tolerance; the fixtures
+    record every gap); the decode steps are teacher-forced with the oracle's
+    tokens, so one differing step cannot derail the rest;
+  * KV lengths equal to prompt + steps.
+
+Cases: config E at b=1 (512-token prompt, the bench workload; single-token
+steps on the kernel-per-op graph and on the persistent step kernel), config
+E at b=32 (the four fixture prompts among 28 others, the tcgen05 GEMM path),
+config P's model with the 4-bit packed cache on scheduler
+page lists at a 1031-token context and, with 2 layers, at an 8191-token
+context, and config X's widths and formats (Q4_K attention, Q2_K FFN) with 2
+layers after a 4096-token prompt at b=1 and b=16.
+"""
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+CASES = json.loads((GOLDEN / "model_cases.json").read_text())
+FLOAT_TOL, PACKED_TOL = 2e-3, 2e-2
+VOCAB = 128256
+
+
+def _need(*names):
+    missing = [n for n in names if n not in CASES]
+    if missing:
+        pytest.fail(f"fixture(s) {missing} missing: run tests/golden/make_model_fixtures.py")
+
+
+def _fixture(name):
+    d = np.load(GOLDEN / CASES[name]["file"])
+    return CASES[name], {k: d[k] for k in d.files}
+
+
+def _tol(spec):
+    return PACKED_TOL if spec["kv_bits"][0] else FLOAT_TOL
+
+
+def _check_logits(got, fx, which, tol, label):
+    idx, want = fx[f"idx_{which}"], fx[f"logits_{which}"]
+    err = float(np.max(np.abs(got[idx] - want)))
+    print(f"{label} {which}: max |logit diff| = {err:.3e}")
+    assert err < tol, (label, which, err)
+
+
+def _check_token(tok, fx, step, tol, label):
+    if float(fx["gaps"][step]) > 2 * tol:
+        assert tok == int(fx["tokens"][step]), (label, step, tok, int(fx["tokens"][step]))
+
+
+def _filler_prompt(seed, n):
+    return np.random.default_rng(seed).integers(0, VOCAB, n).tolist()
+
+
+def _scheduler_pages(lens, page_tokens=16):
+    """Scheduler::allocate_kv_pages (src/scheduler.rs:333-361): ceil(tokens/16)
+    ids per request from a running counter, here interleaved across requests so
+    that no sequence's pages are contiguous."""
+    need = [(n + page_tokens - 1) // page_tokens for n in lens]
+    pages, counter = [[] for _ in need], 0
+    for k in range(max(need)):
+        for s in range(len(need)):
+            if k < need[s]:
+                pages[s].append(counter)
+                counter += 1
+    return pages, counter
+
+
+def _run_batch(nb, name, fixtures, batch, filler_len):
+    """Sequences 0..len(fixtures)-1 replay fixture prompts, the rest are filler
+    prompts; every step is one decode_batch over all of them (teacher-forced
+    for the fixture sequences), on scheduler page lists."""
+    _need(*fixtures)
+    spec = CASES[fixtures[0]]
+    fxs = [_fixture(f)[1] for f in fixtures]
+    tol = _tol(spec)
+    steps = spec["steps"]
+    prompts = [fx["prompt"].tolist() for fx in fxs]
+    prompts += [_filler_prompt(1000 + s, filler_len) for s in range(batch - len(fxs))]
+    pages, total = _scheduler_pages([len(p) + steps + 1 for p in prompts])
+    be = nb.CudaBackend(device=0, kv_bits=tuple(spec["kv_bits"]), max_batch=batch,
+                        max_seq_len=spec["max_seq_len"], max_pages=total)
+    eng = nb.InferenceEngine(be)
+    eng.load_model(nb.model_path(spec["config"]))
+    toks = []
+    for s, p in enumerate(prompts):
+        eng.seq_set_pages(s, pages[s])
+        lg, t = eng.prefill(p, seq_id=s, want_logits=s < len(fxs))
+        if s < len(fxs):
+            _check_logits(lg, fxs[s], "first", tol, f"{name}[{s}]")
+            _check_token(t, fxs[s], 0, tol, f"{name}[{s}]")
+            t = int(fxs[s]["tokens"][0])
+        toks.append(t)
+    for i in range(steps):
+        last = i == steps - 1
+        items = [(s, toks[s], len(prompts[s]) + i) for s in range(batch)]
+        out, logits = eng.decode_batch(items, want_logits=last, page_ids=pages)
+        for s in range(batch):
+            if s < len(fxs):
+                _check_token(out[s], fxs[s], i + 1, tol, f"{name}[{s}]")
+                out[s] = int(fxs[s]["tokens"][i + 1])
+                if last:
+                    _check_logits(logits[s], fxs[s], "last", tol, f"{name}[{s}]")
+            assert eng.seq_len(s) == len(prompts[s]) + i + 1
+        toks = list(out)
+    eng.close()
+    be.close()
+
+
+def _run_single(nb, name, flags=0):
+    """One sequence: prefill, then teacher-forced single-token decode steps."""
+    _need(name)
+    spec, fx = _fixture(name)
+    tol = _tol(spec)
+    be = nb.CudaBackend(device=0, kv_bits=tuple(spec["kv_bits"]), max_seq_len=spec["max_seq_len"], flags=flags)
+    eng = nb.InferenceEngine(be)
+    eng.load_model(nb.model_path(spec["config"]))
+    n = spec["prompt_len"]
+    lg, t = eng.prefill(fx["prompt"].tolist())
+    _check_logits(lg, fx, "first", tol, name)
+    _check_token(t, fx, 0, tol, name)
+    for i in range(spec["steps"]):
+        lg, t = eng.decode_with_cache(int(fx["tokens"][i]), n + i, want_logits=i == spec["steps"] - 1)
+        _check_token(t, fx, i + 1, tol, name)
+    _check_logits(lg, fx, "last", tol, name)
+    assert eng.seq_len() == n + spec["steps"]
+    eng.close()
+    be.close()
+
+
+def test_config_e_b1_prompt512(nb):
+    _run_single(nb, "e_s1")
+
+
+def test_config_e_b1_prompt512_persistent_step(nb):
+    from nexus_b200 import _lib as L
+    _run_single(nb, "e_s1", flags=L.CFG_PERSISTENT)
+
+
+def test_config_e_b32_prompt512(nb):
+    _run_batch(nb, "e_b32", ["e_s1", "e_s2", "e_s3", "e_s4"], batch=32, filler_len=512)
+
+
+def test_config_p_packed_kv_ctx1k(nb):
+    # 8 requests (the tensor-core GEMM and packed attention paths): the fixture
+    # request at 1031 tokens among 7 others
+    _run_batch(nb, "p_1k", ["p_1k"], batch=8, filler_len=777)
+
+
+def test_config_p_packed_kv_ctx8k_two_layers(nb):
+    _run_batch(nb, "p_8k_l2", ["p_8k_l2"], batch=8, filler_len=300)
+
+
+def test_config_x_two_layers_b1_prompt4096(nb):
+    _run_single(nb, "x_l2")
+
+
+def test_config_x_two_layers_b16_prompt4096(nb):
+    _run_batch(nb, "x_l2_b16", ["x_l2"], batch=16, filler_len=200)
