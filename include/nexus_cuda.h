@@ -97,6 +97,10 @@ typedef struct {
 #define NEXUS_CFG_NO_PDL 0x2u    /* no programmatic dependent launch between kernels */
 #define NEXUS_CFG_PERSISTENT 0x4u /* single-token steps on the persistent whole-step kernel
                                      (one launch per token) instead of the kernel-per-op graph */
+#define NEXUS_CFG_FAULT_STALL_BARRIER 0x100u /* fault injection for tests of the error path: the
+                                     persistent step kernel's grid barrier waits for a CTA that does
+                                     not exist, so every step gives up after its bounded wait (about
+                                     a second) and returns NEXUS_E_TIMEOUT; the context stays usable */
 
 typedef struct nexus_cuda_backend nexus_cuda_backend;
 

@@ -42,6 +42,7 @@ OP_ATTENTION_PACKED = 13
 CFG_NO_GRAPH = 0x1
 CFG_NO_PDL = 0x2
 CFG_PERSISTENT = 0x4
+CFG_FAULT_STALL_BARRIER = 0x100
 
 
 class Caps(C.Structure):

@@ -122,9 +122,15 @@ static int set_err(nexus_cuda_backend *b, int code, const std::string &msg) {
     return code;
 }
 
+// A failed allocation is reported as NEXUS_E_OOM (and cleared: it does not
+// poison the context); any other CUDA error as NEXUS_E_CUDA.
 #define NX_CUDA(b, call)                                                                        \
     do {                                                                                        \
         cudaError_t e_ = (call);                                                                \
+        if (e_ == cudaErrorMemoryAllocation) {                                                  \
+            cudaGetLastError();                                                                 \
+            return set_err((b), NEXUS_E_OOM, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+        }                                                                                       \
         if (e_ != cudaSuccess)                                                                  \
             return set_err((b), NEXUS_E_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
     } while (0)
@@ -1391,6 +1397,7 @@ static int model_load(nexus_cuda_backend *b, const char *path, nexus_cuda_model 
         sp.pages = dev_pages(m);
         sp.out_tokens = m->out_tokens;
         sp.err = reinterpret_cast<int *>(m->out_tokens + kMaxChunk);
+        sp.bar_extra = (b->cfg.flags & NEXUS_CFG_FAULT_STALL_BARRIER) ? 1u : 0u;
         bool fmts_ok = true;
         for (const StepLayer &L : hl)
             for (const StepMat *w : {&L.qkv, &L.o, &L.gateup, &L.down}) fmts_ok = fmts_ok && gemm_supported(w->fmt);

@@ -182,6 +182,7 @@ struct StepParams {
     float *gpart;                   // [grid * warps][2][32] partial row sums of shared row groups
     unsigned *gcounters;            // [max row groups], zero between launches
     unsigned *bar;                  // grid barrier: arrivals, generation
+    unsigned bar_extra;             // 0; 1 = fault injection: barriers wait for one CTA too many
 };
 struct StepLaunch {
     int warps, grid;

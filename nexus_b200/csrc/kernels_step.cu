@@ -20,14 +20,25 @@
 // the 24-bit input planes once, with the RMSNorm folded in, and each warp
 // dots its items with dp4a) splits the matrix's items -- (row group of 32
 // rows, 256-column super-block) tiles, Q8_0 tiles in two halves -- evenly
-// over all warps of the grid: warp w of the N warps takes items
-// [w*T/N, (w+1)*T/N).  A row group whose items one warp holds is finished by
-// that warp; a group split between warps leaves one partial per warp in
-// global memory, and the warp whose arrival completes the group's item count
-// adds the partials in warp order (deterministic) and runs the epilogue (the
-// GEMV's fused epilogues: RoPE + KV append, residual add, SwiGLU, logits +
-// argmax).  The attention phase runs attn_block (attn_block.cuh) over
+// over the CTAs (CTA c of C takes [c*T/C, (c+1)*T/C)) and each CTA's share
+// evenly over its warps.  A row group one warp holds is finished by that
+// warp; the partials of a group held by several warps meet in shared memory
+// and are added in warp order; a group crossing a CTA boundary leaves each
+// CTA's sum in global memory and the CTA whose items complete it (an atomic
+// item count per group) adds them in CTA order -- all deterministic -- and
+// runs the fused epilogue (RoPE + KV append, residual add, SwiGLU, logits +
+// argmax, chosen at run time so all phases of a format share one body of
+// code).  The attention phase runs attn_block (attn_block.cuh) over
 // (KV head, context slice) blocks spread over the CTAs.
+//
+// Measured (Llama-3-8B shape, b = 1): correct (the parity tests run it), but
+// 3.7 ms per token against 1.8 ms for the kernel-per-op graph, so it is
+// opt-in (NEXUS_CFG_PERSISTENT).  Timestamps per phase show ~11 us of fixed
+// cost per phase -- ~3 us from the barrier to the phase's first instruction,
+// 2-3 us (6 for k = 14336) of input preparation, ~2 us of partial sums and
+// ~2.5 us of grid barrier -- while separate kernels under programmatic
+// dependent launch overlap much of that with the previous kernel.  Pulling
+// the next matrix into L2 during a phase made both paths slower.
 //
 // Shared memory per CTA: W warps x 2 ring slots of 4.5 KB (one Q4_K/Q4_0
 // tile, a Q2_K tile and its side words, or half a Q8_0 tile), then the input
@@ -51,7 +62,7 @@ namespace step {
 
 constexpr int kSlot = 9 * 512;          // ring slot bytes
 constexpr int kNst = 2;                 // ring slots per warp
-constexpr int kAttnTps = 32;            // attention: tokens per context slice, at least
+constexpr int kAttnTps = 64;            // attention: tokens per context slice, at least
 constexpr unsigned kSpin = 1u << 21;    // bounded waits (mbarrier polls, barrier polls)
 
 struct Geo {
@@ -138,9 +149,11 @@ __device__ __forceinline__ bool wait_slot(Ring &r) {
 
 // Grid barrier over the CTAs of the launch (all resident: cooperative launch).
 // bar[0] counts arrivals, bar[1] is the generation; the last CTA to arrive
-// resets the count and advances the generation.  False when it gave up or the
-// error flag is set.
-__device__ __forceinline__ bool grid_sync(unsigned *bar, int *err) {
+// resets the count and advances the generation.  False when it gave up (after
+// about a second of polling) or the error flag is set.  `extra` > 0 is the
+// fault-injection hook of the error path: the barrier then waits for CTAs that
+// do not exist, every CTA gives up, sets the flag and leaves.
+__device__ __forceinline__ bool grid_sync(unsigned *bar, int *err, unsigned extra) {
     __shared__ int s_ok;
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -149,7 +162,7 @@ __device__ __forceinline__ bool grid_sync(unsigned *bar, int *err) {
         __threadfence();
         const unsigned prev = atomicAdd(bar, 1u);
         int ok = 1;
-        if (prev == gridDim.x - 1) {
+        if (prev == gridDim.x - 1 + extra) {
             bar[0] = 0u;
             __threadfence();
             atomicAdd(bar + 1, 1u);
@@ -174,6 +187,7 @@ __device__ __forceinline__ bool grid_sync(unsigned *bar, int *err) {
 struct Smem {
     uint8_t *xs;     // input planes (GEMV phases) / attention scratch
     float *misc;     // [W] RMSNorm partial sums
+    float *red;      // [W][2][32] warp partials of shared row groups
 };
 
 template <int FMT>
@@ -185,58 +199,110 @@ __device__ __forceinline__ float dot_item(const uint8_t *slot, const XSb &x, int
     else return sb_dot_q2k<1>(c, reinterpret_cast<const uint32_t *>(slot + 5 * 512)[lane], x, 0);
 }
 
-// Row group g's sum over this warp's items is `a`: run the epilogue, or, when
-// the group's items are spread over several warps, leave the partial in global
-// memory; the arrivals count the group's items and the arrival that completes
-// them adds the partials in warp order (warps with no items hold none).
-template <int EPI>
-__device__ __noinline__ void flush(const StepParams &sp, const GemvParams &gp, int g, float a, long long T,
-                                   long long ipg, long long nw, long long gw, long long i0, long long i1, int lane) {
-    // warps holding items of group g: owner(first item) .. owner(last item),
-    // owner(i) = ((i + 1) * nw - 1) / T
-    const long long f = (((long long)g * ipg + 1) * nw - 1) / T;
-    const long long l = ((((long long)g + 1) * ipg) * nw - 1) / T;
-    if (f == l) {
-        gemv_epilogue<EPI>(gp, g, 0, lane, a);
-        return;
+// The fused epilogue of row group g (gemv_epilogue), chosen at run time so
+// that every matrix phase of a format shares one body of code.
+__device__ __noinline__ void epilogue_rt(const GemvParams &gp, int epi, int g, int lane, float tot) {
+    switch (epi) {
+    case EPI_QKV: gemv_epilogue<EPI_QKV>(gp, g, 0, lane, tot); break;
+    case EPI_ADD: gemv_epilogue<EPI_ADD>(gp, g, 0, lane, tot); break;
+    case EPI_SWIGLU: gemv_epilogue<EPI_SWIGLU>(gp, g, 0, lane, tot); break;
+    case EPI_ARGMAX: gemv_epilogue<EPI_ARGMAX>(gp, g, 0, lane, tot); break;
+    default: gemv_epilogue<EPI_STORE>(gp, g, 0, lane, tot); break;
     }
-    const int sl = ((gw * T / nw) / ipg == g) ? 0 : 1;
-    sp.gpart[((size_t)gw * 2 + sl) * 32 + lane] = a;
-    __threadfence();
-    __syncwarp();
-    const long long g0 = (long long)g * ipg, g1 = g0 + ipg;
-    const unsigned mine = (unsigned)(min(i1, g1) - max(i0, g0));
-    unsigned last = 0;
-    if (lane == 0) last = atomicAdd(&sp.gcounters[g], mine) + mine == (unsigned)ipg;
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (!last) return;
-    __threadfence();
-    float tot = 0.0f;
-    for (long long q = f; q <= l; q++) {
-        const long long s0 = q * T / nw, s1 = (q + 1) * T / nw;
-        if (s1 <= s0) continue;
-        const int s = (s0 / ipg == g) ? 0 : 1;
-        tot += __ldcg(&sp.gpart[((size_t)q * 2 + s) * 32 + lane]);
+}
+
+// Item ranges.  CTA c of the grid takes items [c*T/C, (c+1)*T/C) of a matrix;
+// warp w of the CTA takes [c0 + w*n/W, c0 + (w+1)*n/W) of the CTA's n items.
+struct Split {
+    long long c0, c1;  // this CTA's items
+    long long i0, i1;  // this warp's items
+};
+template <int W>
+__device__ __forceinline__ Split split_items(long long T, int warp) {
+    Split s;
+    const long long C = gridDim.x;
+    s.c0 = (long long)blockIdx.x * T / C;
+    s.c1 = ((long long)blockIdx.x + 1) * T / C;
+    const long long n = s.c1 - s.c0;
+    s.i0 = s.c0 + warp * n / W;
+    s.i1 = s.c0 + (warp + 1) * n / W;
+    return s;
+}
+
+// The CTA's row groups that more than one warp holds, or that other CTAs share:
+// the warps' partials (red[w][0] = the warp's first group, red[w][1] = its
+// last) are added in warp order; a group inside the CTA gets its epilogue,
+// a group crossing a CTA boundary leaves the CTA's sum in global memory and
+// the CTA whose items complete the group (an atomic item count per group) adds
+// the CTAs' sums in CTA order and runs the epilogue.  Deterministic.
+template <int W>
+__device__ __noinline__ void finish_groups(const StepParams &sp, const GemvParams &gp, int epi, const float *red,
+                                           const Split sp_, long long T, long long ipg, int warp, int lane) {
+    const long long c0 = sp_.c0, c1 = sp_.c1, n = c1 - c0;
+    if (n <= 0) return;
+    const long long gA = c0 / ipg, gB = (c1 - 1) / ipg;
+    const long long C = gridDim.x;
+    for (long long g = gA + warp; g <= gB; g += W) {
+        const long long lo = max(g * ipg, c0), hi = min((g + 1) * ipg, c1);
+        const bool inside = lo == g * ipg && hi == (g + 1) * ipg;
+        // warps of this CTA holding items of g: owner(lo) .. owner(hi - 1),
+        // owner(i) = ((i - c0 + 1) * W - 1) / n
+        const long long wf = ((lo - c0 + 1) * W - 1) / n, wl = ((hi - c0) * W - 1) / n;
+        if (wf == wl && inside) continue;  // one warp held the whole group and finished it
+        float tot = 0.0f;
+        for (long long w = wf; w <= wl; w++) {
+            const long long s0 = c0 + w * n / W, s1 = c0 + (w + 1) * n / W;
+            if (s1 <= s0) continue;
+            tot += red[((int)w * 2 + (s0 / ipg == g ? 0 : 1)) * 32 + lane];
+        }
+        if (inside) {
+            epilogue_rt(gp, epi, (int)g, lane, tot);
+            continue;
+        }
+        const int cs = g == gA ? 0 : 1;
+        sp.gpart[((size_t)blockIdx.x * 2 + cs) * 32 + lane] = tot;
+        __threadfence();
+        __syncwarp();
+        unsigned last = 0;
+        if (lane == 0) {
+            const unsigned mine = (unsigned)(hi - lo);
+            last = atomicAdd(&sp.gcounters[g], mine) + mine == (unsigned)ipg;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) continue;
+        __threadfence();
+        // CTAs holding items of g: owner((g*ipg)) .. owner((g+1)*ipg - 1), owner(i) = ((i + 1) * C - 1) / T
+        const long long cf = ((g * ipg + 1) * C - 1) / T, cl = (((g + 1) * ipg) * C - 1) / T;
+        float all = 0.0f;
+        for (long long c = cf; c <= cl; c++) {
+            const long long s0 = c * T / C, s1 = (c + 1) * T / C;
+            if (s1 <= s0) continue;
+            all += __ldcg(&sp.gpart[((size_t)c * 2 + (s0 / ipg == g ? 0 : 1)) * 32 + lane]);
+        }
+        if (lane == 0) sp.gcounters[g] = 0u;
+        epilogue_rt(gp, epi, (int)g, lane, all);
     }
-    if (lane == 0) sp.gcounters[g] = 0u;
-    gemv_epilogue<EPI>(gp, g, 0, lane, tot);
 }
 
 // One matrix phase (every thread of the CTA calls it).  The ring state comes
 // in and goes out by value so it stays in registers across the hot loop.  A
 // wait that gives up sets the error flag, which the next grid barrier reports
 // to every CTA.
-template <int W, int FMT, int EPI>
-__device__ __noinline__ Ring gemv_phase(const StepParams &sp, const GemvParams &gp, const StepMat w,
+template <int W, int FMT>
+__device__ __noinline__ Ring gemv_phase(const StepParams &sp, const GemvParams &gp, const int epi, const StepMat w,
                                         const StepMat nxt, const bool has_next, Ring r, const Smem sm) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const Geo G = geo(w);
     const int k = w.k, n_sb = G.n_sb;
-    const long long nw = (long long)gridDim.x * W, gw = (long long)blockIdx.x * W + warp;
-    long long i0, i1, n0 = 0, n1 = 0;
-    warp_range(G.items, nw, gw, i0, i1);
-    if (has_next) warp_range(geo(nxt).items, nw, gw, n0, n1);
-
+    const Split it_ = split_items<W>(G.items, warp);
+    const long long i0 = it_.i0, i1 = it_.i1;
+    long long n0 = 0, n1 = 0;
+    if (has_next) {
+        const Split nx = split_items<W>(geo(nxt).items, warp);
+        n0 = nx.i0;
+        n1 = nx.i1;
+    }
+    // the ring may still be loading this phase's first items: start on the input
     // ---- input planes (24-bit x per super-block), RMSNorm folded into u ----
     uint8_t *tb = sm.xs;
     uint32_t *zh = reinterpret_cast<uint32_t *>(tb);
@@ -265,19 +331,24 @@ __device__ __noinline__ Ring gemv_phase(const StepParams &sp, const GemvParams &
     const long long ipg = (long long)n_sb * G.halves;
     const StepMat *nptr = has_next ? &nxt : nullptr;
     float acc = 0.0f;
-    int gcur = -1;
+    long long gcur = -1;
     bool ok = true;
+    const long long gfirst = i0 / ipg;
+    auto close_group = [&](long long g, float a) {
+        if (i0 <= g * ipg && (g + 1) * ipg <= i1) epilogue_rt(gp, epi, (int)g, lane, a);  // the warp's own group
+        else sm.red[(warp * 2 + (g == gfirst ? 0 : 1)) * 32 + lane] = a;
+    };
     if (lane == 0) top_up(r, w, i0, i1 - i0, nptr, n0, n1 - n0);
     for (long long it = i0; it < i1; it++) {
         if (!wait_slot(r)) {
             ok = false;
             break;
         }
-        const int g = (int)(it / ipg);
+        const long long g = it / ipg;
         const int rem = (int)(it % ipg);
         const int s_sb = rem / G.halves, h = rem % G.halves;
         if (g != gcur) {
-            if (gcur >= 0) flush<EPI>(sp, gp, gcur, acc, G.items, ipg, nw, gw, i0, i1, lane);
+            if (gcur >= 0) close_group(gcur, acc);
             gcur = g;
             acc = 0.0f;
         }
@@ -291,23 +362,33 @@ __device__ __noinline__ Ring gemv_phase(const StepParams &sp, const GemvParams &
         __syncwarp();
         if (lane == 0) top_up(r, w, i0, i1 - i0, nptr, n0, n1 - n0);
     }
-    if (ok && gcur >= 0) flush<EPI>(sp, gp, gcur, acc, G.items, ipg, nw, gw, i0, i1, lane);
+    if (ok && gcur >= 0) close_group(gcur, acc);
     // every lane learns what lane 0 issued (the failure path drains it)
     r.issued = __shfl_sync(0xffffffffu, r.issued, 0);
     if (!ok && lane == 0) atomicExch(sp.err, 1);
+    __syncthreads();
+    if (ok) finish_groups<W>(sp, gp, epi, sm.red, it_, G.items, ipg, warp, lane);
     return r;
 }
 
-template <int W, int EPI>
-__device__ __forceinline__ Ring gemv_fmt(const StepParams &sp, const GemvParams &gp, const StepMat &w,
+template <int W>
+__device__ __forceinline__ Ring gemv_fmt(const StepParams &sp, const GemvParams &gp, int epi, const StepMat &w,
                                          const StepMat *next, Ring r, const Smem &sm) {
     const StepMat nx = next ? *next : w;
     switch (w.fmt) {
-    case 12: return gemv_phase<W, 12, EPI>(sp, gp, w, nx, next != nullptr, r, sm);
-    case 8: return gemv_phase<W, 8, EPI>(sp, gp, w, nx, next != nullptr, r, sm);
-    case 2: return gemv_phase<W, 2, EPI>(sp, gp, w, nx, next != nullptr, r, sm);
-    default: return gemv_phase<W, 10, EPI>(sp, gp, w, nx, next != nullptr, r, sm);
+    case 12: return gemv_phase<W, 12>(sp, gp, epi, w, nx, next != nullptr, r, sm);
+    case 8: return gemv_phase<W, 8>(sp, gp, epi, w, nx, next != nullptr, r, sm);
+    case 2: return gemv_phase<W, 2>(sp, gp, epi, w, nx, next != nullptr, r, sm);
+    default: return gemv_phase<W, 10>(sp, gp, epi, w, nx, next != nullptr, r, sm);
     }
+}
+
+// L2 prefetch of a small read-only vector (the next phase's RMSNorm weights)
+// while the grid barrier is pending.
+__device__ __forceinline__ void prefetch_l2(const void *p, size_t bytes) {
+    const char *c = static_cast<const char *>(p);
+    for (size_t off = (size_t)threadIdx.x * 128; off < bytes; off += (size_t)blockDim.x * 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(c + off));
 }
 
 template <int W, int G>
@@ -358,6 +439,7 @@ __global__ void __launch_bounds__(W * 32, 1) k_decode_step(StepParams sp) {
     sm.xs = smem + (size_t)W * kNst * kSlot;
     sm.misc = reinterpret_cast<float *>(
         sm.xs + x_region_bytes<W, G>(max(sp.hidden, max(sp.hq * sp.head_dim, sp.ffn))));
+    sm.red = sm.misc + 32;
     if (lane == 0) {
         for (int i = 0; i < kNst; i++) mbar_init(&full[warp][i], 1);
         mbar_init_fence();
@@ -369,10 +451,8 @@ __global__ void __launch_bounds__(W * 32, 1) k_decode_step(StepParams sp) {
     bool ok = true;
     {
         // the first matrix's first items
-        const long long nw = (long long)gridDim.x * W, gw = (long long)blockIdx.x * W + warp;
-        long long i0, i1;
-        warp_range(geo(layers[0].qkv).items, nw, gw, i0, i1);
-        if (lane == 0) top_up(r, layers[0].qkv, i0, i1 - i0, nullptr, 0, 0);
+        const Split s0 = split_items<W>(geo(layers[0].qkv).items, warp);
+        if (lane == 0) top_up(r, layers[0].qkv, s0.i0, s0.i1 - s0.i0, nullptr, 0, 0);
     }
     for (int l = 0; l < sp.num_layers && ok; l++) {
         const StepLayer &L = layers[l];
@@ -396,10 +476,10 @@ __global__ void __launch_bounds__(W * 32, 1) k_decode_step(StepParams sp) {
         g.qkv.pages = sp.pages;
         g.qkv.seqs = sp.seqs;
         g.qkv.seq_ids = sp.seq_ids;
-        r = gemv_fmt<W, EPI_QKV>(sp, g, L.qkv, &L.o, r, sm);
-        if (!(ok = grid_sync(sp.bar, sp.err))) break;
+        r = gemv_fmt<W>(sp, g, EPI_QKV, L.qkv, &L.o, r, sm);
+        if (!(ok = grid_sync(sp.bar, sp.err, sp.bar_extra))) break;
         attn_phase<W, G>(sp, L, sm.xs);
-        if (!(ok = grid_sync(sp.bar, sp.err))) break;
+        if (!(ok = grid_sync(sp.bar, sp.err, sp.bar_extra))) break;
         // o_proj + residual
         GemvParams o = {};
         o.n = H;
@@ -409,8 +489,9 @@ __global__ void __launch_bounds__(W * 32, 1) k_decode_step(StepParams sp) {
         o.x_stride = o.k;
         o.y = sp.x_hidden;
         o.y_stride = H;
-        r = gemv_fmt<W, EPI_ADD>(sp, o, L.o, &L.gateup, r, sm);
-        if (!(ok = grid_sync(sp.bar, sp.err))) break;
+        r = gemv_fmt<W>(sp, o, EPI_ADD, L.o, &L.gateup, r, sm);
+        prefetch_l2(L.ffn_norm, (size_t)H * 4);
+        if (!(ok = grid_sync(sp.bar, sp.err, sp.bar_extra))) break;
         // ffn_norm -> gate|up -> SwiGLU
         GemvParams gu = {};
         gu.n = L.gateup.n;
@@ -422,8 +503,8 @@ __global__ void __launch_bounds__(W * 32, 1) k_decode_step(StepParams sp) {
         gu.eps = sp.eps;
         gu.y = sp.gated;
         gu.y_stride = sp.ffn;
-        r = gemv_fmt<W, EPI_SWIGLU>(sp, gu, L.gateup, &L.down, r, sm);
-        if (!(ok = grid_sync(sp.bar, sp.err))) break;
+        r = gemv_fmt<W>(sp, gu, EPI_SWIGLU, L.gateup, &L.down, r, sm);
+        if (!(ok = grid_sync(sp.bar, sp.err, sp.bar_extra))) break;
         // down + residual
         GemvParams dn = {};
         dn.n = H;
@@ -433,8 +514,9 @@ __global__ void __launch_bounds__(W * 32, 1) k_decode_step(StepParams sp) {
         dn.x_stride = sp.ffn;
         dn.y = sp.x_hidden;
         dn.y_stride = H;
-        r = gemv_fmt<W, EPI_ADD>(sp, dn, L.down, l + 1 < sp.num_layers ? &layers[l + 1].qkv : &sp.head, r, sm);
-        ok = grid_sync(sp.bar, sp.err);
+        r = gemv_fmt<W>(sp, dn, EPI_ADD, L.down, l + 1 < sp.num_layers ? &layers[l + 1].qkv : &sp.head, r, sm);
+        prefetch_l2(l + 1 < sp.num_layers ? layers[l + 1].attn_norm : sp.out_norm, (size_t)H * 4);
+        ok = grid_sync(sp.bar, sp.err, sp.bar_extra);
     }
     if (ok) {
         // output norm -> LM head -> logits + greedy argmax (transformer_logits, greedy_token)
@@ -449,8 +531,8 @@ __global__ void __launch_bounds__(W * 32, 1) k_decode_step(StepParams sp) {
         hd.y = sp.logits;
         hd.y_stride = sp.head.n;
         hd.seqs = sp.seqs;
-        r = gemv_fmt<W, EPI_ARGMAX>(sp, hd, sp.head, nullptr, r, sm);
-        ok = grid_sync(sp.bar, sp.err);
+        r = gemv_fmt<W>(sp, hd, EPI_ARGMAX, sp.head, nullptr, r, sm);
+        ok = grid_sync(sp.bar, sp.err, sp.bar_extra);
     }
     if (ok) {
         if (blockIdx.x == 0 && threadIdx.x == 0) {
@@ -526,7 +608,7 @@ cudaError_t step_plan(const StepParams &p, int device, StepLaunch *out) {
         StepFn fn = step_kernel(W, G);
         if (!fn) continue;
         // ring | input planes or attention scratch | RMSNorm sums
-        const size_t smem = (size_t)W * step::kNst * step::kSlot + x_region(W, G, kmax) + 4 * 32;
+        const size_t smem = (size_t)W * step::kNst * step::kSlot + x_region(W, G, kmax) + 4 * 32 + 4 * W * 2 * 32;
         if (smem + 1024 > (size_t)optin) continue;  // + the kernel's static shared memory
         e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
@@ -542,7 +624,7 @@ cudaError_t step_plan(const StepParams &p, int device, StepLaunch *out) {
     return cudaErrorNotSupported;
 }
 
-size_t step_gpart_floats(const StepLaunch &l) { return (size_t)l.grid * l.warps * 2 * 32; }
+size_t step_gpart_floats(const StepLaunch &l) { return (size_t)l.grid * 2 * 32; }
 
 cudaError_t launch_decode_step(const StepParams &p, const StepLaunch &l, cudaStream_t st) {
     StepFn fn = step_kernel(l.warps, p.hkv > 0 ? p.hq / p.hkv : 0);
