@@ -262,6 +262,19 @@ int nexus_cuda_prefill(nexus_cuda_model *m, uint32_t seq_id, const uint32_t *tok
 int nexus_cuda_generate(nexus_cuda_model *m, uint32_t seq_id, const uint32_t *prompt, size_t n,
                         size_t max_tokens, uint32_t *out);
 
+/* generate_with_draft_tokens with greedy sampling (src/engine/mod.rs:1244-1291):
+ * out gets n + max_tokens ids, the prompt then the greedy continuation (the
+ * same tokens as nexus_cuda_generate); *accepted / *rejected count the
+ * positions p < min(n_draft, max_tokens) where draft[p] equals / differs from
+ * the generated token.  Each window of up to `window` tokens (0 = 8) -- the
+ * next verified token followed by the draft tokens after it -- is checked in
+ * one multi-token forward step (the reference decodes one token per call); the
+ * cache keeps the tokens up to the first rejected draft.  Stop sequences are
+ * not handled (greedy runs to max_tokens). */
+int nexus_cuda_generate_with_draft(nexus_cuda_model *m, uint32_t seq_id, const uint32_t *prompt, size_t n,
+                                   const uint32_t *draft, size_t n_draft, size_t max_tokens, uint32_t window,
+                                   uint32_t *out, uint32_t *accepted, uint32_t *rejected);
+
 /* KV pages.  The KV cache of every layer is a pool of max_pages pages of
  * page_tokens tokens (nexus_cuda_config); token t of a sequence lives in page
  * page_ids[t / page_tokens] of its list, at slot t % page_tokens.  A sequence

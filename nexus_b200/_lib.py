@@ -132,6 +132,8 @@ SIGNATURES = [
     ("nexus_cuda_prefill", C.c_int, [P, C.c_uint32, P, C.c_size_t, P, C.POINTER(C.c_uint32)]),
     ("nexus_cuda_generate", C.c_int, [P, C.c_uint32, P, C.c_size_t, C.c_size_t, P]),
     ("nexus_cuda_decode_batch", C.c_int, [P, C.POINTER(DecodeItem), C.c_size_t, P, P]),
+    ("nexus_cuda_generate_with_draft", C.c_int, [P, C.c_uint32, P, C.c_size_t, P, C.c_size_t, C.c_size_t,
+                                                 C.c_uint32, P, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]),
     ("nexus_cuda_last_step_ms", C.c_int, [P, C.POINTER(C.c_float)]),
     ("nexus_cuda_profile_decode", C.c_int, [P, C.c_uint32, C.c_uint32, C.c_uint32, C.POINTER(KernelProfile),
                                             C.c_int, C.POINTER(C.c_int)]),

@@ -2135,6 +2135,71 @@ extern "C" int nexus_cuda_generate(nexus_cuda_model *m, uint32_t seq_id, const u
     return NEXUS_OK;
 }
 
+// generate_with_draft_tokens at temperature 0 (src/engine/mod.rs:1244-1291):
+// the output is the greedy continuation; a draft token counts as accepted when
+// it equals the greedy token of its position.  Instead of one decode per token
+// the draft is verified in windows: the next verified token and the following
+// draft tokens run as one multi-token step (causal attention inside the step),
+// the greedy token after each of them comes back, the drafts that match are
+// kept and the cache is cut back to the first mismatch.
+extern "C" int nexus_cuda_generate_with_draft(nexus_cuda_model *m, uint32_t seq_id, const uint32_t *prompt,
+                                              size_t n, const uint32_t *draft, size_t n_draft, size_t max_tokens,
+                                              uint32_t window, uint32_t *out, uint32_t *accepted, uint32_t *rejected) {
+    if (!m || !out || (n && !prompt) || (n_draft && !draft))
+        return set_err(m ? m->b : nullptr, NEXUS_E_INVALID, "NULL argument");
+    if (seq_id >= m->max_batch) return set_err(m->b, NEXUS_E_INVALID, "bad sequence id");
+    std::lock_guard<std::mutex> lk(m->b->mu);
+    cudaSetDevice(m->b->device);
+    const uint32_t win = std::max<uint32_t>(1, std::min<uint32_t>(window ? window : 8, kMaxChunk));
+    memcpy(out, prompt, n * 4);
+    uint32_t next = 0;
+    int rc = prefill_impl(m, seq_id, prompt, n, nullptr, &next);
+    if (rc) return rc;
+    if (n == 0) next = 0;  // sample_token on empty logits returns 0 (src/engine/mod.rs:825-827)
+    if (max_tokens) {
+        rc = check_slot(m, seq_id, (uint32_t)std::min<size_t>(max_tokens, 0xffffffffu));
+        if (!rc) rc = check_position(m, n + max_tokens - 1);
+        if (rc) return rc;
+    }
+    NX_CUDA(m->b, cudaEventRecord(m->ev0, m->b->stream));
+    size_t i = 0;  // generated tokens so far; out[n + i] is the next to verify
+    StepItem it[kMaxChunk];
+    uint32_t am[kMaxChunk];
+    while (i < max_tokens) {
+        // window: the verified token, then the drafts that follow it
+        size_t w = std::min<size_t>(win, max_tokens - i);
+        if (i + 1 >= n_draft) w = 1;
+        else w = std::min(w, n_draft - i);
+        const uint32_t base = m->seq_len[seq_id];
+        std::vector<uint32_t> toks(w);
+        toks[0] = next;
+        for (size_t j = 1; j < w; j++) toks[j] = draft[i + j];
+        for (size_t p = 0; p < w;) {
+            const int mc = step_chunk(w - p);
+            for (int j = 0; j < mc; j++)
+                it[j] = {seq_id, toks[p + j], (uint32_t)(n + i + p + j), base + (uint32_t)(p + j)};
+            rc = host_step(m, it, mc, nullptr, 0, am + p);
+            if (rc) return rc;
+            p += mc;
+        }
+        // keep the verified token and every draft that matches the greedy token before it
+        size_t J = 1;
+        while (J < w && toks[J] == am[J - 1]) J++;
+        for (size_t j = 0; j < J; j++) out[n + i + j] = toks[j];
+        m->seq_len[seq_id] = base + (uint32_t)J;  // drop the K/V of a rejected draft
+        next = am[J - 1];
+        i += J;
+    }
+    cudaEventRecord(m->ev1, m->b->stream);
+    cudaEventSynchronize(m->ev1);
+    cudaEventElapsedTime(&m->last_ms, m->ev0, m->ev1);
+    uint32_t acc = 0, rej = 0;
+    for (size_t p = 0; p < std::min(n_draft, max_tokens); p++) (draft[p] == out[n + p] ? acc : rej)++;
+    if (accepted) *accepted = acc;
+    if (rejected) *rejected = rej;
+    return NEXUS_OK;
+}
+
 extern "C" int nexus_cuda_decode_batch(nexus_cuda_model *m, const nexus_decode_item *items, size_t n,
                                        uint32_t *out_tokens, float *out_logits) {
     if (!m || (n && !items)) return set_err(m ? m->b : nullptr, NEXUS_E_INVALID, "NULL argument");

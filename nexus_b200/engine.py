@@ -328,6 +328,20 @@ class InferenceEngine:
                                               _ptr(out)), self.backend.handle)
         return out.tolist()
 
+    def generate_with_draft_tokens(self, prompt: Sequence[int], max_tokens: int, draft: Sequence[int],
+                                   window: int = 8, seq_id: int = 0) -> tuple[list[int], tuple[int, int]]:
+        """generate_with_draft_tokens at temperature 0 (src/engine/mod.rs:1244-1291):
+        returns (prompt + greedy continuation, (accepted, rejected)); draft
+        windows are verified in one multi-token step each."""
+        p = np.ascontiguousarray(np.asarray(prompt, np.uint32))
+        d = np.ascontiguousarray(np.asarray(draft, np.uint32))
+        out = np.zeros(p.size + max_tokens, np.uint32)
+        acc, rej = C.c_uint32(), C.c_uint32()
+        L.check(self._lib.nexus_cuda_generate_with_draft(self.model, seq_id, _ptr(p) if p.size else None, p.size,
+                                                         _ptr(d) if d.size else None, d.size, max_tokens, window,
+                                                         _ptr(out), C.byref(acc), C.byref(rej)), self.backend.handle)
+        return out.tolist(), (acc.value, rej.value)
+
     def decode_batch(self, items: Sequence[tuple[int, int, int]], want_logits: bool = False,
                      page_ids: Optional[Sequence[Sequence[int]]] = None):
         """items: (seq_id, token, position) per sequence; page_ids: optional

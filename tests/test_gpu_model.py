@@ -231,3 +231,44 @@ def test_head_dim_128_single_token_paths(nb, oracle, persistent):
     assert e.generate(p, 12) == m.generate(p, 12)
     e.close()
     b.close()
+
+
+@pytest.mark.parametrize("window", [1, 4, 8, 32])
+def test_generate_with_draft_tokens(nb, oracle, tiny_path, window):
+    """generate_with_draft_tokens at temperature 0 (src/engine/mod.rs:1244-1291):
+    the output is the greedy continuation whatever the draft; accepted counts the
+    draft positions equal to it.  Windows of draft tokens are verified in one
+    multi-token step each (8+ tokens on the tensor-core GEMM)."""
+    b = nb.CudaBackend(device=0, max_seq_len=256)
+    e = nb.InferenceEngine(b)
+    e.load_model(tiny_path)
+    m = oracle.Model(tiny_path)
+    p = prompt(8, 30, 4096)
+    ref = m.generate(p, 24)
+    good = ref[30:]
+    bad = list(good[:20])
+    for q in (2, 9, 15):
+        bad[q] = (bad[q] + 1) % 4096
+    for draft, want in [(good, (24, 0)), (bad, (17, 3)), ([], (0, 0)), (good + [5] * 10, (24, 0))]:
+        out, stats = e.generate_with_draft_tokens(p, 24, draft, window=window)
+        assert out == ref
+        assert stats == want
+        assert e.seq_len() == 30 + 24
+    e.close()
+    b.close()
+
+
+def test_generate_with_draft_tokens_head_dim_128(nb, oracle):
+    path = nb.model_path("tp_small")
+    b = nb.CudaBackend(device=0, max_seq_len=128)
+    e = nb.InferenceEngine(b)
+    e.load_model(path)
+    m = oracle.Model(path, threads=os.cpu_count() or 1, max_seq_len=128)
+    p = prompt(9, 17, 8192)
+    ref = m.generate(p, 20)
+    draft = list(ref[17:])
+    draft[11] = (draft[11] + 7) % 8192
+    out, stats = e.generate_with_draft_tokens(p, 20, draft, window=8)
+    assert out == ref and stats == (19, 1)
+    e.close()
+    b.close()
