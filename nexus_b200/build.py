@@ -33,6 +33,7 @@ UNITS = {
     "kernels_gemm.cu": [],
     "kernels_attn.cu": [],
     "kernels_attn_pk.cu": [],
+    "kernels_attn_prefill.cu": [],
     "kernels_step.cu": [],
     "kernels_misc.cu": [],
     "engine.cu": [],

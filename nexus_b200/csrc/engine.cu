@@ -994,6 +994,7 @@ struct nexus_cuda_model {
     int nsplit[kMaxChunk + 1] = {};     // attention slices per (sequence, KV head), float cache
     int nsplit_pk[kMaxChunk + 1] = {};  // the same for the packed-cache tensor-core kernel
     cudaGraphExec_t graph[kMaxChunk + 1] = {};
+    cudaGraphExec_t graph_chunk[kMaxChunk + 1] = {};  // steps of one sequence's consecutive tokens
     bool use_graph = true, use_pdl = true;
     // single-token steps as one persistent kernel (kernels_step.cu)
     bool use_step = false;
@@ -1020,6 +1021,8 @@ static void model_release(nexus_cuda_model *m) {
     cudaSetDevice(m->b->device);
     cudaStreamSynchronize(m->b->stream);
     for (auto &g : m->graph)
+        if (g) cudaGraphExecDestroy(g);
+    for (auto &g : m->graph_chunk)
         if (g) cudaGraphExecDestroy(g);
     for (auto &L : m->layers) {
         L.qkv.release();
@@ -1601,7 +1604,9 @@ static int step_chunk(size_t remaining) {
 }
 
 // Enqueue one fused decode step for `mc` tokens whose DevSeq entries are on the device.
-static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof = nullptr) {
+// chunk: the mc tokens are consecutive positions of one sequence (a prefill
+// chunk or a draft window), so attention runs as one causal chunk kernel.
+static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof = nullptr, bool chunk = false) {
     const nexus_cuda_model_info &I = m->info;
     cudaStream_t st = m->b->stream;
     // this rank's share of heads and FFN rows (all of them without tensor parallelism)
@@ -1726,7 +1731,9 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         a.counters = m->counters;
         a.pdl = pdl;
         if (prof) prof->begin();
-        if ((e = launch_attention(a, st)) != cudaSuccess) return e;
+        if (chunk && mc > 1 && attention_prefill_supported(a)) e = launch_attention_prefill(a, st);
+        else e = launch_attention(a, st);
+        if (e != cudaSuccess) return e;
         if (prof) prof->end("attention", attn_bytes);
         // o_proj + residual
         GemvParams o = {};
@@ -1857,34 +1864,36 @@ static cudaError_t enqueue_persistent_step(nexus_cuda_model *m, StepProfiler *pr
     return e;
 }
 
-static int run_step(nexus_cuda_model *m, int mc) {
+static int run_step(nexus_cuda_model *m, int mc, bool chunk = false) {
     nexus_cuda_backend *b = m->b;
     cudaStream_t st = b->stream;
     if (mc == 1 && m->use_step) {
         NX_CUDA(b, enqueue_persistent_step(m));
         return NEXUS_OK;
     }
+    chunk = chunk && mc > 1;
+    cudaGraphExec_t *graphs = chunk ? m->graph_chunk : m->graph;
     if (m->use_graph && m->has_head) {
-        if (!m->graph[mc]) {
+        if (!graphs[mc]) {
             cudaGraph_t g = nullptr;
             NX_CUDA(b, cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-            cudaError_t e = enqueue_step(m, mc);
+            cudaError_t e = enqueue_step(m, mc, nullptr, chunk);
             cudaError_t e2 = cudaStreamEndCapture(st, &g);
             if (e != cudaSuccess || e2 != cudaSuccess) {
                 if (g) cudaGraphDestroy(g);
                 return set_err(b, NEXUS_E_CUDA, std::string("graph capture: ") +
                                                    cudaGetErrorString(e != cudaSuccess ? e : e2));
             }
-            e = cudaGraphInstantiate(&m->graph[mc], g, 0);
+            e = cudaGraphInstantiate(&graphs[mc], g, 0);
             cudaGraphDestroy(g);
             if (e != cudaSuccess) {
-                m->graph[mc] = nullptr;
+                graphs[mc] = nullptr;
                 return set_err(b, NEXUS_E_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
             }
         }
-        NX_CUDA(b, cudaGraphLaunch(m->graph[mc], st));
+        NX_CUDA(b, cudaGraphLaunch(graphs[mc], st));
     } else {
-        NX_CUDA(b, enqueue_step(m, mc));
+        NX_CUDA(b, enqueue_step(m, mc, nullptr, chunk));
     }
     return NEXUS_OK;
 }
@@ -1923,7 +1932,10 @@ static int host_step(nexus_cuda_model *m, const StepItem *items, int mc, float *
     NX_CUDA(b, pages_upload(m));
     NX_CUDA(b, cudaMemcpyAsync(m->seqs, m->h_seqs, mc * sizeof(DevSeq), cudaMemcpyHostToDevice, st));
     NX_CUDA(b, cudaMemcpyAsync(m->seq_ids, m->h_seq_ids, mc * 4, cudaMemcpyHostToDevice, st));
-    int rc = run_step(m, mc);
+    bool chunk = true;  // one sequence, consecutive slots
+    for (int t = 1; t < mc; t++)
+        chunk = chunk && items[t].sid == items[0].sid && items[t].slot == items[0].slot + (uint32_t)t;
+    int rc = run_step(m, mc, chunk);
     if (rc) return rc;
     const size_t V = m->info.vocab_rows;
     std::vector<float> gathered;

@@ -131,6 +131,11 @@ cudaError_t launch_attention(const AttnParams &p, cudaStream_t st);
 // 128, G in {1, 2, 4, 8}, bits in {2, 3, 4, 6, 8}; launch_attention routes there
 bool attention_pk_supported(const AttnParams &p);
 cudaError_t launch_attention_pk(const AttnParams &p, cudaStream_t st);
+// causal attention for m consecutive tokens of one sequence (seqs[0].slot is
+// the first token's slot) on the tensor cores (kernels_attn_prefill.cu):
+// float cache, head_dim 128, G in {1, 2, 4, 8}
+bool attention_prefill_supported(const AttnParams &p);
+cudaError_t launch_attention_prefill(const AttnParams &p, cudaStream_t st);
 
 // packed KV append (PackedKvBuffer::add, src/engine/mod.rs:209-232) for m tokens
 struct KvPackParams {
