@@ -120,6 +120,31 @@ def test_qgemm_batched(backend, oracle, nb, shape, m, fmt):
     w.close()
 
 
+@pytest.mark.parametrize("fmt", FORMATS)
+@pytest.mark.parametrize("shape", SWEEP, ids=lambda s: f"{s[0]}x{s[1]}")
+def test_qgemm_sweep_shapes_all_batches(backend, oracle, nb, shape, fmt):
+    """Config S in full on the tensor-core path: all five weight shapes, all
+    four formats, M in {16, 64, 512} (and the GEMV's 1 and 4 above); tokens 0,
+    M/2 and M-1 against the oracle's sequential f32 matvec.  The 128256-row
+    head repeats 4096 drawn rows (quantizing 525M values would dominate the
+    test); every other shape is drawn in full."""
+    n, k = shape
+    rng = np.random.default_rng(90 + n + k)
+    if n > 16384:
+        base = oracle.quantize(getattr(oracle, fmt), weights(rng, 4096 * k))
+        q = np.tile(base.reshape(4096, -1), (n // 4096 + 1, 1))[:n].reshape(-1)
+    else:
+        q = oracle.quantize(getattr(oracle, fmt), weights(rng, n * k))
+    w = nb.QWeight(backend, getattr(nb, fmt), n, k, q)
+    for m in (16, 64, 512):
+        x = rng.standard_normal((m, k)).astype(np.float32)
+        y = w.matvec(x)
+        for t in sorted({0, m // 2, m - 1}):
+            ref = oracle.qmatvec(getattr(oracle, fmt), q, n, k, x[t], threads=16)
+            assert rel_err(y[t], ref) < REL_TOL, (m, t, rel_err(y[t], ref))
+    w.close()
+
+
 @pytest.mark.parametrize("fmt", ["Q8_0", "Q4_0"])
 @pytest.mark.parametrize("m", [33, 64, 130])
 def test_qgemm_wide_matrix_token_tile(backend, oracle, nb, m, fmt):
