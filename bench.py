@@ -636,8 +636,8 @@ def main():
         "config": {"workload": f"{args.config}: prompt {PROMPT_LEN} (seed {SEED_PROMPT}), greedy decode b=1, "
                                f"context {PROMPT_LEN}-{PROMPT_LEN + args.warmup + args.steps}",
                    "model": args.config, "global_batch": 1, "seq_len": PROMPT_LEN + GEN_TOKENS,
-                   "parallelism": f"tp{world} (heads, FFN and vocab rows per rank; NCCL all-reduce per sublayer)"
-                   if world > 1 else "single GPU",
+                   "parallelism": f"tp{world} (heads, FFN and vocab rows per rank; one all-reduce per sublayer, "
+                                  f"{backend.tp_allreduce_kind()})" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2: every step streams all weights "
                          f"({info.weight_bytes / 1e9:.3f} GB) from HBM",
                    "weight_bytes_per_token": info.weight_bytes},

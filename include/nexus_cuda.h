@@ -91,12 +91,16 @@ typedef struct {
     uint32_t max_pages;    /* KV pages in the pool per rank; 0 = max_batch * ceil(max_seq_len /
                               page_tokens) (every sequence can hold max_seq_len tokens) */
     uint32_t flags;        /* NEXUS_CFG_* */
+    uint32_t tp_timeout_ms; /* tensor parallelism: how long nexus_cuda_tp_init waits for every
+                               rank to join before it gives up with NEXUS_E_COMM; 0 = 120 s */
 } nexus_cuda_config;
 
 #define NEXUS_CFG_NO_GRAPH 0x1u  /* launch kernels directly instead of a CUDA graph */
 #define NEXUS_CFG_NO_PDL 0x2u    /* no programmatic dependent launch between kernels */
 #define NEXUS_CFG_PERSISTENT 0x4u /* single-token steps on the persistent whole-step kernel
                                      (one launch per token) instead of the kernel-per-op graph */
+#define NEXUS_CFG_NCCL_ALLREDUCE 0x8u /* tensor parallelism: NCCL for every all-reduce instead of
+                                        the one-shot peer-memory all-reduce of the hidden state */
 #define NEXUS_CFG_FAULT_STALL_BARRIER 0x100u /* fault injection for tests of the error path: the
                                      persistent step kernel's grid barrier waits for a CTA that does
                                      not exist, so every step gives up after its bounded wait (about
@@ -125,11 +129,23 @@ const char *nexus_cuda_last_error(const nexus_cuda_backend *b);
  * rank (e.g. over torch.distributed), and each rank calls tp_init on its
  * backend before nexus_cuda_model_load.  Layers are then sharded: query/KV
  * heads, FFN rows and LM-head rows per rank; o_proj and down are column
- * slices whose partial sums meet in one all-reduce per sublayer (NCCL, loaded
- * at tp_init).  Every rank must make the same model calls in the same order. */
+ * slices whose partial sums meet in one all-reduce per sublayer (over peer
+ * memory, or NCCL, loaded at tp_init).  Every rank must make the same model
+ * calls in the same order.  tp_init returns NEXUS_E_COMM when not every rank
+ * joined within tp_timeout_ms (the group is then torn down on this rank). */
 #define NEXUS_TP_ID_BYTES 128
 int nexus_cuda_tp_unique_id(void *id, size_t id_bytes);
 int nexus_cuda_tp_init(nexus_cuda_backend *b, int rank, int world, const void *id, size_t id_bytes);
+/* How the hidden-state all-reduces of a tensor-parallel backend run:
+ * NEXUS_TP_NONE (not initialised or world 1), NEXUS_TP_NCCL, or
+ * NEXUS_TP_PEER -- one kernel per all-reduce over NVLink peer memory (CUDA IPC
+ * mapped staging buffers and flags, bounded waits), set up at tp_init unless
+ * NEXUS_CFG_NCCL_ALLREDUCE is given or a peer cannot be mapped.  The sampled
+ * logits' all-gather runs on NCCL either way. */
+#define NEXUS_TP_NONE 0
+#define NEXUS_TP_NCCL 1
+#define NEXUS_TP_PEER 2
+int nexus_cuda_tp_allreduce_kind(const nexus_cuda_backend *b);
 
 /* The slice of a model one rank holds (host-only arithmetic, no device). */
 typedef struct nexus_tp_slice {

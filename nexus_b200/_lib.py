@@ -42,6 +42,8 @@ OP_ATTENTION_PACKED = 13
 CFG_NO_GRAPH = 0x1
 CFG_NO_PDL = 0x2
 CFG_PERSISTENT = 0x4
+CFG_NCCL_ALLREDUCE = 0x8
+TP_NONE, TP_NCCL, TP_PEER = 0, 1, 2
 CFG_FAULT_STALL_BARRIER = 0x100
 
 
@@ -54,7 +56,7 @@ class Caps(C.Structure):
 class Config(C.Structure):
     _fields_ = [("device", C.c_int), ("tp", C.c_int), ("kv_bits_k", C.c_uint32), ("kv_bits_v", C.c_uint32),
                 ("max_batch", C.c_uint32), ("max_seq_len", C.c_uint32), ("page_tokens", C.c_uint32),
-                ("max_pages", C.c_uint32), ("flags", C.c_uint32)]
+                ("max_pages", C.c_uint32), ("flags", C.c_uint32), ("tp_timeout_ms", C.c_uint32)]
 
 
 class Op(C.Structure):
@@ -112,6 +114,7 @@ SIGNATURES = [
     ("nexus_cuda_last_error", C.c_char_p, [P]),
     ("nexus_cuda_tp_unique_id", C.c_int, [P, C.c_size_t]),
     ("nexus_cuda_tp_init", C.c_int, [P, C.c_int, C.c_int, P, C.c_size_t]),
+    ("nexus_cuda_tp_allreduce_kind", C.c_int, [P]),
     ("nexus_tp_plan", C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_int, C.c_int,
                                 C.POINTER(TpSlice)]),
     ("nexus_cuda_execute", C.c_int, [P, C.POINTER(Op)]),

@@ -35,6 +35,7 @@ UNITS = {
     "kernels_attn_pk.cu": [],
     "kernels_attn_prefill.cu": [],
     "kernels_step.cu": [],
+    "kernels_peer.cu": [],
     "kernels_misc.cu": [],
     "engine.cu": [],
     "noalloc.cu": [],

@@ -15,6 +15,8 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <chrono>
+#include <thread>
 #include <vector>
 
 #include "../../include/nexus_cuda.h"
@@ -47,6 +49,15 @@ struct nexus_cuda_backend {
     // tensor parallelism (nexus_cuda_tp_init)
     int tp_rank = 0, tp_world = 1;
     ncclComm_t comm = nullptr;
+    // one-shot peer-memory all-reduce of the hidden state (kernels_peer.cu):
+    // this rank's staging buffers and flags, the peers' mapped through CUDA IPC
+    bool peer_ok = false;
+    bool tp_failed = false;
+    PeerReduce peer = {};
+    float *peer_buf = nullptr;        // [2][max_floats]
+    unsigned *peer_flags = nullptr;   // [kPeerCtas][2]
+    unsigned *peer_epoch = nullptr;   // [kPeerCtas]
+    std::vector<void *> peer_mapped;  // peers' buffers opened with cudaIpcOpenMemHandle
 };
 
 // NCCL is opened at nexus_cuda_tp_init (no link-time dependency).
@@ -58,6 +69,12 @@ struct NcclApi {
     ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
     const char *(*error_string)(ncclResult_t) = nullptr;
+    // for a bounded wait on the ranks joining (optional: without them the
+    // join waits as long as ncclCommInitRank does)
+    ncclResult_t (*comm_init_rank_config)(ncclComm_t *, int, ncclUniqueId, int, ncclConfig_t *) = nullptr;
+    ncclResult_t (*comm_split)(ncclComm_t, int, int, ncclComm_t *, ncclConfig_t *) = nullptr;
+    ncclResult_t (*get_async_error)(ncclComm_t, ncclResult_t *) = nullptr;
+    ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
     bool ok = false;
 };
 
@@ -78,6 +95,10 @@ static NcclApi *nccl_api(std::string *why) {
         api.all_gather = (decltype(api.all_gather))dlsym(h, "ncclAllGather");
         api.comm_destroy = (decltype(api.comm_destroy))dlsym(h, "ncclCommDestroy");
         api.error_string = (decltype(api.error_string))dlsym(h, "ncclGetErrorString");
+        api.comm_init_rank_config = (decltype(api.comm_init_rank_config))dlsym(h, "ncclCommInitRankConfig");
+        api.comm_split = (decltype(api.comm_split))dlsym(h, "ncclCommSplit");
+        api.get_async_error = (decltype(api.get_async_error))dlsym(h, "ncclCommGetAsyncError");
+        api.comm_abort = (decltype(api.comm_abort))dlsym(h, "ncclCommAbort");
         api.ok = api.get_unique_id && api.comm_init_rank && api.all_reduce && api.all_gather && api.comm_destroy &&
                  api.error_string;
         if (!api.ok) load_error = "NCCL library lacks a required symbol";
@@ -88,6 +109,18 @@ static NcclApi *nccl_api(std::string *why) {
 
 static std::mutex g_backend_mu;
 
+static void peer_release(nexus_cuda_backend *b) {
+    for (void *p : b->peer_mapped) cudaIpcCloseMemHandle(p);
+    b->peer_mapped.clear();
+    if (b->peer_buf) cudaFree(b->peer_buf);
+    if (b->peer_flags) cudaFree(b->peer_flags);
+    if (b->peer_epoch) cudaFree(b->peer_epoch);
+    b->peer_buf = nullptr;
+    b->peer_flags = nullptr;
+    b->peer_epoch = nullptr;
+    b->peer_ok = false;
+}
+
 static void backend_free_now(nexus_cuda_backend *b) {
     cudaSetDevice(b->device);
     if (b->stream) {
@@ -95,6 +128,7 @@ static void backend_free_now(nexus_cuda_backend *b) {
         cudaStreamDestroy(b->stream);
     }
     if (b->dev_err) cudaFree(b->dev_err);
+    peer_release(b);
     if (b->comm) {
         if (NcclApi *api = nccl_api(nullptr)) api->comm_destroy(b->comm);
     }
@@ -431,6 +465,83 @@ extern "C" int nexus_cuda_tp_unique_id(void *id, size_t id_bytes) {
     return NEXUS_OK;
 }
 
+// Polls a nonblocking communicator's pending call (on the host) until it
+// settles or `limit_ms` passes; ncclInProgress means the limit passed.
+static ncclResult_t nccl_settle(NcclApi *api, ncclComm_t *comm, ncclResult_t r, uint32_t limit_ms) {
+    const auto t0 = std::chrono::steady_clock::now();
+    while (r == ncclInProgress) {
+        const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0);
+        if (ms.count() > (long long)limit_ms) return ncclInProgress;
+        std::this_thread::sleep_for(std::chrono::milliseconds(1));
+        ncclResult_t st = ncclSuccess;
+        const ncclResult_t q = *comm ? api->get_async_error(*comm, &st) : ncclInvalidArgument;
+        r = q != ncclSuccess ? q : st;
+    }
+    return r;
+}
+
+// Staging buffers and flags for the one-shot all-reduce, mapped into every
+// peer: each rank's CUDA IPC handles are all-gathered over NCCL and opened.
+static constexpr size_t kPeerMaxFloats = 1u << 20;  // 4 MB: up to 256 tokens of H = 4096
+static cudaError_t peer_setup(nexus_cuda_backend *b, NcclApi *api) {
+    const int world = b->tp_world, rank = b->tp_rank;
+    cudaError_t e = dalloc(&b->peer_buf, 2 * kPeerMaxFloats);
+    if (e == cudaSuccess) e = dalloc(&b->peer_flags, (size_t)2 * kPeerCtas);
+    if (e == cudaSuccess) e = dalloc(&b->peer_epoch, (size_t)kPeerCtas);
+    if (e == cudaSuccess) e = cudaMemset(b->peer_flags, 0, (size_t)2 * kPeerCtas * 4);
+    if (e == cudaSuccess) e = cudaMemset(b->peer_epoch, 0, (size_t)kPeerCtas * 4);
+    if (e != cudaSuccess) return e;
+    cudaIpcMemHandle_t h[2];
+    if ((e = cudaIpcGetMemHandle(&h[0], b->peer_buf)) != cudaSuccess) return e;
+    if ((e = cudaIpcGetMemHandle(&h[1], b->peer_flags)) != cudaSuccess) return e;
+    uint8_t *dh = nullptr;
+    const size_t hb = sizeof(h);
+    if ((e = dalloc(&dh, (size_t)world * hb)) != cudaSuccess) return e;
+    std::vector<uint8_t> all((size_t)world * hb);
+    e = cudaMemcpy(dh + (size_t)rank * hb, h, hb, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) {
+        ncclResult_t r = api->all_gather(dh + (size_t)rank * hb, dh, hb, ncclUint8, b->comm, b->stream);
+        e = r == ncclSuccess ? cudaStreamSynchronize(b->stream) : cudaErrorUnknown;
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(all.data(), dh, all.size(), cudaMemcpyDeviceToHost);
+    cudaFree(dh);
+    if (e != cudaSuccess) return e;
+    PeerReduce &pr = b->peer;
+    pr = PeerReduce{};
+    for (int r = 0; r < world; r++) {
+        if (r == rank) {
+            pr.bufs[r][0] = b->peer_buf;
+            pr.bufs[r][1] = b->peer_buf + kPeerMaxFloats;
+            pr.flags[r] = b->peer_flags;
+            continue;
+        }
+        cudaIpcMemHandle_t ph[2];
+        memcpy(ph, all.data() + (size_t)r * hb, hb);
+        void *pb = nullptr, *pf = nullptr;
+        if ((e = cudaIpcOpenMemHandle(&pb, ph[0], cudaIpcMemLazyEnablePeerAccess)) != cudaSuccess) return e;
+        b->peer_mapped.push_back(pb);
+        if ((e = cudaIpcOpenMemHandle(&pf, ph[1], cudaIpcMemLazyEnablePeerAccess)) != cudaSuccess) return e;
+        b->peer_mapped.push_back(pf);
+        pr.bufs[r][0] = static_cast<float *>(pb);
+        pr.bufs[r][1] = static_cast<float *>(pb) + kPeerMaxFloats;
+        pr.flags[r] = static_cast<unsigned *>(pf);
+    }
+    pr.epoch = b->peer_epoch;
+    pr.rank = rank;
+    pr.world = world;
+    pr.max_floats = kPeerMaxFloats;
+    // every rank has mapped every peer before the first all-reduce
+    ncclResult_t r = api->all_reduce(b->peer_epoch, b->peer_epoch, 1, ncclUint32, ncclMax, b->comm, b->stream);
+    e = r == ncclSuccess ? cudaStreamSynchronize(b->stream) : cudaErrorUnknown;
+    if (e == cudaSuccess) b->peer_ok = true;
+    return e;
+}
+
+extern "C" int nexus_cuda_tp_allreduce_kind(const nexus_cuda_backend *b) {
+    if (!b || b->tp_world < 2) return NEXUS_TP_NONE;
+    return b->peer_ok ? NEXUS_TP_PEER : NEXUS_TP_NCCL;
+}
+
 extern "C" int nexus_cuda_tp_init(nexus_cuda_backend *b, int rank, int world, const void *id, size_t id_bytes) {
     if (!b || !id || id_bytes < sizeof(ncclUniqueId) || world < 1 || rank < 0 || rank >= world)
         return set_err(b, NEXUS_E_INVALID, "tp init: bad argument");
@@ -442,13 +553,51 @@ extern "C" int nexus_cuda_tp_init(nexus_cuda_backend *b, int rank, int world, co
     cudaSetDevice(b->device);
     ncclUniqueId u;
     memcpy(&u, id, sizeof(u));
-    ncclResult_t r = api->comm_init_rank(&b->comm, world, u, rank);
-    if (r != ncclSuccess) {
-        b->comm = nullptr;
-        return set_err(b, NEXUS_E_COMM, std::string("ncclCommInitRank: ") + api->error_string(r));
+    const uint32_t limit_ms = b->cfg.tp_timeout_ms ? b->cfg.tp_timeout_ms : 120000u;
+    if (api->comm_init_rank_config && api->comm_split && api->get_async_error && api->comm_abort) {
+        // Join on a nonblocking communicator, polled against the limit, then
+        // split off a blocking one over the same ranks for the decode steps
+        // (whose collectives are captured in CUDA graphs).
+        ncclConfig_t nb = NCCL_CONFIG_INITIALIZER;
+        nb.blocking = 0;
+        ncclComm_t boot = nullptr;
+        ncclResult_t r = nccl_settle(api, &boot, api->comm_init_rank_config(&boot, world, u, rank, &nb), limit_ms);
+        if (r != ncclSuccess) {
+            if (boot) api->comm_abort(boot);
+            cudaGetLastError();
+            if (r == ncclInProgress)
+                return set_err(b, NEXUS_E_COMM, "tp init: not every rank joined within " + std::to_string(limit_ms) +
+                                                     " ms (group torn down on this rank)");
+            return set_err(b, NEXUS_E_COMM, std::string("ncclCommInitRankConfig: ") + api->error_string(r));
+        }
+        ncclConfig_t bl = NCCL_CONFIG_INITIALIZER;
+        bl.blocking = 1;
+        ncclComm_t comm = nullptr;
+        r = api->comm_split(boot, 0, rank, &comm, &bl);
+        if (r == ncclInProgress) r = nccl_settle(api, &comm, r, limit_ms);
+        api->comm_abort(boot);
+        if (r != ncclSuccess || !comm) {
+            if (comm) api->comm_abort(comm);
+            cudaGetLastError();
+            return set_err(b, NEXUS_E_COMM, std::string("ncclCommSplit: ") + api->error_string(r));
+        }
+        b->comm = comm;
+    } else {
+        ncclResult_t r = api->comm_init_rank(&b->comm, world, u, rank);
+        if (r != ncclSuccess) {
+            b->comm = nullptr;
+            return set_err(b, NEXUS_E_COMM, std::string("ncclCommInitRank: ") + api->error_string(r));
+        }
     }
     b->tp_rank = rank;
     b->tp_world = world;
+    if (!(b->cfg.flags & NEXUS_CFG_NCCL_ALLREDUCE) && world <= kPeerMaxRanks) {
+        // the peer-memory all-reduce; on any failure the NCCL all-reduce stays in use
+        if (peer_setup(b, api) != cudaSuccess) {
+            peer_release(b);
+            cudaGetLastError();
+        }
+    }
     return NEXUS_OK;
 }
 
@@ -1619,6 +1768,11 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
     // residual, the others store their part, and the all-reduce sums them
     auto reduce_hidden = [&]() -> cudaError_t {
         if (!tp) return cudaSuccess;
+        if (m->b->peer_ok && (size_t)mc * H <= m->b->peer.max_floats) {
+            PeerReduce pr = m->b->peer;
+            pr.err = reinterpret_cast<int *>(m->out_tokens + kMaxChunk);
+            return launch_peer_allreduce(pr, m->hidden, (size_t)mc * H, st);
+        }
         ncclResult_t r = nccl->all_reduce(m->hidden, m->hidden, (size_t)mc * H, ncclFloat32, ncclSum, m->b->comm, st);
         return r == ncclSuccess ? cudaSuccess : cudaErrorUnknown;
     };
@@ -1867,6 +2021,9 @@ static cudaError_t enqueue_persistent_step(nexus_cuda_model *m, StepProfiler *pr
 static int run_step(nexus_cuda_model *m, int mc, bool chunk = false) {
     nexus_cuda_backend *b = m->b;
     cudaStream_t st = b->stream;
+    if (b->tp_failed)
+        return set_err(b, NEXUS_E_TIMEOUT, "an earlier all-reduce gave up on a peer: the tensor-parallel group is "
+                                           "out of step; free the backend and build a new group");
     if (mc == 1 && m->use_step) {
         NX_CUDA(b, enqueue_persistent_step(m));
         return NEXUS_OK;
@@ -1908,7 +2065,9 @@ static int device_timeout(nexus_cuda_model *m) {
         cudaMemsetAsync(m->step.attn_counters, 0, (size_t)m->step.hkv * 4, m->b->stream);
     }
     cudaStreamSynchronize(m->b->stream);
-    return set_err(m->b, NEXUS_E_TIMEOUT, "a device wait timed out (weight stream did not arrive)");
+    // the ranks no longer agree on how many all-reduces have run
+    if (m->b->tp_world > 1) m->b->tp_failed = true;
+    return set_err(m->b, NEXUS_E_TIMEOUT, "a device wait timed out (weight stream or a peer did not arrive)");
 }
 
 // Host-driven step over `items` (at most kMaxChunk), results to host.

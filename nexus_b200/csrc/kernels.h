@@ -200,6 +200,20 @@ cudaError_t step_plan(const StepParams &p, int device, StepLaunch *out);
 size_t step_gpart_floats(const StepLaunch &l);
 cudaError_t launch_decode_step(const StepParams &p, const StepLaunch &l, cudaStream_t st);
 
+// ---- kernels_peer.cu: one-shot all-reduce over NVLink peer memory (TP) ----
+constexpr int kPeerMaxRanks = 8;
+constexpr int kPeerCtas = 32;
+struct PeerReduce {
+    float *bufs[kPeerMaxRanks][2];   // every rank's two staging buffers (peer mappings for the others)
+    unsigned *flags[kPeerMaxRanks];  // every rank's epoch flags [kPeerCtas][2]
+    unsigned *epoch;                 // this rank's epoch per CTA [kPeerCtas]
+    int rank, world;
+    size_t max_floats;               // capacity of one staging buffer
+    int *err;                        // set when a peer's flag never arrives
+};
+// x[0..n) <- the sum over ranks of every rank's x (rank order, bit-identical on all ranks)
+cudaError_t launch_peer_allreduce(const PeerReduce &pr, float *x, size_t n, cudaStream_t st);
+
 // ---- kernels_misc.cu ----
 // embedding row gather with bit-exact dequantization; also resets seqs[t].best
 struct EmbedParams {

@@ -59,7 +59,8 @@ class CudaBackend:
     """``Backend`` trait implementation for BackendType::Cuda."""
 
     def __init__(self, device: int = 0, kv_bits: tuple[int, int] = (0, 0), max_batch: int = 1,
-                 max_seq_len: int = 0, flags: int = 0, page_tokens: int = 0, max_pages: int = 0):
+                 max_seq_len: int = 0, flags: int = 0, page_tokens: int = 0, max_pages: int = 0,
+                 tp_timeout_ms: int = 0):
         lib = L.load()
         cfg = L.Config()
         lib.nexus_cuda_config_default(C.byref(cfg))
@@ -71,6 +72,7 @@ class CudaBackend:
         if page_tokens:
             cfg.page_tokens = page_tokens
         cfg.max_pages = max_pages
+        cfg.tp_timeout_ms = tp_timeout_ms
         h = C.c_void_p()
         L.check(lib.nexus_cuda_backend_create(C.byref(cfg), C.byref(h)))
         self._lib = lib
@@ -81,6 +83,11 @@ class CudaBackend:
         """Join the tensor-parallel group `uid` (from tp_unique_id on rank 0)."""
         buf = C.create_string_buffer(bytes(uid), L.TP_ID_BYTES)
         L.check(self._lib.nexus_cuda_tp_init(self.handle, rank, world, buf, L.TP_ID_BYTES), self.handle)
+
+    def tp_allreduce_kind(self) -> str:
+        """"none", "nccl" or "peer": how the hidden-state all-reduces run."""
+        return {L.TP_NONE: "none", L.TP_NCCL: "nccl", L.TP_PEER: "peer"}[
+            self._lib.nexus_cuda_tp_allreduce_kind(self.handle)]
 
     # -- trait methods --
     def name(self) -> str:

@@ -13,11 +13,24 @@
   usable.
 * Bad tensor-parallel arguments are refused on the host before NCCL is
   touched.
+* A tensor-parallel rank that never joins: rank 0 of a world of 2 calls
+  nexus_cuda_tp_init and nobody else does.  The join waits on the host (a
+  nonblocking NCCL communicator polled against tp_timeout_ms), gives up with
+  NEXUS_E_COMM, tears its half of the group down, and the same process then
+  runs a single-GPU model.  The rank runs as a child process with its own
+  time limit, so a join that did not give up could not stall the test run;
+  no kernel is in flight at any point.
 
 The reference has no device path; its decode errors are Result<_, String>
 and it falls back silently to a stateless decode when a tensor is missing
 (src/engine/mod.rs:1160-1166).  Here errors are status codes.
 """
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
 import numpy as np
 import pytest
 
@@ -87,3 +100,43 @@ def test_tensor_parallel_bad_arguments_refused(nb):
             be.tp_init(rank, world, uid)
         assert err.value.code == L.NEXUS_E_INVALID
     be.close()
+
+
+_NEVER_JOINS = r"""
+import sys, time
+sys.path.insert(0, sys.argv[1])
+import numpy as np
+import nexus_b200 as nb
+from nexus_b200 import NexusError
+from nexus_b200 import _lib as L
+be = nb.CudaBackend(device=0, tp_timeout_ms=3000)
+t0 = time.time()
+try:
+    be.tp_init(0, 2, nb.tp_unique_id())
+    code = 0
+except NexusError as e:
+    code, msg = e.code, str(e)
+took = time.time() - t0
+assert code == L.NEXUS_E_COMM, code
+assert be.tp_allreduce_kind() == "none"
+be.close()
+be = nb.CudaBackend(device=0)
+e = nb.InferenceEngine(be)
+e.load_model(sys.argv[2])
+assert len(e.generate(list(range(1, 9)), 4)) == 12
+e.close()
+be.close()
+print("OK", round(took, 2), msg)
+"""
+
+
+def test_tensor_parallel_rank_never_joins(nb, tiny_path):
+    root = Path(__file__).resolve().parents[1]
+    t0 = time.time()
+    r = subprocess.run([sys.executable, "-c", _NEVER_JOINS, str(root), str(tiny_path)], capture_output=True,
+                       text=True, timeout=180, env={**os.environ, "NCCL_NVLS_ENABLE": "0"})
+    print(r.stdout[-500:], r.stderr[-1500:])
+    assert r.returncode == 0, r.stderr[-3000:]
+    took = float(r.stdout.split("OK", 1)[1].split()[0])
+    assert 2.5 < took < 60, took
+    assert time.time() - t0 < 170
