@@ -99,6 +99,12 @@ typedef struct {
 #define NEXUS_CFG_NO_PDL 0x2u    /* no programmatic dependent launch between kernels */
 #define NEXUS_CFG_PERSISTENT 0x4u /* single-token steps on the persistent whole-step kernel
                                      (one launch per token) instead of the kernel-per-op graph */
+#define NEXUS_CFG_GEMV_16BIT 0x10u /* steps of 1-7 tokens: the GEMVs whose inputs are normalized
+                                    (q/k/v, o_proj, gate/up, the head) read them as 16-bit instead of
+                                    24-bit integers (one dp4a fewer per four weights; down keeps 24
+                                    bits).  About 8% faster at b = 1 on the 8B shape, but its logits
+                                    then differ from the reference's by ~2e-3, the edge of the
+                                    2e-3 bound; off by default */
 #define NEXUS_CFG_NCCL_ALLREDUCE 0x8u /* tensor parallelism: NCCL for every all-reduce instead of
                                         the one-shot peer-memory all-reduce of the hidden state */
 #define NEXUS_CFG_FAULT_STALL_BARRIER 0x100u /* fault injection for tests of the error path: the
@@ -249,6 +255,9 @@ typedef struct {
     float rms_norm_eps;
     uint64_t weight_bytes; /* device bytes of all streamed weights (per decode step) */
     int body_format;       /* format of blk.*.attn_q (for reporting) */
+    uint32_t max_batch;    /* sequences (nexus_cuda_config.max_batch) */
+    uint32_t page_tokens;  /* KV page size in tokens */
+    uint32_t max_pages;    /* KV pages in the pool (per rank) */
 } nexus_cuda_model_info;
 
 /* InferenceEngine::load_model (src/engine/mod.rs:539-692): mmaps the GGUF,
@@ -321,6 +330,88 @@ typedef struct {
 } nexus_decode_item;
 int nexus_cuda_decode_batch(nexus_cuda_model *m, const nexus_decode_item *items, size_t n,
                             uint32_t *out_tokens, float *out_logits);
+
+/* ---- Request scheduler (src/scheduler.rs:126-365), host only ----
+ * FIFO admission of up to max_batch_size running requests, each given
+ * ceil((prompt_len + max_tokens) / page_size_tokens) KV page ids (at least
+ * one) while at most max_kv_pages are in use (0 = no limit, Scheduler::new).
+ * Request ids are the caller's.  Unlike the reference, whose page ids come
+ * from a counter that never goes back, a released id is reused (smallest
+ * first): the ids name pages of the device KV pool.  A request needs at least
+ * one token (the reference would keep an empty one running without ever
+ * giving it a decode item).  Arrays returned through a pointer stay valid
+ * until the next call on the scheduler.  Buffers too small for the result
+ * give NEXUS_E_INVALID with the needed count in *n and change nothing. */
+typedef struct nexus_scheduler nexus_scheduler;
+/* ScheduledDecode (src/scheduler.rs:106-115); position = the request's token
+ * count, so `token` is its token number position - 1 */
+typedef struct {
+    uint64_t id;
+    uint32_t token;
+    uint32_t position;
+    uint32_t generated;
+    uint32_t prompt_len;
+    uint32_t n_pages;
+    const uint32_t *kv_pages;
+} nexus_scheduled_decode;
+/* Scheduler::with_kv_pages (:152-166) */
+int nexus_scheduler_create(uint32_t max_batch_size, uint32_t page_size_tokens, uint32_t max_kv_pages,
+                           nexus_scheduler **out);
+int nexus_scheduler_destroy(nexus_scheduler *s);
+/* Scheduler::add_request (:169-172); NEXUS_E_INVALID for a used id or no tokens */
+int nexus_scheduler_add_request(nexus_scheduler *s, uint64_t id, const uint32_t *tokens, size_t n,
+                                uint32_t max_tokens);
+/* Scheduler::get_next_batch (:175-179): ids of the requests admitted now */
+int nexus_scheduler_get_next_batch(nexus_scheduler *s, uint64_t *ids, size_t max, size_t *n);
+/* Scheduler::decode_batch (:207-229): admits pending work, then one item per running request */
+int nexus_scheduler_decode_batch(nexus_scheduler *s, nexus_scheduled_decode *items, size_t max, size_t *n);
+/* Scheduler::append_generated (:232-251); *found = 0 when id is not running */
+int nexus_scheduler_append_generated(nexus_scheduler *s, uint64_t id, uint32_t token, int *found);
+/* Scheduler::step (:254-281): ids of the requests that advanced */
+int nexus_scheduler_step(nexus_scheduler *s, uint64_t *ids, size_t max, size_t *n);
+/* Scheduler::get_completed (:284-287): takes the completed requests' ids */
+int nexus_scheduler_get_completed(nexus_scheduler *s, uint64_t *ids, size_t max, size_t *n);
+/* Scheduler::complete_request (:290-314) */
+int nexus_scheduler_complete_request(nexus_scheduler *s, uint64_t id, int *found);
+/* Scheduler::stats (:317-322) */
+int nexus_scheduler_stats(nexus_scheduler *s, size_t *pending, size_t *running, size_t *completed);
+/* Scheduler::kv_page_stats (:324-331): pages in use, max_kv_pages (0 = no limit) */
+int nexus_scheduler_kv_page_stats(nexus_scheduler *s, size_t *used, size_t *max_pages);
+/* Scheduler::kv_allocation (:333-335): NEXUS_E_INVALID when the request holds no pages */
+int nexus_scheduler_kv_allocation(nexus_scheduler *s, uint64_t id, uint32_t *page_ids, size_t max, size_t *n,
+                                  size_t *capacity_tokens);
+/* Request::tokens of a pending, running or completed (not yet taken) request:
+ * the prompt followed by the generated tokens */
+int nexus_scheduler_tokens(nexus_scheduler *s, uint64_t id, uint32_t *out, size_t max, size_t *n);
+
+/* ---- Continuous batching (no counterpart: the reference server runs one
+ * generate_with_config per request behind the engine mutex,
+ * src/server/mod.rs:407,416, and never calls decode_batch) ----
+ * One tick: pending requests are admitted (Scheduler::fill_running, :182-204)
+ * and each new one gets a free device sequence with its page ids bound
+ * (nexus_cuda_seq_set_pages) and all but its last prompt token prefilled;
+ * then one nexus_cuda_decode_batch step runs every running request's decode
+ * item and each greedy token is appended (append_generated).  A request's
+ * tokens equal greedy nexus_cuda_generate(prompt, max_tokens) run alone.
+ * One event per request that produced a token or ended in this tick: its
+ * id, the token, its index among the request's generated tokens, done = 1
+ * when the request completed, status NEXUS_E_INVALID for a request the model
+ * cannot hold (prompt_len + max_tokens - 1 > max_seq_len), which ends without
+ * tokens.  The scheduler's page size must equal the model's page_tokens,
+ * max_kv_pages must be set and within the model's pool, max_batch_size within
+ * its max_batch and max_events >= max_batch_size.  From its first tick the
+ * scheduler owns every sequence of the model (their pages are released
+ * then); requests cancelled with nexus_scheduler_complete_request give their
+ * sequence back at the next tick. */
+typedef struct {
+    uint64_t request_id;
+    uint32_t token;
+    uint32_t index;
+    uint32_t done;
+    int32_t status;
+} nexus_serve_event;
+int nexus_cuda_serve_step(nexus_cuda_model *m, nexus_scheduler *s, nexus_serve_event *events, size_t max_events,
+                          size_t *n_events);
 
 /* Device time of the last decode/prefill call in milliseconds (CUDA events). */
 int nexus_cuda_last_step_ms(const nexus_cuda_model *m, float *ms);

@@ -70,12 +70,23 @@ class ModelInfo(C.Structure):
     _fields_ = [("num_layers", C.c_uint32), ("hidden_size", C.c_uint32), ("ff_dim", C.c_uint32),
                 ("num_heads", C.c_uint32), ("num_kv_heads", C.c_uint32), ("head_dim", C.c_uint32),
                 ("vocab_rows", C.c_uint32), ("max_seq_len", C.c_uint32), ("rope_freq_base", C.c_float),
-                ("rms_norm_eps", C.c_float), ("weight_bytes", C.c_uint64), ("body_format", C.c_int)]
+                ("rms_norm_eps", C.c_float), ("weight_bytes", C.c_uint64), ("body_format", C.c_int),
+                ("max_batch", C.c_uint32), ("page_tokens", C.c_uint32), ("max_pages", C.c_uint32)]
 
 
 class DecodeItem(C.Structure):
     _fields_ = [("seq_id", C.c_uint32), ("token", C.c_uint32), ("position", C.c_uint32),
                 ("n_pages", C.c_uint32), ("page_ids", C.POINTER(C.c_uint32))]
+
+
+class ScheduledDecode(C.Structure):
+    _fields_ = [("id", C.c_uint64), ("token", C.c_uint32), ("position", C.c_uint32), ("generated", C.c_uint32),
+                ("prompt_len", C.c_uint32), ("n_pages", C.c_uint32), ("kv_pages", C.POINTER(C.c_uint32))]
+
+
+class ServeEvent(C.Structure):
+    _fields_ = [("request_id", C.c_uint64), ("token", C.c_uint32), ("index", C.c_uint32), ("done", C.c_uint32),
+                ("status", C.c_int32)]
 
 
 class KernelProfile(C.Structure):
@@ -137,6 +148,20 @@ SIGNATURES = [
     ("nexus_cuda_decode_batch", C.c_int, [P, C.POINTER(DecodeItem), C.c_size_t, P, P]),
     ("nexus_cuda_generate_with_draft", C.c_int, [P, C.c_uint32, P, C.c_size_t, P, C.c_size_t, C.c_size_t,
                                                  C.c_uint32, P, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]),
+    ("nexus_scheduler_create", C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, C.POINTER(P)]),
+    ("nexus_scheduler_destroy", C.c_int, [P]),
+    ("nexus_scheduler_add_request", C.c_int, [P, C.c_uint64, P, C.c_size_t, C.c_uint32]),
+    ("nexus_scheduler_get_next_batch", C.c_int, [P, P, C.c_size_t, C.POINTER(C.c_size_t)]),
+    ("nexus_scheduler_decode_batch", C.c_int, [P, C.POINTER(ScheduledDecode), C.c_size_t, C.POINTER(C.c_size_t)]),
+    ("nexus_scheduler_append_generated", C.c_int, [P, C.c_uint64, C.c_uint32, C.POINTER(C.c_int)]),
+    ("nexus_scheduler_step", C.c_int, [P, P, C.c_size_t, C.POINTER(C.c_size_t)]),
+    ("nexus_scheduler_get_completed", C.c_int, [P, P, C.c_size_t, C.POINTER(C.c_size_t)]),
+    ("nexus_scheduler_complete_request", C.c_int, [P, C.c_uint64, C.POINTER(C.c_int)]),
+    ("nexus_scheduler_stats", C.c_int, [P, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
+    ("nexus_scheduler_kv_page_stats", C.c_int, [P, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
+    ("nexus_scheduler_kv_allocation", C.c_int, [P, C.c_uint64, P, C.c_size_t, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
+    ("nexus_scheduler_tokens", C.c_int, [P, C.c_uint64, P, C.c_size_t, C.POINTER(C.c_size_t)]),
+    ("nexus_cuda_serve_step", C.c_int, [P, P, C.POINTER(ServeEvent), C.c_size_t, C.POINTER(C.c_size_t)]),
     ("nexus_cuda_last_step_ms", C.c_int, [P, C.POINTER(C.c_float)]),
     ("nexus_cuda_profile_decode", C.c_int, [P, C.c_uint32, C.c_uint32, C.c_uint32, C.POINTER(KernelProfile),
                                             C.c_int, C.POINTER(C.c_int)]),

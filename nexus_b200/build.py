@@ -40,7 +40,7 @@ UNITS = {
     "engine.cu": [],
     "noalloc.cu": [],
 }
-CXX_UNITS = ["host.cpp"]
+CXX_UNITS = ["host.cpp", "scheduler.cpp"]
 
 
 def nvcc() -> str:

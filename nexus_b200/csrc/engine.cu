@@ -1139,6 +1139,7 @@ struct nexus_cuda_model {
     PageMap pm;
     uint32_t *page_table = nullptr;   // device copy of pm.table
     uint32_t max_seq = 0, max_batch = 1, bits_k = 0, bits_v = 0;
+    int x_bits_norm = 24;  // GEMV input bits for matrices with normalized inputs
     size_t bpt_k = 0, bpt_v = 0;
     int nsplit[kMaxChunk + 1] = {};     // attention slices per (sequence, KV head), float cache
     int nsplit_pk[kMaxChunk + 1] = {};  // the same for the packed-cache tensor-core kernel
@@ -1306,8 +1307,14 @@ static int model_load(nexus_cuda_backend *b, const char *path, nexus_cuda_model 
         pm.caller.assign(m->max_batch, 0);
         pm.owner.assign(pm.pool, -1);
         pm.dirty.assign(m->max_batch, 0);
+        I.max_batch = m->max_batch;
+        I.page_tokens = pm.page_tokens;
+        I.max_pages = pm.pool;
     }
     m->use_graph = !(b->cfg.flags & NEXUS_CFG_NO_GRAPH);
+    // GEMV inputs of qkv, o_proj, gate/up and the head (normalized) as 16-bit
+    // integers only on request; down always reads 24-bit ones
+    m->x_bits_norm = (b->cfg.flags & NEXUS_CFG_GEMV_16BIT) ? 16 : 24;
     m->use_pdl = !(b->cfg.flags & NEXUS_CFG_NO_PDL);
     cudaSetDevice(b->device);
 
@@ -1482,9 +1489,9 @@ static int model_load(nexus_cuda_backend *b, const char *path, nexus_cuda_model 
     NX_CUDA(b, malloc_tracked(m, &m->logits, (size_t)MC * (m->has_head ? m->v_l : I.vocab_rows)));
     if (tp > 1) NX_CUDA(b, malloc_tracked(m, &m->logits_gather, (size_t)tp * MC * m->v_l));
     const int G = (int)(Hq / Hkv);
-    // context slices of >= 64 tokens, at most 64 per (sequence, KV head); the
-    // kernel uses only as many as the current context needs
-    int max_split = std::max(1, std::min(64, (int)((m->max_seq + 63) / 64)));
+    // context slices of >= NX_ATTN_TPS tokens, at most 64 per (sequence, KV
+    // head); the kernel uses only as many as the current context needs
+    int max_split = std::max(1, std::min(64, (int)((m->max_seq + NX_ATTN_TPS - 1) / NX_ATTN_TPS)));
     for (int mm = 1; mm <= MC; mm++) m->nsplit[mm] = max_split;
     // the packed-cache kernel: about 8 CTAs per SM over the whole step (its
     // CTAs stream whole 64-token tiles and need no more slices than that)
@@ -1808,6 +1815,7 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         g.x_stride = H;
         g.norm_w = L.attn_norm;
         g.epi = EPI_QKV;
+        g.x_bits = m->x_bits_norm;
         g.qkv.hq = Hq;
         g.qkv.hkv = Hkv;
         g.qkv.head_dim = D;
@@ -1902,6 +1910,7 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         o.x = m->attn;
         o.x_stride = qdim;
         o.epi = lead ? EPI_ADD : EPI_STORE;
+        o.x_bits = m->x_bits_norm;
         o.y = m->hidden;
         o.y_stride = H;
         if (prof) prof->begin();
@@ -1923,6 +1932,7 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         gu.x_stride = H;
         gu.norm_w = L.ffn_norm;
         gu.epi = EPI_SWIGLU;
+        gu.x_bits = m->x_bits_norm;
         gu.y = m->gated;
         gu.y_stride = F;
         if (prof) prof->begin();
@@ -1964,6 +1974,7 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         hd.x_stride = H;
         hd.norm_w = m->out_norm;
         hd.epi = EPI_ARGMAX;
+        hd.x_bits = m->x_bits_norm;
         hd.y = m->logits;
         hd.y_stride = (int)m->v_l;
         hd.row_offset = (int)m->sl.vocab_begin;

@@ -59,6 +59,12 @@ struct QkvEpilogue {
     const uint32_t *seq_ids;    // [m] cache row of each batch entry
 };
 
+// Decode attention: a context slice holds at least this many tokens (the
+// step's slice count per (sequence, KV head) is sized with it).
+#ifndef NX_ATTN_TPS
+#define NX_ATTN_TPS 64
+#endif
+
 struct GemvParams {
     int fmt;
     const uint4 *w_main;
@@ -85,6 +91,7 @@ struct GemvParams {
     int nst;                // weight ring slots per warp (set by the launcher)
     int *err;               // device flag set when a bounded wait gives up (may be NULL)
     int row_offset;         // EPI_ARGMAX: global index of local row 0 (vocab slice of a rank)
+    int x_bits;             // GEMV input precision: 16 (normalized inputs) or 24 (default, 0)
 };
 
 cudaError_t launch_gemv(const GemvParams &p, cudaStream_t st);

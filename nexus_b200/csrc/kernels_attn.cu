@@ -29,7 +29,7 @@
 namespace nx {
 
 constexpr int kAttnWarps = 8;
-constexpr int kTokensPerSplit = 64;  // a slice holds at least this many tokens
+constexpr int kTokensPerSplit = NX_ATTN_TPS;  // a slice holds at least this many tokens
 
 template <int VEC, int G>
 __global__ void __launch_bounds__(kAttnWarps * 32, G <= 4 ? 2 : 1) k_attn(AttnParams p) {

@@ -72,7 +72,7 @@ __device__ __forceinline__ uint32_t byte_of(uint32_t w, int j) { return (w >> (8
 // Q4_K super-block (tiles.cuh): chunk 0 = d|dmin, scales; chunks 1..8 = qs.
 // Low nibbles are masked in place; high nibbles are used in place as 16*q
 // (one mask, no shift) and their sums carry a factor 16 removed at the end.
-template <int P>
+template <int P, int NB = 3>
 __device__ __forceinline__ float sb_dot_q4k(const uint4 *c, const XSb &x, int part) {
     const uint4 c0 = NX_CH(0);
     const float d = h2f_bits(c0.x), dmin = h2f_bits(c0.x >> 16);
@@ -88,18 +88,23 @@ __device__ __forceinline__ float sb_dot_q4k(const uint4 *c, const XSb &x, int pa
     for (int k = 0; k < CPP; k++) {
         const int cc = part * CPP + k;
         const uint4 q = NX_CH(1 + cc);
-        const uint4 zhl = x.zh[cc], zml = x.zm[cc], zll = x.zl[cc];
-        const uint4 zhh = x.zh[8 + cc], zmh = x.zm[8 + cc], zlh = x.zl[8 + cc];
+        const uint4 zhl = x.zh[cc], zll = x.zl[cc];
+        const uint4 zhh = x.zh[8 + cc], zlh = x.zl[8 + cc];
+        uint4 zml = {}, zmh = {};
+        if constexpr (NB == 3) {
+            zml = x.zm[cc];
+            zmh = x.zm[8 + cc];
+        }
         int ah = 0, am = 0, al = 0, ah2 = 0, am2 = 0, al2 = 0;
 #define NX_Q4K_STEP(W)                                              \
     {                                                               \
         const uint32_t lo = q.W & 0x0f0f0f0fu;                      \
         const uint32_t hi = q.W & 0xf0f0f0f0u;                      \
         ah = dp4a_us(lo, zhl.W, ah);                                \
-        am = dp4a_uu(lo, zml.W, am);                                \
+        if constexpr (NB == 3) am = dp4a_uu(lo, zml.W, am);         \
         al = dp4a_uu(lo, zll.W, al);                                \
         ah2 = dp4a_us(hi, zhh.W, ah2);                              \
-        am2 = dp4a_uu(hi, zmh.W, am2);                              \
+        if constexpr (NB == 3) am2 = dp4a_uu(hi, zmh.W, am2);       \
         al2 = dp4a_uu(hi, zlh.W, al2);                              \
     }
         NX_Q4K_STEP(x) NX_Q4K_STEP(y) NX_Q4K_STEP(z) NX_Q4K_STEP(w)
@@ -122,13 +127,14 @@ __device__ __forceinline__ float sb_dot_q4k(const uint4 *c, const XSb &x, int pa
     // |b*16| < 2^29 (16 * 63 * 8 chunks * 16 products of <= 15*255); the
     // factor 16 is exact in f32
     const float hsum = (float)bh + 0.0625f * (float)bh16;
-    const float msum = (float)bm + 0.0625f * (float)bm16;
     const float lsum = (float)bl + 0.0625f * (float)bl16;
+    if constexpr (NB == 2) return x.u * (d * (256.0f * hsum + lsum) - dmin * mn);
+    const float msum = (float)bm + 0.0625f * (float)bm16;
     return x.u * (d * (65536.0f * hsum + (256.0f * msum + lsum)) - dmin * mn);
 }
 
 // Q8_0 super-block: chunk 0 = eight f16 scales, chunks 1+2b, 2+2b = qs of block b
-template <int P>
+template <int P, int NB = 3>
 __device__ __forceinline__ float sb_dot_q80(const uint4 *c, const XSb &x, int part) {
     float acc = 0.0f;
     const uint4 c0 = NX_CH(0);
@@ -139,7 +145,6 @@ __device__ __forceinline__ float sb_dot_q80(const uint4 *c, const XSb &x, int pa
         const int b = part * BPP + k;
         const uint4 q0 = NX_CH(1 + 2 * b), q1 = NX_CH(2 + 2 * b);
         const uint4 h0 = x.zh[2 * b], h1 = x.zh[2 * b + 1], l0 = x.zl[2 * b], l1 = x.zl[2 * b + 1];
-        const uint4 m0 = x.zm[2 * b], m1 = x.zm[2 * b + 1];
         int ah = dp4a_ss(q0.x, h0.x, 0);
         ah = dp4a_ss(q0.y, h0.y, ah);
         ah = dp4a_ss(q0.z, h0.z, ah);
@@ -148,14 +153,18 @@ __device__ __forceinline__ float sb_dot_q80(const uint4 *c, const XSb &x, int pa
         ah = dp4a_ss(q1.y, h1.y, ah);
         ah = dp4a_ss(q1.z, h1.z, ah);
         ah = dp4a_ss(q1.w, h1.w, ah);
-        int am = dp4a_su(q0.x, m0.x, 0);
-        am = dp4a_su(q0.y, m0.y, am);
-        am = dp4a_su(q0.z, m0.z, am);
-        am = dp4a_su(q0.w, m0.w, am);
-        am = dp4a_su(q1.x, m1.x, am);
-        am = dp4a_su(q1.y, m1.y, am);
-        am = dp4a_su(q1.z, m1.z, am);
-        am = dp4a_su(q1.w, m1.w, am);
+        int am = 0;
+        if constexpr (NB == 3) {
+            const uint4 m0 = x.zm[2 * b], m1 = x.zm[2 * b + 1];
+            am = dp4a_su(q0.x, m0.x, 0);
+            am = dp4a_su(q0.y, m0.y, am);
+            am = dp4a_su(q0.z, m0.z, am);
+            am = dp4a_su(q0.w, m0.w, am);
+            am = dp4a_su(q1.x, m1.x, am);
+            am = dp4a_su(q1.y, m1.y, am);
+            am = dp4a_su(q1.z, m1.z, am);
+            am = dp4a_su(q1.w, m1.w, am);
+        }
         int al = dp4a_su(q0.x, l0.x, 0);
         al = dp4a_su(q0.y, l0.y, al);
         al = dp4a_su(q0.z, l0.z, al);
@@ -165,7 +174,8 @@ __device__ __forceinline__ float sb_dot_q80(const uint4 *c, const XSb &x, int pa
         al = dp4a_su(q1.z, l1.z, al);
         al = dp4a_su(q1.w, l1.w, al);
         const float db = h2f_bits(sw[b >> 1] >> (16 * (b & 1)));
-        acc += db * (65536.0f * (float)ah + (256.0f * (float)am + (float)al));
+        if constexpr (NB == 2) acc += db * (256.0f * (float)ah + (float)al);
+        else acc += db * (65536.0f * (float)ah + (256.0f * (float)am + (float)al));
     }
     return x.u * acc;
 }
@@ -214,7 +224,7 @@ __device__ __forceinline__ float sb_dot_q80_half(const uint4 *c, const XSb &x, i
 }
 
 // Q4_0 super-block: chunk 0 = eight f16 scales, chunk 1+b = qs of block b (q - 8)
-template <int P>
+template <int P, int NB = 3>
 __device__ __forceinline__ float sb_dot_q40(const uint4 *c, const XSb &x, int part) {
     float acc = 0.0f;
     const uint4 c0 = NX_CH(0);
@@ -225,31 +235,36 @@ __device__ __forceinline__ float sb_dot_q40(const uint4 *c, const XSb &x, int pa
         const int b = part * BPP + k;
         const uint4 q = NX_CH(1 + b);
         const uint4 hl = x.zh[2 * b], hh = x.zh[2 * b + 1], ll = x.zl[2 * b], lh = x.zl[2 * b + 1];
-        const uint4 ml = x.zm[2 * b], mh = x.zm[2 * b + 1];
+        uint4 ml = {}, mh = {};
+        if constexpr (NB == 3) {
+            ml = x.zm[2 * b];
+            mh = x.zm[2 * b + 1];
+        }
         int ah = 0, am = 0, al = 0;
-#define NX_Q40_STEP(W)                                  \
-    {                                                   \
-        const uint32_t lo = q.W & 0x0f0f0f0fu;          \
-        const uint32_t hi = (q.W >> 4) & 0x0f0f0f0fu;   \
-        ah = dp4a_us(lo, hl.W, ah);                     \
-        ah = dp4a_us(hi, hh.W, ah);                     \
-        am = dp4a_uu(lo, ml.W, am);                     \
-        am = dp4a_uu(hi, mh.W, am);                     \
-        al = dp4a_uu(lo, ll.W, al);                     \
-        al = dp4a_uu(hi, lh.W, al);                     \
+#define NX_Q40_STEP(W)                                          \
+    {                                                           \
+        const uint32_t lo = q.W & 0x0f0f0f0fu;                  \
+        const uint32_t hi = (q.W >> 4) & 0x0f0f0f0fu;           \
+        ah = dp4a_us(lo, hl.W, ah);                             \
+        ah = dp4a_us(hi, hh.W, ah);                             \
+        if constexpr (NB == 3) am = dp4a_uu(lo, ml.W, am);      \
+        if constexpr (NB == 3) am = dp4a_uu(hi, mh.W, am);      \
+        al = dp4a_uu(lo, ll.W, al);                             \
+        al = dp4a_uu(hi, lh.W, al);                             \
     }
         NX_Q40_STEP(x) NX_Q40_STEP(y) NX_Q40_STEP(z) NX_Q40_STEP(w)
 #undef NX_Q40_STEP
         const int s32 = x.sz[2 * b] + x.sz[2 * b + 1];  // < 2^28
         const float db = h2f_bits(sw[b >> 1] >> (16 * (b & 1)));
-        acc += db * (65536.0f * (float)ah + (256.0f * (float)am + ((float)al - 8.0f * (float)s32)));
+        if constexpr (NB == 2) acc += db * (256.0f * (float)ah + ((float)al - 8.0f * (float)s32));
+        else acc += db * (65536.0f * (float)ah + (256.0f * (float)am + ((float)al - 8.0f * (float)s32)));
     }
     return x.u * acc;
 }
 
 // Q2_K super-block: chunk 0 = 16 scale bytes, chunks 1..4 = qs words (one per
 // 16-element sub-block, bit-plane ordered), aux = d | dmin << 16
-template <int P>
+template <int P, int NB = 3>
 __device__ __forceinline__ float sb_dot_q2k(const uint4 *c, uint32_t aux, const XSb &x, int part) {
     const float d = h2f_bits(aux), dmin = h2f_bits(aux >> 16);
     const uint4 c0 = NX_CH(0);
@@ -262,17 +277,21 @@ __device__ __forceinline__ float sb_dot_q2k(const uint4 *c, uint32_t aux, const 
         const int j = part * JPP + k;
         const uint4 qq = NX_CH(1 + (j >> 2));
         const uint32_t qw = (j & 3) == 0 ? qq.x : (j & 3) == 1 ? qq.y : (j & 3) == 2 ? qq.z : qq.w;
-        const uint4 h = x.zh[j], mm = x.zm[j], l = x.zl[j];
+        const uint4 h = x.zh[j], l = x.zl[j];
         const uint32_t p0 = qw & 0x03030303u, p1 = (qw >> 2) & 0x03030303u;
         const uint32_t p2 = (qw >> 4) & 0x03030303u, p3 = (qw >> 6) & 0x03030303u;
         int ah = dp4a_us(p0, h.x, 0);
         ah = dp4a_us(p1, h.y, ah);
         ah = dp4a_us(p2, h.z, ah);
         ah = dp4a_us(p3, h.w, ah);
-        int am = dp4a_uu(p0, mm.x, 0);
-        am = dp4a_uu(p1, mm.y, am);
-        am = dp4a_uu(p2, mm.z, am);
-        am = dp4a_uu(p3, mm.w, am);
+        int am = 0;
+        if constexpr (NB == 3) {
+            const uint4 mm = x.zm[j];
+            am = dp4a_uu(p0, mm.x, 0);
+            am = dp4a_uu(p1, mm.y, am);
+            am = dp4a_uu(p2, mm.z, am);
+            am = dp4a_uu(p3, mm.w, am);
+        }
         int al = dp4a_uu(p0, l.x, 0);
         al = dp4a_uu(p1, l.y, al);
         al = dp4a_uu(p2, l.z, al);
@@ -284,31 +303,52 @@ __device__ __forceinline__ float sb_dot_q2k(const uint4 *c, uint32_t aux, const 
         bl += sc * al;
         mn += (float)m * (float)x.sz[j];
     }
+    if constexpr (NB == 2) return x.u * (d * (256.0f * (float)bh + (float)bl) - dmin * mn);
     return x.u * (d * (65536.0f * (float)bh + (256.0f * (float)bm + (float)bl)) - dmin * mn);
 }
 #undef NX_CH
 
-template <int FMT, int P>
+template <int FMT, int P, int NB = 3>
 __device__ __forceinline__ float sb_dot(const uint4 *c, uint32_t aux, const XSb &x, int part) {
-    if constexpr (FMT == 12) return sb_dot_q4k<P>(c, x, part);
-    else if constexpr (FMT == 8) return sb_dot_q80<P>(c, x, part);
-    else if constexpr (FMT == 2) return sb_dot_q40<P>(c, x, part);
-    else return sb_dot_q2k<P>(c, aux, x, part);
+    if constexpr (FMT == 12) return sb_dot_q4k<P, NB>(c, x, part);
+    else if constexpr (FMT == 8) return sb_dot_q80<P, NB>(c, x, part);
+    else if constexpr (FMT == 2) return sb_dot_q40<P, NB>(c, x, part);
+    else return sb_dot_q2k<P, NB>(c, aux, x, part);
 }
 
-// Shared-memory bytes of the prepared input of one token: zh[k], zm[k],
-// zl[k], sz[k/16], u[k/256], padded to 16 bytes so every token's image is
-// aligned.
-__host__ __device__ __forceinline__ size_t tok_smem_bytes(int k) {
-    return ((size_t)3 * k + (size_t)4 * (k / 16) + (size_t)4 * (k / 256) + 15) / 16 * 16;
+// Shared-memory bytes of the prepared input of one token: zh[k], zm[k] (24-bit
+// inputs only), zl[k], sz[k/16], u[k/256], padded to 16 bytes so every
+// token's image is aligned.  NB = bytes per input element (3: 24-bit, 2: 16-bit).
+__host__ __device__ __forceinline__ size_t tok_smem_bytes(int k, int nb = 3) {
+    return ((size_t)nb * k + (size_t)4 * (k / 16) + (size_t)4 * (k / 256) + 15) / 16 * 16;
 }
 
-// Prepare super-block s of one token: 24-bit quantization of x (times the
-// RMSNorm weight when fused) from the lane's 8 values v (elements
-// 8*lane .. 8*lane+7).  The quantization is scale-invariant, so RMSNorm's
+// The planes of one token's prepared image (tok_smem_bytes layout).
+struct TokPlanes {
+    uint32_t *zh, *zm, *zl;
+    int *sz;
+    float *u;
+};
+template <int NB>
+__device__ __forceinline__ TokPlanes tok_planes(uint8_t *tb, int k) {
+    TokPlanes t;
+    t.zh = reinterpret_cast<uint32_t *>(tb);
+    t.zm = NB == 3 ? reinterpret_cast<uint32_t *>(tb + k) : nullptr;
+    t.zl = reinterpret_cast<uint32_t *>(tb + (NB - 1) * k);
+    t.sz = reinterpret_cast<int *>(tb + NB * k);
+    t.u = reinterpret_cast<float *>(tb + NB * k + 4 * (k / 16));
+    return t;
+}
+
+// Prepare super-block s of one token: 24-bit (NB = 3) or 16-bit (NB = 2)
+// quantization of x (times the RMSNorm weight when fused) from the lane's 8
+// values v (elements 8*lane .. 8*lane+7).  16-bit inputs serve matrices
+// whose inputs are normalized (RMSNorm outputs, attention outputs): one dp4a
+// fewer per four weights; heavy-tailed inputs (SwiGLU outputs) keep 24 bits.  The quantization is scale-invariant, so RMSNorm's
 // rstd is not needed here: the caller multiplies u[s] by rstd once the sum of
 // squares, accumulated in *ss, is known.  (x*rstd)*w and rstd*(x*w) agree to
 // f32 rounding, far below the 24-bit step.
+template <int NB = 3>
 __device__ __forceinline__ void prep_sb_vals(float (&v)[8], const float (&w)[8], bool has_w, int s, int lane,
                                              uint32_t *zh, uint32_t *zm, uint32_t *zl, int *sz, float *u,
                                              float *ss) {
@@ -322,19 +362,22 @@ __device__ __forceinline__ void prep_sb_vals(float (&v)[8], const float (&w)[8],
 #pragma unroll
     for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
     amax = warp_max(amax);
-    const float inv = (amax > 0.0f && amax <= 3.0e38f) ? 8388607.0f / amax : 0.0f;
+    constexpr int ZMAX = NB == 3 ? 8388607 : 32767;
+    constexpr float FZMAX = (float)ZMAX;
+    const float inv = (amax > 0.0f && amax <= 3.0e38f) ? FZMAX / amax : 0.0f;
     int z[8], psum = 0;
 #pragma unroll
     for (int i = 0; i < 8; i++) {
-        // v * inv can round to 2^23 for the largest element; the top byte is signed
-        z[i] = max(-8388607, min(8388607, __float2int_rn(v[i] * inv)));
+        // v * inv can round to 2^23 (2^15) for the largest element; the top byte is signed
+        z[i] = max(-ZMAX, min(ZMAX, __float2int_rn(v[i] * inv)));
         psum += z[i];
     }
+    constexpr int HS = NB == 3 ? 16 : 8;  // shift of the signed top byte
     uint32_t h0 = 0, h1 = 0, m0 = 0, m1 = 0, l0 = 0, l1 = 0;
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        h0 |= ((uint32_t)(z[i] >> 16) & 0xffu) << (8 * i);
-        h1 |= ((uint32_t)(z[4 + i] >> 16) & 0xffu) << (8 * i);
+        h0 |= ((uint32_t)(z[i] >> HS) & 0xffu) << (8 * i);
+        h1 |= ((uint32_t)(z[4 + i] >> HS) & 0xffu) << (8 * i);
         m0 |= ((uint32_t)(z[i] >> 8) & 0xffu) << (8 * i);
         m1 |= ((uint32_t)(z[4 + i] >> 8) & 0xffu) << (8 * i);
         l0 |= ((uint32_t)z[i] & 0xffu) << (8 * i);
@@ -343,20 +386,22 @@ __device__ __forceinline__ void prep_sb_vals(float (&v)[8], const float (&w)[8],
     const int wi = 64 * s + 2 * lane;
     zh[wi] = h0;
     zh[wi + 1] = h1;
-    zm[wi] = m0;
-    zm[wi + 1] = m1;
+    if constexpr (NB == 3) {
+        zm[wi] = m0;
+        zm[wi + 1] = m1;
+    }
     zl[wi] = l0;
     zl[wi + 1] = l1;
     psum += __shfl_xor_sync(0xffffffffu, psum, 1);
     if ((lane & 1) == 0) sz[16 * s + (lane >> 1)] = psum;
-    if (lane == 0) u[s] = amax / 8388607.0f;
+    if (lane == 0) u[s] = amax / FZMAX;
 }
 
 // One warp prepares super-blocks warp, warp + W, ... of one token.  All of a
 // pass's loads are issued before any is used (one memory round trip per
 // kPrepBatch super-blocks instead of one per super-block).
 constexpr int kPrepBatch = 4;
-template <int W>
+template <int W, int NB = 3>
 __device__ __forceinline__ float prep_token(const float *__restrict__ x, const float *__restrict__ nw, int n_sb,
                                             int warp, int lane, uint32_t *zh, uint32_t *zm, uint32_t *zl, int *sz,
                                             float *u) {
@@ -387,7 +432,7 @@ __device__ __forceinline__ float prep_token(const float *__restrict__ x, const f
                     w[0] = wa[i].x; w[1] = wa[i].y; w[2] = wa[i].z; w[3] = wa[i].w;
                     w[4] = wb[i].x; w[5] = wb[i].y; w[6] = wb[i].z; w[7] = wb[i].w;
                 }
-                prep_sb_vals(v, w, nw != nullptr, s, lane, zh, zm, zl, sz, u, &ss);
+                prep_sb_vals<NB>(v, w, nw != nullptr, s, lane, zh, zm, zl, sz, u, &ss);
             }
         }
     }
@@ -490,7 +535,7 @@ struct Ring {
 
 constexpr unsigned kMbarSpinLimit = 1u << 20;
 
-template <int FMT, int M, int EPI>
+template <int FMT, int M, int EPI, int NB>
 __global__ void __launch_bounds__(Ring<FMT>::W * 32, 1) k_gemv(GemvParams p) {
     using R = Ring<FMT>;
     constexpr int W = R::W, NST = R::NST;
@@ -513,7 +558,7 @@ __global__ void __launch_bounds__(Ring<FMT>::W * 32, 1) k_gemv(GemvParams p) {
 
     uint8_t *ring = smem + (size_t)warp * NST * R::SLOT_BYTES;
     uint8_t *xs = smem + (size_t)W * NST * R::SLOT_BYTES;
-    const size_t tok_bytes = tok_smem_bytes(k);
+    const size_t tok_bytes = tok_smem_bytes(k, NB);
     float *red = reinterpret_cast<float *>(xs + tok_bytes * M);      // [W][2][M][32]
     float *misc = red + W * 2 * M * 32;                              // [W*M]
 
@@ -552,13 +597,9 @@ __global__ void __launch_bounds__(Ring<FMT>::W * 32, 1) k_gemv(GemvParams p) {
     // with a fused RMSNorm the sum of squares comes out of the same pass.
 #pragma unroll
     for (int t = 0; t < M; t++) {
-        uint8_t *tb = xs + tok_bytes * t;
-        uint32_t *zh = reinterpret_cast<uint32_t *>(tb);
-        uint32_t *zm = reinterpret_cast<uint32_t *>(tb + k);
-        uint32_t *zl = reinterpret_cast<uint32_t *>(tb + 2 * k);
-        int *sz = reinterpret_cast<int *>(tb + 3 * k);
-        float *u = reinterpret_cast<float *>(tb + 3 * k + 4 * (k / 16));
-        float ss = prep_token<W>(p.x + (size_t)t * p.x_stride, p.norm_w, n_sb, warp, lane, zh, zm, zl, sz, u);
+        const TokPlanes tp = tok_planes<NB>(xs + tok_bytes * t, k);
+        float ss = prep_token<W, NB>(p.x + (size_t)t * p.x_stride, p.norm_w, n_sb, warp, lane, tp.zh, tp.zm, tp.zl,
+                                     tp.sz, tp.u);
         if (p.norm_w) {
             ss = warp_sum(ss);
             if (lane == 0) misc[warp * M + t] = ss;
@@ -572,7 +613,7 @@ __global__ void __launch_bounds__(Ring<FMT>::W * 32, 1) k_gemv(GemvParams p) {
             float ss = 0.0f;
             for (int w = 0; w < W; w++) ss += misc[w * M + t];
             const float rstd = 1.0f / sqrtf(ss / (float)k + p.eps);
-            float *u = reinterpret_cast<float *>(xs + tok_bytes * t + 3 * k + 4 * (k / 16));
+            float *u = tok_planes<NB>(xs + tok_bytes * t, k).u;
             for (int s = threadIdx.x; s < n_sb; s += W * 32) u[s] *= rstd;
         }
         __syncthreads();
@@ -610,14 +651,14 @@ __global__ void __launch_bounds__(Ring<FMT>::W * 32, 1) k_gemv(GemvParams p) {
                 auxw = reinterpret_cast<const uint32_t *>(ring + (size_t)slot * R::SLOT_BYTES + R::ITEM_BYTES)[lane];
 #pragma unroll
             for (int t = 0; t < M; t++) {
-                const uint8_t *tb = xs + tok_bytes * t;
+                const TokPlanes tp = tok_planes<NB>(xs + tok_bytes * t, k);
                 XSb xsb;
-                xsb.zh = reinterpret_cast<const uint4 *>(tb) + 16 * s_sb;
-                xsb.zm = reinterpret_cast<const uint4 *>(tb + k) + 16 * s_sb;
-                xsb.zl = reinterpret_cast<const uint4 *>(tb + 2 * k) + 16 * s_sb;
-                xsb.sz = reinterpret_cast<const int *>(tb + 3 * k) + 16 * s_sb;
-                xsb.u = reinterpret_cast<const float *>(tb + 3 * k + 4 * (k / 16))[s_sb];
-                acc[t] += sb_dot<FMT, 1>(cbase, auxw, xsb, 0);
+                xsb.zh = reinterpret_cast<const uint4 *>(tp.zh) + 16 * s_sb;
+                xsb.zm = NB == 3 ? reinterpret_cast<const uint4 *>(tp.zm) + 16 * s_sb : nullptr;
+                xsb.zl = reinterpret_cast<const uint4 *>(tp.zl) + 16 * s_sb;
+                xsb.sz = tp.sz + 16 * s_sb;
+                xsb.u = tp.u[s_sb];
+                acc[t] += sb_dot<FMT, 1, NB>(cbase, auxw, xsb, 0);
             }
             // every lane has consumed the slot's values: refill it with item j + NST
             __syncwarp();
@@ -647,20 +688,23 @@ __global__ void __launch_bounds__(Ring<FMT>::W * 32, 1) k_gemv(GemvParams p) {
 
 // ---------------------------------------------------------------------------
 template <int FMT>
-static size_t gemv_smem_bytes(int k, int m) {
+static size_t gemv_smem_bytes(int k, int m, int nb = 3) {
     using R = Ring<FMT>;
-    return (size_t)R::W * R::NST * R::SLOT_BYTES + tok_smem_bytes(k) * m + (size_t)4 * R::W * 2 * m * 32 +
+    return (size_t)R::W * R::NST * R::SLOT_BYTES + tok_smem_bytes(k, nb) * m + (size_t)4 * R::W * 2 * m * 32 +
            (size_t)4 * R::W * m;
 }
 
-template <int FMT, int M, int EPI>
+// bytes per prepared input element: 16-bit inputs on request, else 24-bit
+__host__ __device__ __forceinline__ int gemv_nb(const GemvParams &p) { return p.x_bits == 16 ? 2 : 3; }
+
+template <int FMT, int M, int EPI, int NB>
 static cudaError_t launch_fmt_m_epi(const GemvParams &pin, cudaStream_t st) {
     using R = Ring<FMT>;
     GemvParams p = pin;
     const int groups = (p.n + 31) / 32;
     const int n_sb = p.k / 256;
-    const size_t smem = gemv_smem_bytes<FMT>(p.k, M);
-    auto fn = k_gemv<FMT, M, EPI>;
+    const size_t smem = gemv_smem_bytes<FMT>(p.k, M, NB);
+    auto fn = k_gemv<FMT, M, EPI, NB>;
     if (smem > 220 * 1024) return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -696,16 +740,21 @@ static cudaError_t launch_fmt_m_epi(const GemvParams &pin, cudaStream_t st) {
     return cudaLaunchKernelEx(&cfg, fn, p);
 }
 
-template <int FMT, int M>
-static cudaError_t launch_epi(const GemvParams &p, cudaStream_t st) {
+template <int FMT, int M, int NB>
+static cudaError_t launch_epi_nb(const GemvParams &p, cudaStream_t st) {
     switch (p.epi) {
-    case EPI_STORE: return launch_fmt_m_epi<FMT, M, EPI_STORE>(p, st);
-    case EPI_ADD: return launch_fmt_m_epi<FMT, M, EPI_ADD>(p, st);
-    case EPI_SWIGLU: return launch_fmt_m_epi<FMT, M, EPI_SWIGLU>(p, st);
-    case EPI_QKV: return launch_fmt_m_epi<FMT, M, EPI_QKV>(p, st);
-    case EPI_ARGMAX: return launch_fmt_m_epi<FMT, M, EPI_ARGMAX>(p, st);
+    case EPI_STORE: return launch_fmt_m_epi<FMT, M, EPI_STORE, NB>(p, st);
+    case EPI_ADD: return launch_fmt_m_epi<FMT, M, EPI_ADD, NB>(p, st);
+    case EPI_SWIGLU: return launch_fmt_m_epi<FMT, M, EPI_SWIGLU, NB>(p, st);
+    case EPI_QKV: return launch_fmt_m_epi<FMT, M, EPI_QKV, NB>(p, st);
+    case EPI_ARGMAX: return launch_fmt_m_epi<FMT, M, EPI_ARGMAX, NB>(p, st);
     default: return cudaErrorInvalidValue;
     }
+}
+
+template <int FMT, int M>
+static cudaError_t launch_epi(const GemvParams &p, cudaStream_t st) {
+    return gemv_nb(p) == 2 ? launch_epi_nb<FMT, M, 2>(p, st) : launch_epi_nb<FMT, M, 3>(p, st);
 }
 
 // Tokens [t0, t0 + m) of a batch: per-token pointers move, shared ones stay.
@@ -726,7 +775,7 @@ template <int FMT>
 cudaError_t launch_gemv_fmt(const GemvParams &p, cudaStream_t st) {
     // A batch whose prepared inputs do not fit next to the weight rings runs
     // as two launches of half the tokens.
-    if (p.m > 1 && gemv_smem_bytes<FMT>(p.k, p.m) > 220 * 1024) {
+    if (p.m > 1 && gemv_smem_bytes<FMT>(p.k, p.m, gemv_nb(p)) > 220 * 1024) {
         const int h = p.m / 2;
         cudaError_t e = launch_gemv_fmt<FMT>(token_slice(p, 0, h), st);
         if (e != cudaSuccess) return e;

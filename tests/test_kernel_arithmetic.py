@@ -7,8 +7,10 @@ checked on the CPU (no GPU, no CUDA library):
   PackedKvBuffer stores (src/engine/mod.rs:209-256);
 * the GEMV input planes (nexus_b200/csrc/kernels_gemv.cuh): x ~= u*z with z a
   24-bit integer held as a signed high byte and unsigned middle and low
-  bytes, the clamp that keeps the top byte in range, and the error of the
-  24-bit form against the 16-bit one on heavy-tailed inputs.
+  bytes (or a 16-bit one as a signed high and an unsigned low byte), the
+  clamp that keeps the top byte in range, the error of the 24-bit form
+  against the 16-bit one on heavy-tailed inputs, and the 16-bit form's error
+  on normalized inputs.
 """
 import numpy as np
 import pytest
@@ -127,3 +129,42 @@ def test_24bit_error_on_heavy_tailed_inputs():
         errs[levels] = abs(approx - exact) / (np.abs(w) @ np.abs(x))
     assert errs[8388607] < errs[32767] / 50
     assert errs[8388607] < 1e-7
+
+
+def planes16(z):
+    """kernels_gemv.cuh prep_sb_vals<2>: signed high byte, unsigned low byte."""
+    z = np.asarray(z, np.int64)
+    h = ((z >> 8) & 0xFF).astype(np.uint8).view(np.int8).astype(np.int64)
+    return h, z & 0xFF
+
+
+def test_16bit_planes_recombine_and_clamp():
+    z = np.concatenate([np.arange(-600, 600), [-32767, -32766, -256, -1, 0, 1, 255, 32766, 32767]])
+    h, lo = planes16(z)
+    assert np.array_equal(h * 256 + lo, z)
+    rng = np.random.default_rng(4)
+    for _ in range(2000):
+        v = rng.standard_normal(256).astype(np.float32) * np.float32(10.0 ** rng.uniform(-3, 3))
+        amax = np.float32(np.max(np.abs(v)))
+        zc = np.clip(np.rint((v * (np.float32(32767.0) / amax)).astype(np.float32)).astype(np.int64), -32767, 32767)
+        h, lo = planes16(zc)
+        assert np.array_equal(h * 256 + lo, zc)
+
+
+def test_16bit_error_on_normalized_inputs():
+    """RMSNorm outputs (Gaussian-like, the inputs of q/k/v, o_proj, gate/up and
+    the head): the 16-bit form keeps the dot-product error near 1e-5 of the
+    absolute sum, the range the per-op 1e-3 bound leaves far behind."""
+    rng = np.random.default_rng(12)
+    k = 4096
+    x = rng.standard_normal(k)
+    x = (x / np.sqrt(np.mean(x * x))).astype(np.float32)
+    w = rng.standard_normal(k)
+    exact = w @ x.astype(np.float64)
+    approx = 0.0
+    for s in range(k // 256):
+        v = x[256 * s:256 * (s + 1)].astype(np.float64)
+        amax = np.max(np.abs(v))
+        z = np.clip(np.rint(v * 32767 / amax), -32767, 32767)
+        approx += (amax / 32767) * (w[256 * s:256 * (s + 1)] @ z)
+    assert abs(approx - exact) / (np.abs(w) @ np.abs(x)) < 2e-5
