@@ -85,7 +85,10 @@ typedef struct {
     uint32_t kv_bits_k;    /* 0 = float KV (KvQuantType::None); else packed key bits */
     uint32_t kv_bits_v;    /* packed value bits (KvQuantType::val_bits, src/quant/mod.rs:150) */
     uint32_t max_batch;    /* largest decode_batch the model will see (>= 1) */
-    uint32_t max_seq_len;  /* 0 = GGUF llama.context_length (src/engine/mod.rs:561) */
+    uint32_t max_seq_len;  /* 0 = GGUF llama.context_length (src/engine/mod.rs:561); KV tokens
+                              kept per sequence: a full cache drops its oldest token
+                              (KvCache::add, src/engine/mod.rs:410-426); positions run to
+                              4 * max_seq_len */
     uint32_t page_tokens;  /* KV page size in tokens, a power of two <= 4096; 0 = 16 (the
                               scheduler's page size, src/scheduler.rs:333-361) */
     uint32_t max_pages;    /* KV pages in the pool per rank; 0 = max_batch * ceil(max_seq_len /

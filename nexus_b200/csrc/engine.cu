@@ -1140,6 +1140,7 @@ struct nexus_cuda_model {
     uint32_t *page_table = nullptr;   // device copy of pm.table
     uint32_t max_seq = 0, max_batch = 1, bits_k = 0, bits_v = 0;
     int x_bits_norm = 24;  // GEMV input bits for matrices with normalized inputs
+    uint64_t rope_positions = 0;  // positions the RoPE table covers
     size_t bpt_k = 0, bpt_v = 0;
     int nsplit[kMaxChunk + 1] = {};     // attention slices per (sequence, KV head), float cache
     int nsplit_pk[kMaxChunk + 1] = {};  // the same for the packed-cache tensor-core kernel
@@ -1286,6 +1287,7 @@ static int model_load(nexus_cuda_backend *b, const char *path, nexus_cuda_model 
         return set_err(b, NEXUS_E_INVALID, "head_dim must be 32/64/128 and Hq/Hkv a power of two <= 8");
     if (H % 256 || F % 256) return set_err(b, NEXUS_E_INVALID, "hidden and ffn sizes must be multiples of 256");
     m->max_seq = I.max_seq_len;
+    m->rope_positions = 4 * (uint64_t)m->max_seq;
     m->max_batch = b->cfg.max_batch;
     m->bits_k = b->cfg.kv_bits_k;
     m->bits_v = b->cfg.kv_bits_v;
@@ -1460,7 +1462,9 @@ static int model_load(nexus_cuda_backend *b, const char *path, nexus_cuda_model 
     // RoPE table with the reference's f32 formula and the host libm
     // (rope_single, src/kernel/mod.rs:259-263)
     {
-        const size_t half = D / 2, npos = m->max_seq + 1;
+        // positions keep growing after the cache is full (it holds the last
+        // max_seq_len tokens): the table covers 4 x max_seq_len of them
+        const size_t half = D / 2, npos = m->rope_positions;
         std::vector<float> cs(npos * half), sn(npos * half);
         for (size_t pos = 0; pos < npos; pos++)
             for (size_t d = 0; d < half; d++) {
@@ -1565,6 +1569,7 @@ static int model_load(nexus_cuda_backend *b, const char *path, nexus_cuda_model 
             StepLaunch &sl = m->step_launch;
             // attention: slices of >= 32 tokens, about one block per CTA
             sp.attn_nsplit = std::max(1, std::min(64, sl.grid / (int)Hkv));
+            sp.max_seq = m->max_seq;
             NX_CUDA(b, malloc_tracked(m, &m->step_layers, hl.size()));
             NX_CUDA(b, cudaMemcpy(m->step_layers, hl.data(), hl.size() * sizeof(StepLayer), cudaMemcpyHostToDevice));
             sp.layers = m->step_layers;
@@ -1610,7 +1615,7 @@ static int pages_bind(nexus_cuda_model *m, uint32_t sid, const uint32_t *ids, ui
     if (pm.caller[sid] && pm.valid[sid] == n && std::equal(ids, ids + n, row)) return NEXUS_OK;  // unchanged
     if (n > pm.per_seq)
         return set_err(m->b, NEXUS_E_INVALID, "page list longer than max_seq_len / page_tokens entries");
-    const uint32_t cached = (m->seq_len[sid] + pm.page_tokens - 1) / pm.page_tokens;
+    const uint32_t cached = (std::min(m->seq_len[sid], m->max_seq) + pm.page_tokens - 1) / pm.page_tokens;
     if (n < cached) return set_err(m->b, NEXUS_E_INVALID, "page list shorter than the sequence's cached tokens");
     for (uint32_t i = 0; i < cached; i++)
         if (ids[i] != row[i])
@@ -1757,6 +1762,22 @@ static cudaError_t launch_linear(nexus_cuda_model *m, GemvParams g, cudaStream_t
 static int step_chunk(size_t remaining) {
     if (remaining >= (size_t)kGemmMinM) return (int)std::min<size_t>(remaining, kMaxChunk);
     return remaining >= 4 ? 4 : remaining >= 2 ? 2 : 1;
+}
+
+// KV cache as a ring (KvCache::add, src/engine/mod.rs:410-426: a full cache
+// drops its oldest token, so attention spans the last max_seq_len tokens).
+// Token number `total` of a sequence (0-based) is written to ring slot
+// total % max_seq_len and attends over min(total + 1, max_seq_len) slots --
+// the same tokens as the reference's shifted cache, in rotated order.
+static inline uint32_t ring_slot(const nexus_cuda_model *m, uint32_t total) { return total % m->max_seq; }
+static inline uint32_t ring_len(const nexus_cuda_model *m, uint32_t total) { return std::min(total + 1, m->max_seq); }
+
+// Tokens of the next step of one sequence that holds `total` tokens: a chunk
+// of consecutive tokens stays inside the ring's first pass (a chunk's tokens
+// attend to each other's slots); once the cache is full, one token per step.
+static int seq_chunk(const nexus_cuda_model *m, uint32_t total, size_t remaining) {
+    if (total >= m->max_seq) return 1;
+    return step_chunk(std::min<size_t>(remaining, m->max_seq - total));
 }
 
 // Enqueue one fused decode step for `mc` tokens whose DevSeq entries are on the device.
@@ -1997,7 +2018,7 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         }
     }
     if (prof) prof->begin();
-    e = launch_advance(m->seqs, mc, m->out_tokens, m->has_head ? pdl : 0, st);
+    e = launch_advance(m->seqs, mc, m->out_tokens, m->max_seq, m->has_head ? pdl : 0, st);
     if (prof) prof->end("advance", 64.0 * mc);
     return e;
 }
@@ -2094,8 +2115,8 @@ static int host_step(nexus_cuda_model *m, const StepItem *items, int mc, float *
         DevSeq s = {};
         s.token = items[t].token;
         s.position = items[t].position;
-        s.slot = items[t].slot;
-        s.seq_len = items[t].slot + 1;
+        s.slot = ring_slot(m, items[t].slot);
+        s.seq_len = ring_len(m, items[t].slot);
         m->h_seqs[t] = s;
         m->h_seq_ids[t] = items[t].sid;
     }
@@ -2165,7 +2186,7 @@ extern "C" int nexus_cuda_seq_reset(nexus_cuda_model *m, uint32_t seq_id) {
 
 extern "C" int nexus_cuda_seq_len(nexus_cuda_model *m, uint32_t seq_id, uint32_t *len) {
     if (!m || !len || seq_id >= m->max_batch) return set_err(m ? m->b : nullptr, NEXUS_E_INVALID, "bad sequence id");
-    *len = m->seq_len[seq_id];
+    *len = std::min(m->seq_len[seq_id], m->max_seq);  // KvCache::seq_len: the cached tokens
     return NEXUS_OK;
 }
 
@@ -2187,15 +2208,14 @@ extern "C" int nexus_cuda_seq_set_pages(nexus_cuda_model *m, uint32_t seq_id, co
 
 static int check_slot(nexus_cuda_model *m, uint32_t sid, uint32_t add) {
     if (sid >= m->max_batch) return set_err(m->b, NEXUS_E_INVALID, "bad sequence id");
-    if ((uint64_t)m->seq_len[sid] + add > m->max_seq)
-        return set_err(m->b, NEXUS_E_INVALID, "KV cache full: the backend does not shift the cache (raise max_seq_len)");
     int rc = pages_default(m, sid);
-    if (!rc) rc = pages_cover(m, sid, (uint64_t)m->seq_len[sid] + add);
+    if (!rc) rc = pages_cover(m, sid, std::min<uint64_t>((uint64_t)m->seq_len[sid] + add, m->max_seq));
     return rc;
 }
 
 static int check_position(nexus_cuda_model *m, uint64_t position) {
-    if (position > m->max_seq) return set_err(m->b, NEXUS_E_INVALID, "position beyond the RoPE table (max_seq_len)");
+    if (position >= m->rope_positions)
+        return set_err(m->b, NEXUS_E_INVALID, "position beyond the RoPE table (4 x max_seq_len positions)");
     return NEXUS_OK;
 }
 
@@ -2231,7 +2251,7 @@ static int prefill_impl(nexus_cuda_model *m, uint32_t seq_id, const uint32_t *to
     size_t p = 0;
     uint32_t last = 0;
     while (p < n) {
-        const int mc = step_chunk(n - p);
+        const int mc = seq_chunk(m, (uint32_t)p, n - p);
         StepItem it[kMaxChunk];
         for (int j = 0; j < mc; j++) it[j] = {seq_id, tokens[p + j], (uint32_t)(p + j), (uint32_t)(p + j)};
         const bool final = p + mc == n;
@@ -2280,8 +2300,8 @@ extern "C" int nexus_cuda_generate(nexus_cuda_model *m, uint32_t seq_id, const u
     DevSeq s = {};
     s.token = next;
     s.position = (uint32_t)n;
-    s.slot = m->seq_len[seq_id];
-    s.seq_len = s.slot + 1;
+    s.slot = ring_slot(m, m->seq_len[seq_id]);
+    s.seq_len = ring_len(m, m->seq_len[seq_id]);
     m->h_seqs[0] = s;
     m->h_seq_ids[0] = seq_id;
     cudaStream_t st = b->stream;
@@ -2353,11 +2373,14 @@ extern "C" int nexus_cuda_generate_with_draft(nexus_cuda_model *m, uint32_t seq_
         if (i + 1 >= n_draft) w = 1;
         else w = std::min(w, n_draft - i);
         const uint32_t base = m->seq_len[seq_id];
+        // a window is cut back to its first rejection, which a wrapped ring
+        // cannot undo: windows stay inside the ring's first pass
+        if ((uint64_t)base + w > m->max_seq) w = 1;
         std::vector<uint32_t> toks(w);
         toks[0] = next;
         for (size_t j = 1; j < w; j++) toks[j] = draft[i + j];
         for (size_t p = 0; p < w;) {
-            const int mc = step_chunk(w - p);
+            const int mc = seq_chunk(m, base + (uint32_t)p, w - p);
             for (int j = 0; j < mc; j++)
                 it[j] = {seq_id, toks[p + j], (uint32_t)(n + i + p + j), base + (uint32_t)(p + j)};
             rc = host_step(m, it, mc, nullptr, 0, am + p);
@@ -2452,8 +2475,8 @@ extern "C" int nexus_cuda_profile_decode(nexus_cuda_model *m, uint32_t seq_id, u
         DevSeq s = {};
         s.token = tok;
         s.position = slot;
-        s.slot = slot;
-        s.seq_len = slot + 1;
+        s.slot = ring_slot(m, slot);
+        s.seq_len = ring_len(m, slot);
         m->h_seqs[0] = s;
         m->h_seq_ids[0] = seq_id;
         NX_CUDA(b, pages_upload(m));

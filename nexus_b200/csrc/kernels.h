@@ -158,7 +158,7 @@ struct KvPackParams {
 };
 cudaError_t launch_kv_pack(const KvPackParams &p, cudaStream_t st);
 // device-chained decode: next token = argmax, positions advance by one
-cudaError_t launch_advance(DevSeq *seqs, int m, uint32_t *out_tokens, int pdl, cudaStream_t st);
+cudaError_t launch_advance(DevSeq *seqs, int m, uint32_t *out_tokens, uint32_t ring, int pdl, cudaStream_t st);
 
 // ---- kernels_step.cu: the single-token decode step as one persistent kernel ----
 // One matrix in the tile layout (tiles.cuh): fmt, tiles, Q2_K side words, rows, columns.
@@ -191,6 +191,7 @@ struct StepParams {
     float *attn_part;               // [hkv][attn_nsplit][G][head_dim + 2]
     unsigned *attn_counters;        // [hkv], zero between launches
     int attn_nsplit;
+    uint32_t max_seq;               // KV ring slots per sequence (the cache keeps the last max_seq tokens)
     float *gpart;                   // [grid * warps][2][32] partial row sums of shared row groups
     unsigned *gcounters;            // [max row groups], zero between launches
     unsigned *bar;                  // grid barrier: arrivals, generation

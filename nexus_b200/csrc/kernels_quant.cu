@@ -335,8 +335,10 @@ cudaError_t launch_kv_pack(const KvPackParams &p, cudaStream_t st) {
 
 // Advance every sequence of a device-chained decode step: the next input token
 // is this step's greedy argmax (0 when no logit was finite), positions move by
-// one, and the token is appended to ring[t][gen_index].
-__global__ void k_advance(DevSeq *seqs, int m, uint32_t *out_tokens) {
+// one, and the KV slot moves to the next slot of the sequence's ring of
+// `ring` slots (a full cache drops its oldest token, KvCache::add,
+// src/engine/mod.rs:410-426), attending over at most `ring` tokens.
+__global__ void k_advance(DevSeq *seqs, int m, uint32_t *out_tokens, uint32_t ring) {
     const int t = threadIdx.x;
     if (t >= m) return;
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -345,12 +347,12 @@ __global__ void k_advance(DevSeq *seqs, int m, uint32_t *out_tokens) {
     out_tokens[t] = tok;
     s.token = tok;
     s.position += 1;
-    s.slot += 1;
-    s.seq_len += 1;
+    s.slot = s.slot + 1 == ring ? 0u : s.slot + 1;
+    s.seq_len = s.seq_len < ring ? s.seq_len + 1 : ring;
     seqs[t] = s;
 }
 
-cudaError_t launch_advance(DevSeq *seqs, int m, uint32_t *out_tokens, int pdl, cudaStream_t st) {
+cudaError_t launch_advance(DevSeq *seqs, int m, uint32_t *out_tokens, uint32_t ring, int pdl, cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(1);
     cfg.blockDim = dim3(32 * ((m + 31) / 32));
@@ -360,7 +362,7 @@ cudaError_t launch_advance(DevSeq *seqs, int m, uint32_t *out_tokens, int pdl, c
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, k_advance, seqs, m, out_tokens);
+    return cudaLaunchKernelEx(&cfg, k_advance, seqs, m, out_tokens, ring);
 }
 
 }  // namespace nx

@@ -544,8 +544,9 @@ __global__ void __launch_bounds__(W * 32, 1) k_decode_step(StepParams sp) {
             sp.out_tokens[0] = tok;
             s.token = tok;
             s.position += 1;
-            s.slot += 1;
-            s.seq_len += 1;
+            // the next slot of the sequence's ring of max_seq slots
+            s.slot = s.slot + 1 == sp.max_seq ? 0u : s.slot + 1;
+            s.seq_len = s.seq_len < sp.max_seq ? s.seq_len + 1 : sp.max_seq;
             sp.seqs[0] = s;
         }
         return;

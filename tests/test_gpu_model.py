@@ -158,13 +158,68 @@ def test_head_dim_128_packed_kv(nb, oracle, bits):
     assert max(errs) < 2e-2, errs
 
 
-def test_kv_overflow_is_an_error_not_a_shift(nb, tiny_path):
-    b = nb.CudaBackend(device=0, max_seq_len=8)
+RING = 24  # max_seq_len of the full-cache tests
+
+
+@pytest.mark.parametrize("flags,kv_bits", [(0, (0, 0)), (0, (4, 4)), (0x4, (0, 0))],
+                         ids=["graph", "packed", "persistent"])
+def test_full_cache_drops_oldest_token(nb, oracle, tiny_path, flags, kv_bits):
+    """KvCache::add on a full cache drops its oldest token and appends the new
+    one (src/engine/mod.rs:410-426), so decoding continues past max_seq_len
+    with attention over the last max_seq_len tokens.  Device-chained generate,
+    single decodes with logits, a prompt longer than the cache and the draft
+    verify path all match the oracle's shifting cache."""
+    b = nb.CudaBackend(device=0, max_seq_len=RING, kv_bits=kv_bits, flags=flags)
     e = nb.InferenceEngine(b)
     e.load_model(tiny_path)
-    e.prefill(list(range(8)))
-    with pytest.raises(nb.NexusError):
-        e.decode_with_cache(1, 8)
+    ref = oracle.Model(tiny_path, kv_bits=kv_bits, max_seq_len=RING)
+    tol = LOGIT_TOL if kv_bits == (0, 0) else 2e-2
+    p = prompt(3, 20, 4096)
+    want = ref.generate(p, 30)
+    assert e.generate(p, 30) == want
+    assert e.seq_len() == RING
+    # single-token decodes past the boundary, logits each step
+    ref2 = oracle.Model(tiny_path, kv_bits=kv_bits, max_seq_len=RING)
+    q = prompt(4, 22, 4096)
+    got, tok = e.prefill(q)
+    assert np.max(np.abs(got - ref2.prefill(q))) < tol
+    for i in range(8):
+        got, tok2 = e.decode_with_cache(tok, len(q) + i)
+        want_l = ref2.decode(tok, len(q) + i)
+        assert np.max(np.abs(got - want_l)) < tol, i
+        tok = tok2
+    assert e.seq_len() == RING
+    # a prompt longer than the cache: the chunks stop at the wrap
+    ref3 = oracle.Model(tiny_path, kv_bits=kv_bits, max_seq_len=RING)
+    r = prompt(5, 61, 4096)
+    got, _ = e.prefill(r)
+    assert np.max(np.abs(got - ref3.prefill(r))) < tol
+    # draft verify across the boundary: the greedy tokens as the draft
+    cont = ref.generate(p, 12)
+    out, (acc, rej) = e.generate_with_draft_tokens(p, 12, cont[len(p):], window=8)
+    assert out == cont and (acc, rej) == (12, 0)
+    e.close()
+    b.close()
+
+
+def test_full_cache_decode_batch(nb, oracle, tiny_path):
+    """Two sequences decoded together past max_seq_len (one wraps first)."""
+    b = nb.CudaBackend(device=0, max_seq_len=RING, max_batch=2)
+    e = nb.InferenceEngine(b)
+    e.load_model(tiny_path)
+    ps = [prompt(6, 18, 4096), prompt(7, 23, 4096)]
+    want = [oracle.Model(tiny_path, max_seq_len=RING).generate(p, 14) for p in ps]
+    toks = []
+    for s, p in enumerate(ps):
+        toks.append(e.prefill(p, seq_id=s, want_logits=False)[1])
+    got = [[t] for t in toks]
+    for i in range(13):
+        toks, _ = e.decode_batch([(s, toks[s], len(ps[s]) + i) for s in range(2)])
+        for s in range(2):
+            got[s].append(toks[s])
+    for s in range(2):
+        assert ps[s] + got[s] == want[s], s
+        assert e.seq_len(s) == RING
     e.close()
     b.close()
 
