@@ -669,11 +669,13 @@ def main():
     if rank == 0 and not args.no_cpu_baseline:
         # bounded (~20 s): a short prompt, so no long CPU prefill holds the GPU;
         # the reference arm times the same steps at the bench's contexts 512+
-        r = time_oracle(path, 64, 1, budget_s=20.0, threads=cpu_threads(), prompt_len=4)
+        r = time_oracle(path, 64, 1, budget_s=20.0, threads=cpu_threads(), prompt_len=4, single_core_steps=2)
         line["cpu_baseline"] = {"value": r["tok_s"], "unit": "tok/s", "cores": r["threads"], "kind": "port",
                                 "sample": f"{r['steps']} decode steps of the same model at contexts "
                                           f"{r['ctx'][0]}-{r['ctx'][1]} after a 4-token prompt (oracle restatement "
-                                          "of the reference CPU path; the reference arm times contexts 512+)"}
+                                          "of the reference CPU path; the reference arm times contexts 512+)",
+                                # the reference's decode path is single-threaded (src/engine/mod.rs:775-801)
+                                "single_core": r["single_core"]}
     if dist is not None:
         barrier(dist, device)
         dist.destroy_process_group()

@@ -58,11 +58,17 @@ constexpr unsigned kSpin = 1u << 22;
 // hi + lo (two MMAs per K step, no min term, no per-super-block scale).
 template <int FMT>
 struct GemmFmt;
+#ifndef NX_Q4K_RAW_SLOTS
+#define NX_Q4K_RAW_SLOTS 3
+#endif
+#ifndef NX_Q4K_STAGES
+#define NX_Q4K_STAGES 6
+#endif
 template <>
 struct GemmFmt<12> {  // Q4_K
     static constexpr bool MIN = true;
     static constexpr int A_MATS = 1;
-    static constexpr int RAW_SLOTS = 3, STAGES = 6;
+    static constexpr int RAW_SLOTS = NX_Q4K_RAW_SLOTS, STAGES = NX_Q4K_STAGES;
 };
 template <>
 struct GemmFmt<8> {  // Q8_0
