@@ -669,7 +669,7 @@ def main():
     if rank == 0 and not args.no_cpu_baseline:
         # bounded (~20 s): a short prompt, so no long CPU prefill holds the GPU;
         # the reference arm times the same steps at the bench's contexts 512+
-        r = time_oracle(path, 64, 1, budget_s=20.0, threads=cpu_threads(), prompt_len=4, single_core_steps=2)
+        r = time_oracle(path, 64, 1, budget_s=20.0, threads=cpu_threads(), prompt_len=4, single_core_steps=1)
         line["cpu_baseline"] = {"value": r["tok_s"], "unit": "tok/s", "cores": r["threads"], "kind": "port",
                                 "sample": f"{r['steps']} decode steps of the same model at contexts "
                                           f"{r['ctx'][0]}-{r['ctx'][1]} after a 4-token prompt (oracle restatement "

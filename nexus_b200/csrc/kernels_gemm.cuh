@@ -31,8 +31,14 @@
 //   warp 9     TMEM allocation + TMA copies of the prepared activations
 //   warp 10    tcgen05.mma issue (one thread)
 // A work unit is (token tile, 128-row tile, K split); a super-block runs as 4
-// quarter stages of 64 K (A: 16 KB in a 6-slot ring, B: NT*256 bytes in a
-// 6- or 8-slot ring), so operands are staged ahead of the MMAs.  K-split partial sums
+// quarter stages of 64 K (A: 128 x 64 f16 per stage in a 6-slot ring, B:
+// NT*256 bytes per stage), so operands are staged ahead of the MMAs.  The
+// super-block formats (Q4_K, Q2_K) keep A in tensor memory: the dequantizing
+// warps write their 32 rows of a stage with one tcgen05.st (32 columns, two
+// f16 per column) and the MMA reads A from there, which takes the 64 KB of
+// dequantized A per super-block off shared memory (written once and read by
+// every MMA); the block formats, whose 64-token tiles need all of tensor
+// memory for accumulators, stage A in shared memory.  K-split partial sums
 // meet in global scratch and the last CTA of a tile adds them in split order
 // (deterministic) before the fused epilogue of kernels_gemv.cuh.
 // Each warp signals a barrier once (after __syncwarp), so the arrival counts
@@ -113,12 +119,15 @@ struct Smem {
     static constexpr int BSLOTS = GF::STAGES;
     static constexpr int A_MAT = 8 * 128 * 16;          // one 128 x 64 f16 matrix
     static constexpr int A_BYTES = GF::A_MATS * A_MAT;  // one quarter stage
+    // the super-block formats keep A in tensor memory (a_in_tmem): no
+    // shared-memory A ring
+    static constexpr int A_SMEM = GF::MIN ? 0 : A_BYTES;
     static constexpr int B_BYTES = NT * 256;
     static constexpr int AMIN_BYTES = GF::MIN ? 2 * 128 * 16 : 0;
     static constexpr int BMIN_BYTES = GF::MIN ? NT * 64 : 0;
     static constexpr int RAW = 0;
     static constexpr int A = RAW + RSLOTS * Raw<FMT>::SLOT;
-    static constexpr int B = A + ASLOTS * A_BYTES;
+    static constexpr int B = A + ASLOTS * A_SMEM;
     static constexpr int AMIN = B + BSLOTS * B_BYTES;
     static constexpr int BMIN = AMIN + 2 * AMIN_BYTES;
     static constexpr int TOTAL = BMIN + 2 * BMIN_BYTES + 1024;  // + alignment slack
@@ -195,6 +204,30 @@ __device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, float (&v)[16]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Lane i of the warp writes v[0..31] to columns taddr.col .. +31 of TMEM lane
+// taddr.lane + i (the warp's 32-lane quarter).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+        "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+        "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// MMA whose A operand is in tensor memory (lane = row, two f16 of K per
+// column), issued by an elected lane of a converged warp.
+__device__ __forceinline__ void umma_f16_ts_w(uint32_t dt, uint32_t at, uint64_t bd, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p, q;\n elect.sync _|p, 0xffffffff;\n setp.ne.b32 q, %4, 0;\n"
+        " @p tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5}, q;\n}\n" ::"r"(dt),
+        "r"(at), "l"(bd), "r"(idesc), "r"(acc), "r"(0u)
+        : "memory");
+}
+
 // Bounded mbarrier wait; false once this CTA has given up (abort set).
 __device__ __forceinline__ bool bwait(unsigned long long *bar, unsigned parity, volatile int *abort_flag, int *err) {
     unsigned n = 0;
@@ -239,30 +272,29 @@ __device__ __forceinline__ void unit_coords(const GemmShape &g, int u, int &tt, 
 }
 
 // Q4_K dequantization of one quarter (qs bytes 32q..32q+31 of the row) into
-// the stage's A chunks.  K order inside a quarter: positions 0..31 are the
-// low nibbles (sub-block q), 32..63 the high nibbles (sub-block q+4); within
-// each 4-byte word the order is bytes 0,2,1,3 (the prepared activations use
-// the same order, so the product is unchanged).
-__device__ __forceinline__ void dq_q4k_quarter(const uint32_t (&w)[8], uint32_t sc_lo, uint32_t sc_hi,
-                                               uint8_t *a_row) {
-    // exact f16 products: (1024+q)*sc - 1024*sc and (1024+16q)*(sc/16) - 64*sc
+// the A stage: K order inside a quarter: positions 0..31 are the low nibbles
+// (sub-block q), 32..63 the high nibbles (sub-block q+4); within each 4-byte
+// word the order is bytes 0,2,1,3 (the prepared activations use the same
+// order, so the product is unchanged).  Exact f16 products:
+// (1024+q)*sc - 1024*sc and (1024+16q)*(sc/16) - 64*sc.
+// The quarter as 32 TMEM columns: K-chunk c (8 elements) in columns
+// 4c..4c+3, two f16 per column, in the K order of the prepared activations.
+__device__ __forceinline__ void dq_q4k_quarter_cols(const uint32_t (&w)[8], uint32_t sc_lo, uint32_t sc_hi,
+                                                    uint32_t (&v)[32]) {
     const uint32_t ml = f16x2_splat((float)sc_lo), bl = f16x2_splat(-1024.0f * (float)sc_lo);
     const uint32_t mh = f16x2_splat((float)sc_hi * 0.0625f), bh = f16x2_splat(-64.0f * (float)sc_hi);
 #pragma unroll
     for (int kc = 0; kc < 4; kc++) {
         const uint32_t w0 = w[2 * kc], w1 = w[2 * kc + 1];
         const uint32_t w0s = w0 >> 8, w1s = w1 >> 8;
-        uint4 lo, hi;
-        lo.x = hfma2u(lop_or(w0, 0x000f000fu), ml, bl);
-        lo.y = hfma2u(lop_or(w0s, 0x000f000fu), ml, bl);
-        lo.z = hfma2u(lop_or(w1, 0x000f000fu), ml, bl);
-        lo.w = hfma2u(lop_or(w1s, 0x000f000fu), ml, bl);
-        hi.x = hfma2u(lop_or(w0, 0x00f000f0u), mh, bh);
-        hi.y = hfma2u(lop_or(w0s, 0x00f000f0u), mh, bh);
-        hi.z = hfma2u(lop_or(w1, 0x00f000f0u), mh, bh);
-        hi.w = hfma2u(lop_or(w1s, 0x00f000f0u), mh, bh);
-        *reinterpret_cast<uint4 *>(a_row + kc * 2048) = lo;
-        *reinterpret_cast<uint4 *>(a_row + (4 + kc) * 2048) = hi;
+        v[4 * kc + 0] = hfma2u(lop_or(w0, 0x000f000fu), ml, bl);
+        v[4 * kc + 1] = hfma2u(lop_or(w0s, 0x000f000fu), ml, bl);
+        v[4 * kc + 2] = hfma2u(lop_or(w1, 0x000f000fu), ml, bl);
+        v[4 * kc + 3] = hfma2u(lop_or(w1s, 0x000f000fu), ml, bl);
+        v[16 + 4 * kc + 0] = hfma2u(lop_or(w0, 0x00f000f0u), mh, bh);
+        v[16 + 4 * kc + 1] = hfma2u(lop_or(w0s, 0x00f000f0u), mh, bh);
+        v[16 + 4 * kc + 2] = hfma2u(lop_or(w1, 0x00f000f0u), mh, bh);
+        v[16 + 4 * kc + 3] = hfma2u(lop_or(w1s, 0x00f000f0u), mh, bh);
     }
 }
 
@@ -304,20 +336,18 @@ __device__ __forceinline__ void dq_q80_quarter(const uint32_t (&w)[16], uint32_t
 
 // Q2_K dequantization of one quarter (sub-blocks 4q..4q+3, one tile word
 // each; bits 2k..2k+1 of byte b are element 16j+4k+b) into exact f16
-// sc_j*q.  K order inside a sub-block: bit-plane k, bytes 0,2,1,3.
-__device__ __forceinline__ void dq_q2k_quarter(const uint32_t (&w)[4], uint32_t sc4, uint8_t *a_row) {
+// sc_j*q.  K order inside a sub-block: bit-plane k, bytes 0,2,1,3; as 32
+// TMEM columns (K-chunk c in columns 4c..4c+3).
+__device__ __forceinline__ void dq_q2k_quarter_cols(const uint32_t (&w)[4], uint32_t sc4, uint32_t (&v)[32]) {
 #pragma unroll
     for (int jj = 0; jj < 4; jj++) {
         const float sc = (float)((sc4 >> (8 * jj)) & 0xfu);
         const uint32_t ms = f16x2_splat(sc), bs = f16x2_splat(-1024.0f * sc);
-        uint32_t v[8];
 #pragma unroll
         for (int k = 0; k < 4; k++) {
-            v[2 * k] = hfma2u(lop_or(w[jj] >> (2 * k), 0x00030003u), ms, bs);
-            v[2 * k + 1] = hfma2u(lop_or(w[jj] >> (2 * k + 8), 0x00030003u), ms, bs);
+            v[8 * jj + 2 * k] = hfma2u(lop_or(w[jj] >> (2 * k), 0x00030003u), ms, bs);
+            v[8 * jj + 2 * k + 1] = hfma2u(lop_or(w[jj] >> (2 * k + 8), 0x00030003u), ms, bs);
         }
-        *reinterpret_cast<uint4 *>(a_row + (2 * jj) * 2048) = make_uint4(v[0], v[1], v[2], v[3]);
-        *reinterpret_cast<uint4 *>(a_row + (2 * jj + 1) * 2048) = make_uint4(v[4], v[5], v[6], v[7]);
     }
 }
 
@@ -380,8 +410,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_units = g.n_tt * g.n_rt * g.nsplit;
-    // per accumulator buffer: D (2NT columns: hi tokens, lo tokens), E (2NT)
-    constexpr uint32_t kTmemCols = 8 * NT;
+    // per accumulator buffer: D (2NT columns: hi tokens, lo tokens), E (2NT);
+    // the super-block formats add their A stages (32 columns each) after the
+    // accumulators; allocations are powers of two
+    constexpr uint32_t kAccCols = 8 * NT;
+    constexpr uint32_t kACol = kAccCols;  // first A stage column
+    constexpr uint32_t kTmemCols = GF::MIN ? 512u : kAccCols;
+    static_assert(!GF::MIN || kAccCols + 32 * S::ASLOTS <= 512, "A stages exceed tensor memory");
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kRawSlots; i++) {
@@ -529,11 +564,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int kk = 0; kk < 4; kk++) {
                         const uint32_t bq = b0 + bs * S::B_BYTES + kk * 2 * NT * 32;
                         const uint64_t bd = umma_desc(bq, NT * 32, 128);
+                        if constexpr (GF::MIN) {
+                            // A in tensor memory: stage `as`, K step kk = 8 columns
+                            umma_f16_ts_w(dcol, tmem + kACol + 32 * as + 8 * kk, bd, idesc, (q | kk) != 0);
+                        } else {
 #pragma unroll
-                        for (int am = 0; am < GF::A_MATS; am++) {
-                            const uint64_t ad =
-                                umma_desc(a0 + as * S::A_BYTES + am * S::A_MAT + kk * 2 * 2048, 2048, 128);
-                            umma_f16_w(dcol, ad, bd, idesc, (q | kk | am) != 0 || (!GF::MIN && s != s0));
+                            for (int am = 0; am < GF::A_MATS; am++) {
+                                const uint64_t ad =
+                                    umma_desc(a0 + as * S::A_BYTES + am * S::A_MAT + kk * 2 * 2048, 2048, 128);
+                                umma_f16_w(dcol, ad, bd, idesc, (q | kk | am) != 0 || s != s0);
+                            }
                         }
                     }
                     umma_commit_w(&st_empty[as]);
@@ -703,8 +743,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         uint32_t w8[8];
 #pragma unroll
                         for (int i = 0; i < 8; i++) w8[i] = wq[8 * qq + i];
-                        dq_q4k_quarter(w8, byte_of(scl, q), byte_of(sch, q), smem + S::A + as * S::A_BYTES + r * 16);
-                        fence_proxy_async_smem();
+                        uint32_t cols[32];
+                        dq_q4k_quarter_cols(w8, byte_of(scl, q), byte_of(sch, q), cols);
+                        tc_fence_after();  // the MMAs that read this stage have completed
+                        tmem_st32(tmem + t_lane + kACol + 32 * as, cols);
+                        tmem_wait_st();
+                        tc_fence_before();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&st_full[as]);
                         if (q == 0) {
@@ -749,8 +793,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         bwait(&st_empty[as], ((c / kASlots) & 1) ^ 1, &abort_s, p.err);
                         const uint4 wv = qq ? qb : qa;
                         const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
-                        dq_q2k_quarter(w4, scw[q] & 0x0f0f0f0fu, smem + S::A + as * S::A_BYTES + r * 16);
-                        fence_proxy_async_smem();
+                        uint32_t cols[32];
+                        dq_q2k_quarter_cols(w4, scw[q] & 0x0f0f0f0fu, cols);
+                        tc_fence_after();  // the MMAs that read this stage have completed
+                        tmem_st32(tmem + t_lane + kACol + 32 * as, cols);
+                        tmem_wait_st();
+                        tc_fence_before();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&st_full[as]);
                         if (q == 0) {
