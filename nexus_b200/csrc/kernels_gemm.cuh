@@ -123,7 +123,7 @@ struct Smem {
     // shared-memory A ring
     static constexpr int A_SMEM = GF::MIN ? 0 : A_BYTES;
     static constexpr int B_BYTES = NT * 256;
-    static constexpr int AMIN_BYTES = GF::MIN ? 2 * 128 * 16 : 0;
+    static constexpr int AMIN_BYTES = 0;  // the min operand lives in tensor memory
     static constexpr int BMIN_BYTES = GF::MIN ? NT * 64 : 0;
     static constexpr int RAW = 0;
     static constexpr int A = RAW + RSLOTS * Raw<FMT>::SLOT;
@@ -215,6 +215,12 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32
         "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
         "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
         : "memory");
+}
+// Lane i of the warp writes v[0..7] to columns taddr.col .. +7 of TMEM lane taddr.lane + i.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
+                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -416,7 +422,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr uint32_t kAccCols = 8 * NT;
     constexpr uint32_t kACol = kAccCols;  // first A stage column
     constexpr uint32_t kTmemCols = GF::MIN ? 512u : kAccCols;
-    static_assert(!GF::MIN || kAccCols + 32 * S::ASLOTS <= 512, "A stages exceed tensor memory");
+    // and the two min-operand stages (8 columns each: K = 16 of one MMA)
+    constexpr uint32_t kMinCol = kACol + 32 * S::ASLOTS;
+    static_assert(!GF::MIN || kMinCol + 16 <= 512, "A stages exceed tensor memory");
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kRawSlots; i++) {
@@ -534,7 +542,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---- MMA issue (whole warp, elected lane) ----
         constexpr uint32_t idesc = umma_idesc<2 * NT>();
         const uint32_t a0 = smem_u32(smem + S::A), b0 = smem_u32(smem + S::B);
-        const uint32_t amin0 = smem_u32(smem + S::AMIN), bmin0 = smem_u32(smem + S::BMIN);
+        const uint32_t bmin0 = smem_u32(smem + S::BMIN);
         unsigned n = 0, c = 0, nu = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, nu++) {
@@ -582,9 +590,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ok = __all_sync(0xffffffffu, bwait(&mn_full[ms], (n >> 1) & 1, &abort_s, p.err));
                         if (!ok) break;
                         tc_fence_after();
-                        const uint64_t ad = umma_desc(amin0 + ms * S::AMIN_BYTES, 2048, 128);
                         const uint32_t bm = bmin0 + ms * S::BMIN_BYTES;
-                        umma_f16_w(ecol, ad, umma_desc(bm, NT * 32, 128), idesc, 0);
+                        umma_f16_ts_w(ecol, tmem + kMinCol + 8 * ms, umma_desc(bm, NT * 32, 128), idesc, 0);
                         umma_commit_w(&mn_empty[ms]);
                     }
                 }
@@ -764,10 +771,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                                    ((uint32_t)__half_as_ushort(__float2half_rn((float)byte_of(mnh, 1))) << 16);
                             m0.w = __half_as_ushort(__float2half_rn((float)byte_of(mnh, 2))) |
                                    ((uint32_t)__half_as_ushort(__float2half_rn((float)byte_of(mnh, 3))) << 16);
-                            uint8_t *am = smem + S::AMIN + ms * S::AMIN_BYTES + r * 16;
-                            *reinterpret_cast<uint4 *>(am) = m0;
-                            *reinterpret_cast<uint4 *>(am + 2048) = make_uint4(0, 0, 0, 0);
-                            fence_proxy_async_smem();
+                            const uint32_t mc[8] = {m0.x, m0.y, m0.z, m0.w, 0u, 0u, 0u, 0u};
+                            tc_fence_after();  // the min MMA that read this stage has completed
+                            tmem_st8(tmem + t_lane + kMinCol + 8 * ms, mc);
+                            tmem_wait_st();
+                            tc_fence_before();
                             __syncwarp();
                             if (lane == 0) mbar_arrive(&mn_full[ms]);
                         }
@@ -813,10 +821,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 mw[i] = __half_as_ushort(__float2half_rn(m0)) |
                                         ((uint32_t)__half_as_ushort(__float2half_rn(m1)) << 16);
                             }
-                            uint8_t *am = smem + S::AMIN + ms * S::AMIN_BYTES + r * 16;
-                            *reinterpret_cast<uint4 *>(am) = make_uint4(mw[0], mw[1], mw[2], mw[3]);
-                            *reinterpret_cast<uint4 *>(am + 2048) = make_uint4(mw[4], mw[5], mw[6], mw[7]);
-                            fence_proxy_async_smem();
+                            tc_fence_after();  // the min MMA that read this stage has completed
+                            tmem_st8(tmem + t_lane + kMinCol + 8 * ms, mw);
+                            tmem_wait_st();
+                            tc_fence_before();
                             __syncwarp();
                             if (lane == 0) mbar_arrive(&mn_full[ms]);
                         }
