@@ -58,7 +58,7 @@ SEED_PROMPT = 1
 # dominant kernel, from one ncu capture of the same kernel and shape (the
 # command and the full table are in the profiles/ summary named here).
 DOMINANT_TRAFFIC = {
-    "gate_up": (66289664, "ncu --set full capture of k_gemv<Q4_K> 28672x4096, 1 token "
+    "gate_up": (66329088, "ncu --set full capture of k_gemv<Q4_K> 28672x4096, 1 token "
                           "(profiles/k_gemv_q4k_gateup_28672x4096_m1.md)"),
 }
 
@@ -246,13 +246,31 @@ def run_ncu_case(args):
     decode steps from the captured graph (5 kernels per layer + 3 per step)."""
     import nexus_b200 as nb
     path = nb.model_path(args.config, threads=cpu_threads())
-    backend = nb.CudaBackend(device=0, max_seq_len=64)
+    b = max(1, args.ncu_batch)
+    backend = nb.CudaBackend(device=0, max_seq_len=64, max_batch=b)
     eng = nb.InferenceEngine(backend)
     eng.load_model(path)
-    prompt = np.random.default_rng(SEED_PROMPT).integers(0, eng.info.vocab_rows, 8).tolist()
-    out = eng.generate(prompt, args.ncu_steps)
-    print(json.dumps({"ncu_case": args.config, "prefill": 8, "decode_steps": args.ncu_steps,
-                      "tokens": out[8:], "kernels_per_step": 5 * eng.info.num_layers + 3}), flush=True)
+    if b == 1:
+        prompt = np.random.default_rng(SEED_PROMPT).integers(0, eng.info.vocab_rows, 8).tolist()
+        out = eng.generate(prompt, args.ncu_steps)
+        print(json.dumps({"ncu_case": args.config, "prefill": 8, "decode_steps": args.ncu_steps,
+                          "tokens": out[8:], "kernels_per_step": 5 * eng.info.num_layers + 3}), flush=True)
+    else:
+        # b sequences of 8 prompt tokens (seed 1 + i), then ncu_steps batched
+        # decode steps over all of them (the tensor-core GEMM path)
+        toks = []
+        for i in range(b):
+            prompt = np.random.default_rng(SEED_PROMPT + i).integers(0, eng.info.vocab_rows, 8).tolist()
+            toks.append(eng.prefill(prompt, seq_id=i, want_logits=False)[1])
+        import torch
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()  # ncu --profile-from-start off captures the decode steps only
+        for s in range(args.ncu_steps):
+            toks, _ = eng.decode_batch([(i, toks[i], 8 + s) for i in range(b)])
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        print(json.dumps({"ncu_case": args.config, "batch": b, "prefill": 8, "decode_steps": args.ncu_steps}),
+              flush=True)
     eng.close()
     backend.close()
     return 0
@@ -524,6 +542,8 @@ def main():
     ap.add_argument("--ref-budget", type=float, default=60.0)
     ap.add_argument("--profile-steps", type=int, default=4)
     ap.add_argument("--batch", type=int, default=32, help="batched-decode measurement (config E at b=32); 1 = off")
+    ap.add_argument("--ncu-batch", type=int, default=1,
+                    help="with --ncu-steps: batched decode steps over this many sequences (8-token prompts each)")
     ap.add_argument("--ncu-steps", type=int, default=0,
                     help="profiling run for ncu: 8-token prefill (2 fused 4-token steps), then this many "
                          "device-chained decode steps; prints a short JSON line")
