@@ -81,18 +81,6 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long *bar, unsigned 
         : "memory");
     return ok != 0;
 }
-// try_wait with a suspend-time hint: a thread whose phase is not complete may
-// be suspended for up to `ns` nanoseconds (it resumes when the phase
-// completes) instead of returning at once to poll again.
-__device__ __forceinline__ bool mbar_try_wait_hint(unsigned long long *bar, unsigned parity, unsigned ns) {
-    unsigned ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
-        : "memory");
-    return ok != 0;
-}
 // Order this thread's earlier generic-proxy shared-memory accesses before
 // later async-proxy (TMA) accesses of the same memory.
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -18,13 +18,14 @@ __device__ __forceinline__ void q4k_kpos(int e, int &quarter, int &pos) {
     pos = hi * 32 + 4 * i + pw;
 }
 
-// One 1024-thread CTA per token: optional RMSNorm ((x*rstd)*w,
-// src/kernel/mod.rs:199-209), a power-of-two scale per token keeping
-// |x| < 2^10 (so the 32-element sub-block sums stay below 2^15, well inside
-// f16 range), the f16 hi/lo split, and the sub-block sums.  The row is read
-// once for its statistics; four groups of 256 threads then take one
-// super-block each at a time.  Image rows per quarter: tokens' hi halves
-// (rows 0..NT-1), then lo halves (NT..2NT-1).
+// 1024-thread CTAs, gridDim.y of them per token: optional RMSNorm
+// ((x*rstd)*w, src/kernel/mod.rs:199-209), a power-of-two scale per token
+// keeping |x| < 2^10 (so the 32-element sub-block sums stay below 2^15, well
+// inside f16 range), the f16 hi/lo split, and the sub-block sums.  Every CTA
+// of a token reads the whole row for its statistics (from L2; all of them
+// get the same values) and then prepares its share of the super-blocks, four
+// groups of 256 threads taking one super-block each at a time.  Image rows
+// per quarter: tokens' hi halves (rows 0..NT-1), then lo halves (NT..2NT-1).
 constexpr int kPrepThreads = 1024;
 template <int FMT, int NT>
 __global__ void __launch_bounds__(kPrepThreads) k_gemm_prep(const float *__restrict__ x, int x_stride,
@@ -73,14 +74,15 @@ __global__ void __launch_bounds__(kPrepThreads) k_gemm_prep(const float *__restr
             const float inv = top > 0.0f && isfinite(top) ? ldexpf(1.0f, 10 - e2) : 1.0f;
             rstd_s = rstd;
             inv_s = inv;
-            tok_scale[tok] = 1.0f / inv;
+            if (blockIdx.y == 0) tok_scale[tok] = 1.0f / inv;
         }
         __syncthreads();
     }
     const float rstd = valid ? rstd_s : 1.0f, inv = valid ? inv_s : 1.0f;
     // thread tid of a 256-thread group handles element tid of its super-block
     const int tid = threadIdx.x & 255, warp = tid >> 5;
-    for (int s = threadIdx.x >> 8; s < n_sb; s += kPrepThreads / 256) {
+    for (int s = blockIdx.y * (kPrepThreads / 256) + (threadIdx.x >> 8); s < n_sb;
+         s += gridDim.y * (kPrepThreads / 256)) {
         float v = 0.0f;
         if (valid) {
             v = xr[s * 256 + tid];
@@ -204,7 +206,8 @@ static cudaError_t launch_nt_epi(const GemvParams &p, const GemmScratch &sc, cud
     const size_t need = (size_t)g.n_tt * g.n_sb * bimg_sb_bytes(NT);
     if (!sc.bimg || need > sc.bimg_bytes || !sc.tok_scale || (size_t)g.mpad > sc.tok_scale_floats)
         return cudaErrorInvalidValue;
-    dim3 pg(g.mpad);
+    // CTAs per token: one super-block per 256-thread group where the row allows
+    dim3 pg(g.mpad, std::max(1, std::min(8, g.n_sb / (kPrepThreads / 256))));
     // programmatic dependent launch: the prep waits for the previous kernel;
     // the GEMM allocates TMEM and streams weights during the prep and waits
     // for it before reading the image or writing results

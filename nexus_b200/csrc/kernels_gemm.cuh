@@ -235,12 +235,9 @@ __device__ __forceinline__ void umma_f16_ts_w(uint32_t dt, uint32_t at, uint64_t
 }
 
 // Bounded mbarrier wait; false once this CTA has given up (abort set).
-#ifndef NX_GEMM_WAIT_HINT_NS
-#define NX_GEMM_WAIT_HINT_NS 0
-#endif
 __device__ __forceinline__ bool bwait(unsigned long long *bar, unsigned parity, volatile int *abort_flag, int *err) {
     unsigned n = 0;
-    while (!(NX_GEMM_WAIT_HINT_NS ? mbar_try_wait_hint(bar, parity, NX_GEMM_WAIT_HINT_NS) : mbar_try_wait(bar, parity))) {
+    while (!mbar_try_wait(bar, parity)) {
         if ((++n & 255u) == 0) {
             if (*abort_flag) return false;
             if (n > kSpin) {
