@@ -86,7 +86,9 @@ def model_path(name_or_cfg, seed: int = 0, threads: int = 0, writer=None) -> Pat
     path = model_dir() / f"{tag}-{config_key(cfg)}.gguf"
     done = path.with_suffix(".ok")
     if not (path.exists() and done.exists()):
-        tmp = path.with_suffix(".tmp")
+        # a private temporary name: several processes (one per GPU) may write
+        # the same model at once; the last rename wins with identical bytes
+        tmp = path.with_suffix(f".{os.getpid()}.tmp")
         writer(str(tmp), threads=threads, **cfg)
         os.replace(tmp, path)
         done.write_text("ok")

@@ -38,6 +38,7 @@ struct nexus_cuda_backend {
     int device = 0;
     cudaStream_t stream = nullptr;
     std::string last_error;
+    std::string step_error;  // why a collective of the step being enqueued failed
     std::mutex mu;
     // Models and resident weights keep their backend alive: destroying a
     // backend that still has children only marks it, and the last child
@@ -72,7 +73,6 @@ struct NcclApi {
     // for a bounded wait on the ranks joining (optional: without them the
     // join waits as long as ncclCommInitRank does)
     ncclResult_t (*comm_init_rank_config)(ncclComm_t *, int, ncclUniqueId, int, ncclConfig_t *) = nullptr;
-    ncclResult_t (*comm_split)(ncclComm_t, int, int, ncclComm_t *, ncclConfig_t *) = nullptr;
     ncclResult_t (*get_async_error)(ncclComm_t, ncclResult_t *) = nullptr;
     ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
     bool ok = false;
@@ -96,7 +96,6 @@ static NcclApi *nccl_api(std::string *why) {
         api.comm_destroy = (decltype(api.comm_destroy))dlsym(h, "ncclCommDestroy");
         api.error_string = (decltype(api.error_string))dlsym(h, "ncclGetErrorString");
         api.comm_init_rank_config = (decltype(api.comm_init_rank_config))dlsym(h, "ncclCommInitRankConfig");
-        api.comm_split = (decltype(api.comm_split))dlsym(h, "ncclCommSplit");
         api.get_async_error = (decltype(api.get_async_error))dlsym(h, "ncclCommGetAsyncError");
         api.comm_abort = (decltype(api.comm_abort))dlsym(h, "ncclCommAbort");
         api.ok = api.get_unique_id && api.comm_init_rank && api.all_reduce && api.all_gather && api.comm_destroy &&
@@ -554,10 +553,9 @@ extern "C" int nexus_cuda_tp_init(nexus_cuda_backend *b, int rank, int world, co
     ncclUniqueId u;
     memcpy(&u, id, sizeof(u));
     const uint32_t limit_ms = b->cfg.tp_timeout_ms ? b->cfg.tp_timeout_ms : 120000u;
-    if (api->comm_init_rank_config && api->comm_split && api->get_async_error && api->comm_abort) {
-        // Join on a nonblocking communicator, polled against the limit, then
-        // split off a blocking one over the same ranks for the decode steps
-        // (whose collectives are captured in CUDA graphs).
+    if (api->comm_init_rank_config && api->get_async_error && api->comm_abort) {
+        // Join on a nonblocking communicator, polled against the limit, so a
+        // rank that never arrives ends the join with NEXUS_E_COMM.
         ncclConfig_t nb = NCCL_CONFIG_INITIALIZER;
         nb.blocking = 0;
         ncclComm_t boot = nullptr;
@@ -570,16 +568,51 @@ extern "C" int nexus_cuda_tp_init(nexus_cuda_backend *b, int rank, int world, co
                                                      " ms (group torn down on this rank)");
             return set_err(b, NEXUS_E_COMM, std::string("ncclCommInitRankConfig: ") + api->error_string(r));
         }
-        ncclConfig_t bl = NCCL_CONFIG_INITIALIZER;
-        bl.blocking = 1;
-        ncclComm_t comm = nullptr;
-        r = api->comm_split(boot, 0, rank, &comm, &bl);
-        if (r == ncclInProgress) r = nccl_settle(api, &comm, r, limit_ms);
+        // Every rank has joined.  The decode steps need a blocking
+        // communicator (their collectives are captured in CUDA graphs): rank 0
+        // draws a second id, the joining communicator carries it to every rank
+        // (a byte-wise sum in which the other ranks contribute zeros), and each
+        // rank builds the step communicator from it with ncclCommInitRank.
+        ncclUniqueId u2 = {};
+        if (rank == 0 && (r = api->get_unique_id(&u2)) != ncclSuccess) {
+            api->comm_abort(boot);
+            return set_err(b, NEXUS_E_COMM, std::string("ncclGetUniqueId: ") + api->error_string(r));
+        }
+        uint8_t *dbuf = nullptr;
+        cudaError_t ce = dalloc(&dbuf, sizeof(u2));
+        if (ce == cudaSuccess) ce = cudaMemcpy(dbuf, &u2, sizeof(u2), cudaMemcpyHostToDevice);
+        if (ce == cudaSuccess) {
+            r = api->all_reduce(dbuf, dbuf, sizeof(u2), ncclUint8, ncclSum, boot, b->stream);
+            if (r == ncclInProgress) r = nccl_settle(api, &boot, r, limit_ms);
+            // the reduction itself, bounded like the join
+            const auto t0 = std::chrono::steady_clock::now();
+            while (r == ncclSuccess && (ce = cudaStreamQuery(b->stream)) == cudaErrorNotReady) {
+                const auto ms =
+                    std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0);
+                if (ms.count() > (long long)limit_ms) {
+                    r = ncclInProgress;
+                    break;
+                }
+                std::this_thread::sleep_for(std::chrono::milliseconds(1));
+            }
+            if (r == ncclSuccess && ce == cudaSuccess) ce = cudaMemcpy(&u2, dbuf, sizeof(u2), cudaMemcpyDeviceToHost);
+        }
         api->comm_abort(boot);
+        if (dbuf) cudaFree(dbuf);
+        if (r != ncclSuccess || ce != cudaSuccess) {
+            cudaGetLastError();
+            if (r == ncclInProgress)
+                return set_err(b, NEXUS_E_COMM, "tp init: the second id did not reach every rank within " +
+                                                     std::to_string(limit_ms) + " ms");
+            return set_err(b, NEXUS_E_COMM, r != ncclSuccess ? std::string("tp init id exchange: ") + api->error_string(r)
+                                                             : std::string("tp init id exchange: ") + cudaGetErrorString(ce));
+        }
+        ncclComm_t comm = nullptr;
+        r = api->comm_init_rank(&comm, world, u2, rank);
         if (r != ncclSuccess || !comm) {
             if (comm) api->comm_abort(comm);
             cudaGetLastError();
-            return set_err(b, NEXUS_E_COMM, std::string("ncclCommSplit: ") + api->error_string(r));
+            return set_err(b, NEXUS_E_COMM, std::string("ncclCommInitRank: ") + api->error_string(r));
         }
         b->comm = comm;
     } else {
@@ -1799,9 +1832,12 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
         if (m->b->peer_ok && (size_t)mc * H <= m->b->peer.max_floats) {
             PeerReduce pr = m->b->peer;
             pr.err = reinterpret_cast<int *>(m->out_tokens + kMaxChunk);
-            return launch_peer_allreduce(pr, m->hidden, (size_t)mc * H, st);
+            const cudaError_t pe = launch_peer_allreduce(pr, m->hidden, (size_t)mc * H, st);
+            if (pe != cudaSuccess) m->b->step_error = std::string("peer all-reduce launch: ") + cudaGetErrorString(pe);
+            return pe;
         }
         ncclResult_t r = nccl->all_reduce(m->hidden, m->hidden, (size_t)mc * H, ncclFloat32, ncclSum, m->b->comm, st);
+        if (r != ncclSuccess) m->b->step_error = std::string("ncclAllReduce(hidden): ") + nccl->error_string(r);
         return r == ncclSuccess ? cudaSuccess : cudaErrorUnknown;
     };
     const int pdl = m->use_pdl ? 1 : 0;
@@ -2007,7 +2043,10 @@ static cudaError_t enqueue_step(nexus_cuda_model *m, int mc, StepProfiler *prof 
             // keys reduce with max; the rest of DevSeq is equal on every rank
             static_assert(sizeof(DevSeq) == 24, "DevSeq is three 64-bit words");
             ncclResult_t r = nccl->all_reduce(m->seqs, m->seqs, (size_t)mc * 3, ncclUint64, ncclMax, m->b->comm, st);
-            if (r != ncclSuccess) return cudaErrorUnknown;
+            if (r != ncclSuccess) {
+                m->b->step_error = std::string("ncclAllReduce(argmax): ") + nccl->error_string(r);
+                return cudaErrorUnknown;
+            }
         }
         if (prof) prof->end("head", gemv_bytes(m->head, mc, H, (int)I.vocab_rows) + 4.0 * H);
     } else {
@@ -2066,12 +2105,14 @@ static int run_step(nexus_cuda_model *m, int mc, bool chunk = false) {
         if (!graphs[mc]) {
             cudaGraph_t g = nullptr;
             NX_CUDA(b, cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+            b->step_error.clear();
             cudaError_t e = enqueue_step(m, mc, nullptr, chunk);
             cudaError_t e2 = cudaStreamEndCapture(st, &g);
             if (e != cudaSuccess || e2 != cudaSuccess) {
                 if (g) cudaGraphDestroy(g);
                 return set_err(b, NEXUS_E_CUDA, std::string("graph capture: ") +
-                                                   cudaGetErrorString(e != cudaSuccess ? e : e2));
+                                                   cudaGetErrorString(e != cudaSuccess ? e : e2) +
+                                                   (b->step_error.empty() ? "" : " (" + b->step_error + ")"));
             }
             e = cudaGraphInstantiate(&graphs[mc], g, 0);
             cudaGraphDestroy(g);
