@@ -357,6 +357,10 @@ typedef struct {
     uint32_t n_pages;
     const uint32_t *kv_pages;
 } nexus_scheduled_decode;
+/* Message of the calling thread's last scheduler call that failed (every
+ * failure of a nexus_scheduler_* call, and the scheduler-side checks of
+ * nexus_cuda_serve_step, return NEXUS_E_INVALID with a message here). */
+const char *nexus_scheduler_last_error(void);
 /* Scheduler::with_kv_pages (:152-166) */
 int nexus_scheduler_create(uint32_t max_batch_size, uint32_t page_size_tokens, uint32_t max_kv_pages,
                            nexus_scheduler **out);

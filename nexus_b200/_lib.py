@@ -148,6 +148,7 @@ SIGNATURES = [
     ("nexus_cuda_decode_batch", C.c_int, [P, C.POINTER(DecodeItem), C.c_size_t, P, P]),
     ("nexus_cuda_generate_with_draft", C.c_int, [P, C.c_uint32, P, C.c_size_t, P, C.c_size_t, C.c_size_t,
                                                  C.c_uint32, P, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]),
+    ("nexus_scheduler_last_error", C.c_char_p, []),
     ("nexus_scheduler_create", C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, C.POINTER(P)]),
     ("nexus_scheduler_destroy", C.c_int, [P]),
     ("nexus_scheduler_add_request", C.c_int, [P, C.c_uint64, P, C.c_size_t, C.c_uint32]),
@@ -204,4 +205,11 @@ def check(rc: int, backend=None) -> None:
     if rc != NEXUS_OK:
         lib = load()
         msg = lib.nexus_cuda_last_error(backend)
+        raise NexusError(rc, msg.decode() if msg else "")
+
+
+def check_scheduler(rc: int) -> None:
+    """Status of a nexus_scheduler_* call, with the scheduler's message."""
+    if rc != NEXUS_OK:
+        msg = load().nexus_scheduler_last_error()
         raise NexusError(rc, msg.decode() if msg else "")

@@ -93,7 +93,13 @@ struct nexus_scheduler {
 
 namespace {
 
-int fail(const char *) { return NEXUS_E_INVALID; }
+// the calling thread's last scheduler error (nexus_scheduler_last_error)
+thread_local std::string g_sched_error;
+
+int fail(const char *msg) {
+    g_sched_error = msg;
+    return NEXUS_E_INVALID;
+}
 
 bool known_id(nexus_scheduler *s, uint64_t id) {
     for (auto &r : s->pending)
@@ -167,12 +173,14 @@ size_t fill_running(nexus_scheduler *s) {
 
 int copy_ids(const std::vector<uint64_t> &v, uint64_t *ids, size_t max, size_t *n) {
     if (n) *n = v.size();
-    if (v.size() > max || (v.size() && !ids)) return NEXUS_E_INVALID;
+    if (v.size() > max || (v.size() && !ids)) return fail("id buffer too small");
     for (size_t i = 0; i < v.size(); i++) ids[i] = v[i];
     return NEXUS_OK;
 }
 
 }  // namespace
+
+extern "C" const char *nexus_scheduler_last_error(void) { return g_sched_error.c_str(); }
 
 extern "C" int nexus_scheduler_create(uint32_t max_batch_size, uint32_t page_size_tokens, uint32_t max_kv_pages,
                                       nexus_scheduler **out) {
@@ -369,7 +377,7 @@ extern "C" int nexus_scheduler_kv_allocation(nexus_scheduler *s, uint64_t id, ui
     if (!s || !n) return fail("NULL argument");
     std::lock_guard<std::mutex> lk(s->mu);
     *n = 0;
-    if (!s->allocations.count(id)) return NEXUS_E_INVALID;  // no allocation (kv_allocation -> None)
+    if (!s->allocations.count(id)) return fail("the request holds no KV pages");  // kv_allocation -> None
     for (auto &r : s->running) {
         if (r.id != id) continue;
         *n = r.kv_pages.size();
@@ -397,7 +405,7 @@ extern "C" int nexus_scheduler_tokens(nexus_scheduler *s, uint64_t id, uint32_t 
     for (auto &r : s->pending)
         if (r.id == id) return emit(r);
     *n = 0;
-    return NEXUS_E_INVALID;
+    return fail("unknown request id (completed requests are forgotten once taken)");
 }
 
 // ---------------------------------------------------------------------------
@@ -405,7 +413,8 @@ extern "C" int nexus_scheduler_tokens(nexus_scheduler *s, uint64_t id, uint32_t 
 
 extern "C" int nexus_cuda_serve_step(nexus_cuda_model *m, nexus_scheduler *s, nexus_serve_event *events,
                                      size_t max_events, size_t *n_events) {
-    if (!m || !s || !n_events) return NEXUS_E_INVALID;
+    g_sched_error.clear();  // a failure below names itself here or in the backend's last error
+    if (!m || !s || !n_events) return fail("NULL argument");
     *n_events = 0;
     nexus_cuda_model_info info = {};
     int rc = nexus_cuda_model_get_info(m, &info);

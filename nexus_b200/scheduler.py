@@ -61,7 +61,7 @@ class Scheduler:
     def __init__(self, max_batch_size: int = 8, page_size_tokens: int = 16, max_kv_pages: Optional[int] = None):
         self._lib = L.load()
         h = C.c_void_p()
-        L.check(self._lib.nexus_scheduler_create(max_batch_size, page_size_tokens, max_kv_pages or 0, C.byref(h)))
+        L.check_scheduler(self._lib.nexus_scheduler_create(max_batch_size, page_size_tokens, max_kv_pages or 0, C.byref(h)))
         self.handle = h
         self.max_batch_size = max_batch_size
         self.page_size_tokens = max(1, page_size_tokens)
@@ -91,7 +91,7 @@ class Scheduler:
 
     def add_request(self, id: str, tokens: Sequence[int], max_tokens: int) -> None:
         toks = np.ascontiguousarray(np.asarray(tokens, np.uint32))
-        L.check(self._lib.nexus_scheduler_add_request(self.handle, self._id(id), toks.ctypes.data, toks.size,
+        L.check_scheduler(self._lib.nexus_scheduler_add_request(self.handle, self._id(id), toks.ctypes.data, toks.size,
                                                       max_tokens))
 
     def get_next_batch(self) -> list[str]:
@@ -101,7 +101,7 @@ class Scheduler:
         cap = self._room()
         items = (L.ScheduledDecode * cap)()
         n = C.c_size_t()
-        L.check(self._lib.nexus_scheduler_decode_batch(self.handle, items, cap, C.byref(n)))
+        L.check_scheduler(self._lib.nexus_scheduler_decode_batch(self.handle, items, cap, C.byref(n)))
         return [ScheduledDecode(self._name[d.id], d.token, d.position, d.generated, d.prompt_len,
                                 [d.kv_pages[j] for j in range(d.n_pages)]) for d in items[:n.value]]
 
@@ -109,7 +109,7 @@ class Scheduler:
         if id not in self._num:
             return False
         found = C.c_int()
-        L.check(self._lib.nexus_scheduler_append_generated(self.handle, self._num[id], token, C.byref(found)))
+        L.check_scheduler(self._lib.nexus_scheduler_append_generated(self.handle, self._num[id], token, C.byref(found)))
         return bool(found.value)
 
     def step(self) -> list[str]:
@@ -122,17 +122,17 @@ class Scheduler:
         if id not in self._num:
             return False
         found = C.c_int()
-        L.check(self._lib.nexus_scheduler_complete_request(self.handle, self._num[id], C.byref(found)))
+        L.check_scheduler(self._lib.nexus_scheduler_complete_request(self.handle, self._num[id], C.byref(found)))
         return bool(found.value)
 
     def stats(self) -> tuple[int, int, int]:
         p, r, c = C.c_size_t(), C.c_size_t(), C.c_size_t()
-        L.check(self._lib.nexus_scheduler_stats(self.handle, C.byref(p), C.byref(r), C.byref(c)))
+        L.check_scheduler(self._lib.nexus_scheduler_stats(self.handle, C.byref(p), C.byref(r), C.byref(c)))
         return p.value, r.value, c.value
 
     def kv_page_stats(self) -> tuple[int, int]:
         used, mx = C.c_size_t(), C.c_size_t()
-        L.check(self._lib.nexus_scheduler_kv_page_stats(self.handle, C.byref(used), C.byref(mx)))
+        L.check_scheduler(self._lib.nexus_scheduler_kv_page_stats(self.handle, C.byref(used), C.byref(mx)))
         return used.value, mx.value
 
     def kv_allocation(self, id: str) -> Optional[KvPageAllocation]:
@@ -143,7 +143,7 @@ class Scheduler:
         if rc != 0 and n.value == 0:
             return None
         buf = (C.c_uint32 * max(1, n.value))()
-        L.check(self._lib.nexus_scheduler_kv_allocation(self.handle, self._num[id], buf, n.value, C.byref(n),
+        L.check_scheduler(self._lib.nexus_scheduler_kv_allocation(self.handle, self._num[id], buf, n.value, C.byref(n),
                                                         C.byref(cap)))
         return KvPageAllocation(id, list(buf[:n.value]), self.page_size_tokens, cap.value)
 
@@ -152,7 +152,7 @@ class Scheduler:
         n = C.c_size_t()
         self._lib.nexus_scheduler_tokens(self.handle, self._num[id], None, 0, C.byref(n))
         buf = (C.c_uint32 * max(1, n.value))()
-        L.check(self._lib.nexus_scheduler_tokens(self.handle, self._num[id], buf, n.value, C.byref(n)))
+        L.check_scheduler(self._lib.nexus_scheduler_tokens(self.handle, self._num[id], buf, n.value, C.byref(n)))
         return list(buf[:n.value])
 
     def close(self) -> None:
@@ -185,8 +185,11 @@ class ContinuousBatcher:
     def tick(self) -> list[ServeEvent]:
         ev = (L.ServeEvent * self._cap)()
         n = C.c_size_t()
-        L.check(self.engine._lib.nexus_cuda_serve_step(self.engine.model, self.scheduler.handle, ev, self._cap,
-                                                       C.byref(n)), self.engine.backend.handle)
+        rc = self.engine._lib.nexus_cuda_serve_step(self.engine.model, self.scheduler.handle, ev, self._cap,
+                                                    C.byref(n))
+        if rc != L.NEXUS_OK and rc == L.NEXUS_E_INVALID and L.load().nexus_scheduler_last_error():
+            L.check_scheduler(rc)
+        L.check(rc, self.engine.backend.handle)
         name = self.scheduler._name
         return [ServeEvent(name[e.request_id], e.token, e.index, bool(e.done), e.status) for e in ev[:n.value]]
 

@@ -145,16 +145,17 @@ def test_cancel_pending_and_unknown():
 
 def test_refusals():
     s = Scheduler(2)
-    with pytest.raises(NexusError):
+    with pytest.raises(NexusError, match="at least one token"):
         s.add_request("e", [], 3)            # never gives a decode item
     s.add_request("x", [1], 1)
-    with pytest.raises(NexusError):
+    with pytest.raises(NexusError, match="already in use"):
         s.add_request("x", [2], 1)           # id in use
     lib = L.load()
     n = C.c_size_t()
     s.add_request("y", [2], 1)
     rc = lib.nexus_scheduler_decode_batch(s.handle, None, 1, C.byref(n))
     assert rc != 0 and n.value == 2         # too small: nothing admitted
+    assert b"too small" in lib.nexus_scheduler_last_error()
     assert s.stats() == (2, 0, 0)
 
 
