@@ -28,7 +28,8 @@ arm writes its model with the oracle's synthetic writer and never loads the
 CUDA library.
 
 Multi-GPU: tensor parallelism over the torchrun ranks (heads, FFN rows and
-vocabulary rows per rank; one NCCL all-reduce per sublayer).  One decode
+vocabulary rows per rank; one all-reduce per sublayer, by the one-shot
+peer-memory kernel over NVLink, NCCL as fallback).  One decode
 stream is served by all ranks, so the scaling is strong: `value` is the
 stream's tokens per second, timed on the device as the max over ranks.
 """
