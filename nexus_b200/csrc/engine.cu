@@ -24,6 +24,7 @@
 #include "kernels.h"
 #include "quant_math.cuh"
 #include "tiles.cuh"
+#include "trace.h"
 
 namespace nx {
 int synth_model_write(const char *path, const nexus_synth_config *cfg, std::string &err);
@@ -2090,6 +2091,7 @@ static cudaError_t enqueue_persistent_step(nexus_cuda_model *m, StepProfiler *pr
 }
 
 static int run_step(nexus_cuda_model *m, int mc, bool chunk = false) {
+    nx::TraceRange tr(chunk ? "step chunk" : "step", mc);
     nexus_cuda_backend *b = m->b;
     cudaStream_t st = b->stream;
     if (b->tp_failed)
@@ -2201,6 +2203,7 @@ static int host_step(nexus_cuda_model *m, const StepItem *items, int mc, float *
 }
 
 extern "C" int nexus_cuda_model_load(nexus_cuda_backend *b, const char *gguf_path, nexus_cuda_model **out) {
+    nx::TraceRange tr("nexus_cuda_model_load");
     if (!b || !gguf_path || !out) return set_err(b, NEXUS_E_INVALID, "NULL argument");
     *out = nullptr;
     std::lock_guard<std::mutex> lk(b->mu);
@@ -2262,6 +2265,7 @@ static int check_position(nexus_cuda_model *m, uint64_t position) {
 
 extern "C" int nexus_cuda_decode(nexus_cuda_model *m, uint32_t seq_id, uint32_t token, uint32_t position,
                                  float *logits, uint32_t *argmax) {
+    nx::TraceRange tr("nexus_cuda_decode");
     if (!m) return set_err(nullptr, NEXUS_E_INVALID, "model is NULL");
     std::lock_guard<std::mutex> lk(m->b->mu);
     cudaSetDevice(m->b->device);
@@ -2312,6 +2316,7 @@ static int prefill_impl(nexus_cuda_model *m, uint32_t seq_id, const uint32_t *to
 
 extern "C" int nexus_cuda_prefill(nexus_cuda_model *m, uint32_t seq_id, const uint32_t *tokens, size_t n,
                                   float *logits, uint32_t *argmax) {
+    nx::TraceRange tr("nexus_cuda_prefill", (long long)n);
     if (!m || (n && !tokens)) return set_err(m ? m->b : nullptr, NEXUS_E_INVALID, "NULL argument");
     if (seq_id >= m->max_batch) return set_err(m->b, NEXUS_E_INVALID, "bad sequence id");
     std::lock_guard<std::mutex> lk(m->b->mu);
@@ -2321,6 +2326,7 @@ extern "C" int nexus_cuda_prefill(nexus_cuda_model *m, uint32_t seq_id, const ui
 
 extern "C" int nexus_cuda_generate(nexus_cuda_model *m, uint32_t seq_id, const uint32_t *prompt, size_t n,
                                    size_t max_tokens, uint32_t *out) {
+    nx::TraceRange tr("nexus_cuda_generate", (long long)max_tokens);
     if (!m || !out || (n && !prompt)) return set_err(m ? m->b : nullptr, NEXUS_E_INVALID, "NULL argument");
     if (seq_id >= m->max_batch) return set_err(m->b, NEXUS_E_INVALID, "bad sequence id");
     std::lock_guard<std::mutex> lk(m->b->mu);
@@ -2388,6 +2394,7 @@ extern "C" int nexus_cuda_generate(nexus_cuda_model *m, uint32_t seq_id, const u
 extern "C" int nexus_cuda_generate_with_draft(nexus_cuda_model *m, uint32_t seq_id, const uint32_t *prompt,
                                               size_t n, const uint32_t *draft, size_t n_draft, size_t max_tokens,
                                               uint32_t window, uint32_t *out, uint32_t *accepted, uint32_t *rejected) {
+    nx::TraceRange tr("nexus_cuda_generate_with_draft", (long long)max_tokens);
     if (!m || !out || (n && !prompt) || (n_draft && !draft))
         return set_err(m ? m->b : nullptr, NEXUS_E_INVALID, "NULL argument");
     if (seq_id >= m->max_batch) return set_err(m->b, NEXUS_E_INVALID, "bad sequence id");
@@ -2448,6 +2455,7 @@ extern "C" int nexus_cuda_generate_with_draft(nexus_cuda_model *m, uint32_t seq_
 
 extern "C" int nexus_cuda_decode_batch(nexus_cuda_model *m, const nexus_decode_item *items, size_t n,
                                        uint32_t *out_tokens, float *out_logits) {
+    nx::TraceRange tr("nexus_cuda_decode_batch", (long long)n);
     if (!m || (n && !items)) return set_err(m ? m->b : nullptr, NEXUS_E_INVALID, "NULL argument");
     std::lock_guard<std::mutex> lk(m->b->mu);
     cudaSetDevice(m->b->device);

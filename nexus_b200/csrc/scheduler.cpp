@@ -38,6 +38,7 @@
 #include <vector>
 
 #include "../../include/nexus_cuda.h"
+#include "trace.h"
 
 namespace {
 
@@ -413,6 +414,7 @@ extern "C" int nexus_scheduler_tokens(nexus_scheduler *s, uint64_t id, uint32_t 
 
 extern "C" int nexus_cuda_serve_step(nexus_cuda_model *m, nexus_scheduler *s, nexus_serve_event *events,
                                      size_t max_events, size_t *n_events) {
+    nx::TraceRange tr("nexus_cuda_serve_step");
     g_sched_error.clear();  // a failure below names itself here or in the backend's last error
     if (!m || !s || !n_events) return fail("NULL argument");
     *n_events = 0;
