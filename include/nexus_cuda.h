@@ -404,7 +404,8 @@ int nexus_scheduler_tokens(nexus_scheduler *s, uint64_t id, uint32_t *out, size_
  * id, the token, its index among the request's generated tokens, done = 1
  * when the request completed, status NEXUS_E_INVALID for a request the model
  * cannot hold (prompt_len + max_tokens - 1 > max_seq_len), which ends without
- * tokens.  The scheduler's page size must equal the model's page_tokens,
+ * tokens, or the status of a failed page binding or prefill for a request
+ * that could not be set up (it ends too; the backend's last error says why).  The scheduler's page size must equal the model's page_tokens,
  * max_kv_pages must be set and within the model's pool, max_batch_size within
  * its max_batch and max_events >= max_batch_size.  From its first tick the
  * scheduler owns every sequence of the model (their pages are released

@@ -474,23 +474,39 @@ extern "C" int nexus_cuda_serve_step(nexus_cuda_model *m, nexus_scheduler *s, ne
         s->running.push_back(std::move(r));
     }
     const uint32_t per_seq = (info.max_seq_len + info.page_tokens - 1) / info.page_tokens;
+    // New requests: one with nothing to generate finishes here (Request::advance
+    // on generated >= max_tokens, src/scheduler.rs:50-70) without a sequence;
+    // the others get a device sequence with their pages bound and their prompt
+    // prefilled up to its last token.  A request whose set-up fails ends with
+    // an error event (the failing call's status; its message stays in the
+    // backend's last error) and gives its sequence and pages back.
+    std::vector<uint64_t> zero;
+    std::vector<std::pair<uint64_t, int>> broken;
     for (size_t i = before; i < s->running.size(); i++) {
         Request &r = s->running[i];
+        if (r.max_tokens == 0) {
+            zero.push_back(r.id);
+            continue;
+        }
         r.seq = s->free_seqs.back();
         s->free_seqs.pop_back();
         const uint32_t np = (uint32_t)std::min<size_t>(r.kv_pages.size(), per_seq);
         rc = nexus_cuda_seq_set_pages(m, (uint32_t)r.seq, r.kv_pages.data(), np);
         if (!rc) rc = nexus_cuda_prefill(m, (uint32_t)r.seq, r.tokens.data(), r.prompt_len - 1, nullptr, nullptr);
-        if (rc) return rc;
+        if (rc) broken.push_back({r.id, rc});
     }
-    // requests that may generate nothing finish without a step
-    // (Request::advance on generated >= max_tokens)
-    std::vector<uint64_t> zero;
-    for (auto &r : s->running)
-        if (r.max_tokens == 0) zero.push_back(r.id);
     for (uint64_t id : zero) {
         append_locked(s, id, 0, nullptr);
         events[(*n_events)++] = {id, 0, 0, 1, 0};
+    }
+    for (const auto &b : broken) {
+        auto it = std::find_if(s->running.begin(), s->running.end(), [&](const Request &r) { return r.id == b.first; });
+        Request r = std::move(*it);
+        s->running.erase(it);
+        r.state = State::Done;
+        finish(s, r);
+        s->completed.push_back(std::move(r));
+        events[(*n_events)++] = {b.first, 0, 0, 1, b.second};
     }
     for (int q : s->seqs_to_release) {
         rc = nexus_cuda_seq_set_pages(m, (uint32_t)q, nullptr, 0);
