@@ -129,3 +129,27 @@ def test_bench_reference_arm_prints_one_contract_line():
     assert d["metric"] == bench.METRIC
     src = (root / "bench.py").read_text()
     assert src.count('"metric": METRIC') == 2 and 'line["metric"]' not in src
+
+
+def _write_tiny(model_dir):
+    import os
+    os.environ["NEXUS_MODEL_DIR"] = model_dir
+    from nexus_b200.configs import model_path
+    from oracle import oracle as O
+    return str(model_path("tiny", writer=O.write_synthetic_model))
+
+
+def test_model_path_concurrent_writers(tmp_path):
+    """Ranks of a multi-GPU run may write the same synthetic model at once:
+    each writes under its own temporary name and the renames leave one
+    complete file (the run that found this raced on a shared name)."""
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(3) as pool:
+        paths = pool.map(_write_tiny, [str(tmp_path)] * 3)
+    assert len(set(paths)) == 1
+    files = sorted(p.name for p in tmp_path.iterdir())
+    assert not [f for f in files if f.endswith(".tmp")], files
+    from oracle import oracle as O
+    m = O.Model(paths[0])
+    assert m.info.num_layers == 4 and m.info.vocab_rows == 4096
