@@ -82,7 +82,7 @@ class Scheduler:
     def _ids(self, fn, cap: int) -> list[str]:
         buf = (C.c_uint64 * max(1, cap))()
         n = C.c_size_t()
-        L.check(fn(self.handle, buf, cap, C.byref(n)))
+        L.check_scheduler(fn(self.handle, buf, cap, C.byref(n)))
         return [self._name[buf[i]] for i in range(n.value)]
 
     def _room(self) -> int:
